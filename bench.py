@@ -1,0 +1,527 @@
+"""Benchmark of the B200 attention block (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-extra]
+
+Workload (every N): qwen3_8b_decode_32k - Qwen3-8B-shaped single-stream decode at context 32768,
+36 layers, 32 q / 8 KV heads, head_dim 128, fp32 KV cache, QK norm and RoPE.  A step is one token:
+36 per-layer launches of the decode kernel (the real forward's order: layer l+1 starts after layer
+l), each streaming that layer's K and V rows [0, 32768] (268 MB) from HBM.  With N > 1 the KV heads
+are split over the ranks as SARA does (cpp/ligguf_distrib.cpp:665-679) and every layer's head
+outputs are all-gathered over NVLink (NCCL) - strong scaling of one stream.  Inputs are larger than
+L2 (9.66 GB of KV per step), so no L2 flush is needed between steps.
+
+At N == 1 the line also carries the other configurations as `extra`: the 4K-context decode, the
+causal 2048-token prefill (fp32 SIMT and bf16 tensor cores) and the BERT attention.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOAD = "qwen3_8b_decode_32k"
+METRIC = "decode attn tokens/s (ctx 32K, 36 layers, fp32 KV)"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-extra", action="store_true", help="skip the other configurations at N=1")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    return ap.parse_args()
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"],
+                "bf16_tflops_sustained": p.get("bf16_tflops_sustained", p["bf16_tflops"]), "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def load_profile_traffic(kernel: str):
+    """dram read+write bytes per launch of `kernel` from the committed ncu summary, or None."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get(kernel)
+    except Exception:
+        return None
+
+
+# ------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"ligguf_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.out = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.out, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.out.close()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        try:
+            os.unlink(self.path)
+        except OSError:
+            pass
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# ------------------------------------------------------------------------------ CPU side
+def cpu_baseline(w, target_s: float = 10.0, max_layers: int = 2):
+    """The reference's CPU attention (oracle/_ref: its fast/lil_math.cpp built from source, AVX2 dots,
+    `omp parallel for` over heads) on a bounded sample of the workload: one decode step of up to
+    `max_layers` layers with a full-length fp32 cache, repeated for about `target_s` seconds; tokens/s
+    extrapolated to all layers.  Falls back to the C restatement when the reference build is absent."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from oracle import oracle as orc
+    try:
+        chk, kind = orc.Checker("ref"), "reference"
+    except FileNotFoundError:
+        chk, kind = orc.Checker("port"), "port"
+    nl = max(1, min(max_layers, w.n_layers))
+    kv_dim = w.n_kv_heads * w.head_dim
+    cfg = orc.Checker.cfg(w.n_heads, w.n_kv_heads, w.head_dim, w.n_context, w.rope_dim, w.eps, int(w.qk_norm),
+                          0, 0)
+    freq = orc.rope_table(w.rope_dim, w.rope_base)
+    layers = []
+    for l in range(nl):
+        kc = np.empty((w.n_context, kv_dim), dtype=np.float32)
+        vc = np.empty_like(kc)
+        orc.kv_synth(kc, 0, kv_dim, kv_dim, 0, l, 1, 0, w.pos, w.seed, w.scale)
+        orc.kv_synth(vc, 0, kv_dim, kv_dim, 0, l, 2, 0, w.pos, w.seed, w.scale)
+        sid = lambda t: (t << 32) | l  # noqa: E731
+        q = orc.synth_f32(w.n_heads * w.head_dim, w.seed, sid(3), 0, w.scale)
+        k = orc.synth_f32(kv_dim, w.seed, sid(4), 0, w.scale)
+        v = orc.synth_f32(kv_dim, w.seed, sid(5), 0, w.scale)
+        qg = orc.synth_f32(w.head_dim, w.seed, sid(6), 0, 0.02, 1.0)
+        kg = orc.synth_f32(w.head_dim, w.seed, sid(7), 0, 0.02, 1.0)
+        layers.append((kc, vc, q, k, v, qg, kg))
+    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    times = []
+    t_end = time.perf_counter() + target_s
+    chk.decode_layer(cfg, *layers[0][:2], freq, layers[0][5], layers[0][6], w.pos, *layers[0][2:5])  # warm
+    while time.perf_counter() < t_end or not times:
+        t0 = time.perf_counter()
+        for (kc, vc, q, k, v, qg, kg) in layers:
+            chk.decode_layer(cfg, kc, vc, freq, qg, kg, w.pos, q, k, v)
+        times.append((time.perf_counter() - t0) / nl)
+    per_layer = statistics.median(times)
+    tok_s = 1.0 / (per_layer * w.n_layers)
+    return {"value": tok_s, "unit": "tokens/s", "cores": min(threads, w.n_heads), "kind": kind,
+            "sample": f"{nl} of {w.n_layers} layers, full {w.pos + 1}-position fp32 cache, {len(times)} repeats "
+                      f"(median {per_layer * 1e3:.1f} ms/layer), tokens/s extrapolated to {w.n_layers} layers; "
+                      f"OpenMP over the {w.n_heads} heads as the reference's MULTITHREAD",
+            "threads_available": threads,
+            "gbs": w.kv_bytes_per_token() * tok_s / 1e9}
+
+
+def run_reference_arm(args):
+    from ligguf_b200.workloads import DECODE_WORKLOADS
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    w = DECODE_WORKLOADS[WORKLOAD]
+    per_step = max(1.0, 30.0 / max(1, args.steps + args.warmup))
+    cb = cpu_baseline(w, target_s=per_step * (args.steps + args.warmup))
+    line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tokens/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 / cb["value"], "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+            "config": {"workload": WORKLOAD, "layers": w.n_layers, "ctx": w.pos + 1, "kv": "fp32",
+                       "heads": [w.n_heads, w.n_kv_heads, w.head_dim], "parallelism": "cpu"},
+            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "gpu_launches": 0}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------------------ GPU side
+def setup_dist(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    import torch
+    torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        pg = dist
+    return rank, world, local, pg
+
+
+def decode_setup(w, rank, world, local):
+    import torch
+    from ligguf_b200 import AttnConfig, CudaAttention, shard_of, synth_fill
+    from ligguf_b200.workloads import (GAMMA_ADD, GAMMA_SCALE, SYNTH_KGAMMA, SYNTH_KNEW, SYNTH_Q, SYNTH_QGAMMA,
+                                       SYNTH_VNEW, stream_id)
+    s = shard_of(w.n_kv_heads, w.n_heads, rank, world)
+    cfg = AttnConfig(n_layers=w.n_layers, n_heads=w.n_heads, n_kv_heads=w.n_kv_heads, head_dim=w.head_dim,
+                     n_context=w.n_context, rope_dim=w.rope_dim, rope_base=w.rope_base, rms_epsilon=w.eps,
+                     qk_norm=w.qk_norm, kv_type=w.kv_type, device=local,
+                     kv_head0=s["kv_head0"], kv_headn=s["kv_headn"] if world > 1 else 0)
+    h = CudaAttention(cfg)
+    dev = torch.device("cuda", local)
+    D = w.head_dim
+    qd, kd = s["q_headn"] * D, s["kv_headn"] * D
+    q = torch.empty(w.n_layers, qd, device=dev)
+    k = torch.empty(w.n_layers, kd, device=dev)
+    v = torch.empty(w.n_layers, kd, device=dev)
+    gam = torch.empty(2, D, device=dev)
+    for l in range(w.n_layers):
+        synth_fill(q[l], qd, w.seed, stream_id(SYNTH_Q, l), s["q_head0"] * D, w.scale)
+        synth_fill(k[l], kd, w.seed, stream_id(SYNTH_KNEW, l), s["kv_head0"] * D, w.scale)
+        synth_fill(v[l], kd, w.seed, stream_id(SYNTH_VNEW, l), s["kv_head0"] * D, w.scale)
+        if w.qk_norm:
+            synth_fill(gam[0], D, w.seed, stream_id(SYNTH_QGAMMA, l), 0, GAMMA_SCALE, GAMMA_ADD)
+            synth_fill(gam[1], D, w.seed, stream_id(SYNTH_KGAMMA, l), 0, GAMMA_SCALE, GAMMA_ADD)
+            g = gam.cpu().numpy()
+            h.set_qk_norm(l, g[0], g[1])
+    h.kv_synth(0, w.n_layers, 0, w.pos, w.seed, w.scale)
+    torch.cuda.synchronize()
+    return h, s, q, k, v
+
+
+def bench_decode(args, w, rank, world, local, pg, peaks):
+    import torch
+    h, s, q, k, v = decode_setup(w, rank, world, local)
+    dev = torch.device("cuda", local)
+    D = w.head_dim
+    out = torch.empty(w.n_layers, s["q_headn"] * D, device=dev)
+    full = torch.empty(w.n_layers, w.n_heads * D, device=dev) if world > 1 else out
+    L = w.n_layers
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L * args.steps)]
+
+    def step(i=None):
+        for l in range(L):
+            if i is not None:
+                ev[i * L + l][0].record()
+            h.decode_async(l, w.pos, q[l], k[l], v[l], out[l])
+            if i is not None:
+                ev[i * L + l][1].record()
+            if world > 1:
+                pg.all_gather_into_tensor(full[l], out[l])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    h.sync()
+    if world > 1:
+        pg.barrier()
+    torch.cuda.synchronize()
+    clk = ClockSampler(local)
+    clk.start()
+    time.sleep(0.3)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(args.steps):
+        step(i)
+    t1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        pg.barrier()
+        torch.cuda.synchronize()
+    clocks = clk.stop()
+    h.sync()
+    elapsed_ms = t0.elapsed_time(t1)
+    kern_ms = [a.elapsed_time(b) for a, b in ev]
+    if world > 1:
+        t = torch.tensor([elapsed_ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+    ms_per_step = elapsed_ms / args.steps
+    tok_s = 1e3 / ms_per_step
+    kern_avg_ms = statistics.mean(kern_ms)
+    bytes_launch = 2 * (w.pos + 1) * s["kv_headn"] * D * 4 + (s["q_headn"] * 2 + s["kv_headn"] * 2) * D * 4
+    achieved = bytes_launch / (kern_avg_ms * 1e-3) / 1e9
+
+    # end to end through the host-pointer C call (pinned host buffers, copies inside the timed region)
+    e2e = bench_decode_e2e(args, w, h, s, q, k, v, world, local, pg)
+    h.close()
+    traffic = load_profile_traffic("decode_kernel")
+    return {
+        "value": tok_s, "ms_per_step": ms_per_step, "clocks": clocks,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
+                     "kernel": "decode_kernel<float,128,4>", "kernel_avg_us": kern_avg_ms * 1e3,
+                     "algorithmic_bytes_per_launch": bytes_launch,
+                     "peak_source": f"{peaks['source']} hbm_gbs (copy)"},
+        "hbm_gbs_step": w.kv_bytes_per_token() / world * tok_s / 1e9 * world,
+        "e2e": e2e, "gpu_launches": args.steps * L,
+    }
+
+
+def bench_decode_e2e(args, w, h, s, q, k, v, world, local, pg):
+    import torch
+    D = w.head_dim
+    L = w.n_layers
+    qh = q.cpu().pin_memory()
+    kh = k.cpu().pin_memory()
+    vh = v.cpu().pin_memory()
+    lib = h.lib
+    steps = max(3, args.steps // 3)
+    if world == 1:
+        outh = torch.empty(L, s["q_headn"] * D).pin_memory()
+
+        def step():
+            for l in range(L):
+                rc = lib.ligguf_cuda_attn_decode(h.handle, l, w.pos, qh[l].data_ptr(), kh[l].data_ptr(),
+                                                 vh[l].data_ptr(), outh[l].data_ptr())
+                if rc:
+                    raise RuntimeError(f"decode failed {rc}")
+        h2d = L * (qh.shape[1] + 2 * kh.shape[1]) * 4
+        d2h = L * outh.shape[1] * 4
+    else:
+        dev = torch.device("cuda", local)
+        qd, kd, od = torch.empty_like(q[0]), torch.empty_like(k[0]), torch.empty_like(q[0])
+        vd = torch.empty_like(v[0])
+        full = torch.empty(w.n_heads * D, device=dev)
+        outh = torch.empty(L, w.n_heads * D).pin_memory()
+
+        def step():
+            for l in range(L):
+                qd.copy_(qh[l], non_blocking=True)
+                kd.copy_(kh[l], non_blocking=True)
+                vd.copy_(vh[l], non_blocking=True)
+                h.decode_async(l, w.pos, qd, kd, vd, od)
+                pg.all_gather_into_tensor(full, od)
+                outh[l].copy_(full, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+        h2d = L * (qh.shape[1] + 2 * kh.shape[1]) * 4
+        d2h = L * w.n_heads * D * 4
+    for _ in range(2):
+        step()
+    if world > 1:
+        pg.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    torch.cuda.synchronize()
+    el = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([el], device=torch.device("cuda", local))
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        el = float(t.item())
+    return {"value": steps / el, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "steps": steps, "api": "ligguf_cuda_attn_decode (host pointers)" if world == 1 else
+            "ligguf_cuda_attn_decode_async + NCCL all-gather, pinned host copies"}
+
+
+# ------------------------------------------------------------------------------ other configurations
+def _time_ms(fn, iters, warm=3):
+    import torch
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / iters
+
+
+def extra_decode_4k(peaks):
+    """qwen3_8b_decode_4k: one token step (36 layer launches) captured in a CUDA graph."""
+    import torch
+    from ligguf_b200.workloads import QWEN3_DECODE_4K as w
+    h, s, q, k, v = decode_setup(w, 0, 1, torch.cuda.current_device())
+    out = torch.empty(w.n_layers, w.n_heads * w.head_dim, device=q.device)
+
+    def step():
+        for l in range(w.n_layers):
+            h.decode_async(l, w.pos, q[l], k[l], v[l], out[l])
+    step()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    ms = _time_ms(g.replay, 50)
+    h.sync()
+    del g
+    h.close()
+    gbs = w.kv_bytes_per_token() / (ms * 1e-3) / 1e9
+    return {"tokens_s": 1e3 / ms, "ms_per_token": ms, "hbm_gbs": gbs, "frac_of_hbm": gbs / peaks["hbm_gbs"],
+            "note": "CUDA-graph replay of the 36 per-layer launches; GB/s counts algorithmic K+V bytes"}
+
+
+def extra_prefill(peaks, mode):
+    import torch
+    from ligguf_b200 import AttnConfig, CudaAttention, synth_fill
+    from ligguf_b200.workloads import QWEN3_PREFILL as w
+    from ligguf_b200.workloads import SYNTH_KNEW, SYNTH_Q, SYNTH_VNEW, stream_id
+    dev = torch.device("cuda", torch.cuda.current_device())
+    cfg = AttnConfig(n_layers=w.n_layers, n_heads=w.n_heads, n_kv_heads=w.n_kv_heads, head_dim=w.head_dim,
+                     n_context=w.n_context, rope_dim=w.rope_dim, rope_base=w.rope_base, rms_epsilon=w.eps,
+                     qk_norm=w.qk_norm, device=dev.index)
+    h = CudaAttention(cfg)
+    import numpy as np
+    g = np.ones(w.head_dim, dtype=np.float32)
+    for l in range(w.n_layers):
+        h.set_qk_norm(l, g, g)
+    n, D = w.n_tokens, w.head_dim
+    q = torch.empty(n, w.n_heads * D, device=dev)
+    k = torch.empty(n, w.n_kv_heads * D, device=dev)
+    v = torch.empty_like(k)
+    out = torch.empty_like(q)
+    synth_fill(q, q.numel(), w.seed, stream_id(SYNTH_Q, 0), 0, w.scale)
+    synth_fill(k, k.numel(), w.seed, stream_id(SYNTH_KNEW, 0), 0, w.scale)
+    synth_fill(v, v.numel(), w.seed, stream_id(SYNTH_VNEW, 0), 0, w.scale)
+
+    def run():
+        for l in range(w.n_layers):
+            h.prefill_async(l, w.pos0, n, q, k, v, out, mode)
+    ms = _time_ms(run, 3 if mode == 0 else 10, warm=1)
+    h.sync()
+    h.close()
+    flops = w.causal_flops_per_layer() * w.n_layers
+    tf = flops / (ms * 1e-3) / 1e12
+    peak = peaks["bf16_tflops"] if mode == 1 else None
+    r = {"ms_36_layers": ms, "tflops": tf, "causal_flops": flops}
+    if peak:
+        r["frac_of_bf16_peak"] = tf / peak
+    return r
+
+
+def extra_bert(peaks, mode):
+    import torch
+    from ligguf_b200 import CudaBertAttention, synth_fill
+    from ligguf_b200.workloads import BERT_BASE as w
+    from ligguf_b200.workloads import SYNTH_K, SYNTH_Q, SYNTH_V, stream_id
+    dev = torch.device("cuda", torch.cuda.current_device())
+    E = w.n_heads * w.head_dim
+    n = w.batch * w.max_len * E
+    q, k, v, out = (torch.empty(n, device=dev) for _ in range(4))
+    for t, x in ((SYNTH_Q, q), (SYNTH_K, k), (SYNTH_V, v)):
+        synth_fill(x, n, w.seed, stream_id(t, 0), 0, w.scale)
+    lens = torch.tensor(w.lens(), dtype=torch.int32, device=dev)
+    h = CudaBertAttention(w.n_heads, w.head_dim, w.batch, w.max_len, dev.index)
+
+    def run():
+        for _ in range(w.n_layers):
+            h.attn_async(w.batch, w.max_len, lens, q, k, v, out, mode)
+    ms = _time_ms(run, 5, warm=1)
+    h.close()
+    flops = w.flops_per_layer() * w.n_layers
+    tf = flops / (ms * 1e-3) / 1e12
+    r = {"ms_12_layers": ms, "tflops": tf, "flops": flops}
+    if mode == 1:
+        r["frac_of_bf16_peak"] = tf / peaks["bf16_tflops"]
+    return r
+
+
+def run_extras(peaks):
+    extra = {}
+    jobs = [("qwen3_8b_decode_4k", lambda: extra_decode_4k(peaks)),
+            ("qwen3_8b_prefill_2048_simt_fp32", lambda: extra_prefill(peaks, 0)),
+            ("qwen3_8b_prefill_2048_tc_bf16", lambda: extra_prefill(peaks, 1)),
+            ("bert_base_attn_simt_fp32", lambda: extra_bert(peaks, 0)),
+            ("bert_base_attn_tc_bf16", lambda: extra_bert(peaks, 1))]
+    for name, fn in jobs:
+        try:
+            extra[name] = fn()
+        except Exception as e:  # the headline line must still print
+            extra[name] = {"error": f"{type(e).__name__}: {e}"[:300]}
+    return extra
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    import torch
+    from ligguf_b200 import load
+    from ligguf_b200.workloads import DECODE_WORKLOADS
+    load()
+    rank, world, local, pg = setup_dist(args)
+    peaks = load_peaks()
+    w = DECODE_WORKLOADS[WORKLOAD]
+    res = bench_decode(args, w, rank, world, local, pg, peaks)
+    extra = {}
+    cb = None
+    if world == 1 and rank == 0:
+        if not args.no_extra:
+            extra = run_extras(peaks)
+        if not args.no_cpu:
+            cb = cpu_baseline(w)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": res["value"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "higher_is_better": True,
+            "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded generator, ~N(0,1)); random-init QK-norm weights",
+            "config": {"workload": WORKLOAD, "layers": w.n_layers, "ctx": w.pos + 1, "kv": "fp32",
+                       "heads": [w.n_heads, w.n_kv_heads, w.head_dim],
+                       "parallelism": f"kv-head shards x{world} + NCCL all-gather per layer" if world > 1
+                       else "single GPU",
+                       "l2": "inputs larger than L2 (KV bytes per step >> 126 MB); no flush"},
+            "hbm_gbs": res["hbm_gbs_step"],
+            "roofline": res["roofline"], "clocks": res["clocks"], "e2e": res["e2e"],
+            "gpu_launches": res["gpu_launches"],
+        }
+        if cb is not None:
+            line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        if extra:
+            line["extra"] = extra
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,197 @@
+/*
+ * ligguf_cuda_attn.h - C ABI of the B200 (sm_100a) attention block for LiGGUF's FAST engine.
+ *
+ * The reference engine has no plugin or FFI layer for attention: the block is inline code in
+ * `void inference(int tok)` (fast/ligguf_fast_qk.cpp:24-105) working on the global
+ * `model_state g_m` (fast/common.h:33-74).  This header is the drop-in boundary that replaces
+ * that inline block: plain C types, plain pointers and sizes, int status codes, no torch and
+ * no CUDA types in any signature (streams and IPC handles travel as `void*`).
+ *
+ * Conventions (mirroring the reference's):
+ *   - one host thread drives one handle, like `inference()` is driven by one thread
+ *     (fast/ligguf_fast_qk.cpp:316-322); a handle is not re-entrant and its kernels of one
+ *     call must not overlap on the GPU with those of another call on the same handle;
+ *   - `pos` is explicit on every call (the reference keeps it in g_m.pos and increments it at
+ *     fast/ligguf_fast_qk.cpp:27); rewinding (kv_backtrack, fast/ligguf_fast_qk.cpp:333-338)
+ *     is therefore just passing a smaller pos;
+ *   - errors never abort: every entry point returns 0 or a negative LIGGUF_ATTN_E* code, and
+ *     ligguf_cuda_attn_last_error() gives a one-line reason (the reference prints with ERR,
+ *     fast/common.h:14, or asserts).
+ */
+#ifndef LIGGUF_CUDA_ATTN_H
+#define LIGGUF_CUDA_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------------------------- */
+#define LIGGUF_ATTN_OK 0
+#define LIGGUF_ATTN_EINVAL (-1)      /* bad argument (NULL, out-of-range layer/pos, bad dims) */
+#define LIGGUF_ATTN_ECUDA (-2)       /* a CUDA runtime call failed */
+#define LIGGUF_ATTN_ENOMEM (-3)      /* device or pinned host allocation failed */
+#define LIGGUF_ATTN_ETIMEDOUT (-4)   /* a bounded in-kernel wait gave up (kernel returned early) */
+#define LIGGUF_ATTN_EUNSUPPORTED (-5)/* shape/type combination without a kernel */
+#define LIGGUF_ATTN_ESTATE (-6)      /* call not valid in the handle's current state */
+
+/* ---- enums ----------------------------------------------------------------------------- */
+/* KV-cache element type.  FAST stores fp16 (`htensor kc, vc`, fast/common.h:60, written with
+ * f32_to_f16_row at fast/ligguf_fast_qk.cpp:61-62); the single-file engines store fp32
+ * (cpp/ligguf.cpp:674-679, cpp/ligguf_distrib.cpp:724-727).  bf16 has no reference
+ * counterpart and exists for the tensor-core prefill path. */
+#define LIGGUF_KV_F32 0
+#define LIGGUF_KV_F16 1
+#define LIGGUF_KV_BF16 2
+
+/* Score scaling.  FAST multiplies by att_scale = 1/sqrtf(head_dim)
+ * (fast/ligguf_fast_qk.cpp:26,85; fast/vdb.cpp:133,203); the cpp/c/SARA engines divide by
+ * sqrtf(head_dim) (cpp/ligguf.cpp:696, c/ligguf.c, cpp/ligguf_distrib.cpp:735). */
+#define LIGGUF_SCALE_MUL 0
+#define LIGGUF_SCALE_DIV 1
+
+/* Prefill / BERT arithmetic: fp32 on CUDA cores (tight-tolerance path) or bf16 operands on
+ * the tcgen05 tensor cores with fp32 accumulation. */
+#define LIGGUF_MODE_SIMT 0
+#define LIGGUF_MODE_TC 1
+
+/* ---- decoder attention handle ---------------------------------------------------------- */
+typedef struct ligguf_attn_cfg {
+    int n_layers;        /* gguf_model::n_layers (fast/lil_gguf.h:166) */
+    int n_heads;         /* query heads of the whole model (gguf_model::n_heads) */
+    int n_kv_heads;      /* KV heads of the whole model (gguf_model::n_kv_heads) */
+    int head_dim;        /* gguf_model::head_dim; 64 or 128 */
+    int n_context;       /* cache positions per layer (gguf_model::n_context after allocate(),
+                            fast/common.cpp:13-19) */
+    int rope_dim;        /* gguf_model::rope_dim; clamped to head_dim and made even exactly as
+                            rope() does (fast/lil_math.cpp:904-906); 0 = no RoPE */
+    float rope_base;     /* gguf_model::rope_base (theta) */
+    const float* rope_freq; /* optional host table of rope_dim/2 inverse frequencies
+                            (model_state::rope_freq, fast/common.cpp:34,38-39); NULL = the
+                            library computes powf(rope_base, -2i/rope_dim) the same way */
+    float rms_epsilon;   /* gguf_model::rms_epsilon, used by the Qwen3 QK norm */
+    int qk_norm;         /* 1 = per-head RMSNorm of q and k before RoPE (arch "qwen3",
+                            fast/ligguf_fast_qk.cpp:42-51) */
+    int kv_type;         /* LIGGUF_KV_* */
+    int scale_mode;      /* LIGGUF_SCALE_* */
+    int device;          /* CUDA device ordinal the cache lives on */
+    int kv_head0;        /* SARA shard: first KV head owned (shard_desc::kv_head0,
+                            cpp/ligguf_distrib.cpp:120-124,665-679); 0 when unsharded */
+    int kv_headn;        /* SARA shard: KV heads owned; 0 = all n_kv_heads */
+} ligguf_attn_cfg;
+
+typedef struct ligguf_attn ligguf_attn;
+
+/* Replaces the attention part of model_state::allocate() (fast/common.cpp:31-39): allocates the
+ * HBM-resident cache [n_layers][n_context][kv_headn*head_dim] (zero-filled, the reference's
+ * kc.resize(...,0)), the RoPE table and per-layer QK-norm weights.  The q heads owned are
+ * [kv_head0*nrep, (kv_head0+kv_headn)*nrep), nrep = n_heads/n_kv_heads
+ * (cpp/ligguf_distrib.cpp:668-669). */
+int ligguf_cuda_attn_init(const ligguf_attn_cfg* cfg, ligguf_attn** out);
+int ligguf_cuda_attn_free(ligguf_attn* h);
+const char* ligguf_cuda_attn_strerror(int status);
+/* One-line reason for the last failure on the calling host thread ("" if none). */
+const char* ligguf_cuda_attn_last_error(void);
+
+/* Device-resident copies of one layer's attn_q_norm / attn_k_norm weights (head_dim floats each,
+ * host pointers; gguf trans_block::att_q_norm/att_k_norm, fast/lil_gguf.h:138-139).  Required
+ * for every layer when cfg.qk_norm is set. */
+int ligguf_cuda_attn_set_qk_norm(ligguf_attn* h, int layer, const float* q_gamma,
+                                 const float* k_gamma);
+
+/* One decode step of one layer: replaces fast/ligguf_fast_qk.cpp:42-105.
+ *   q   [q_headn*head_dim]  raw projection output g_m.q (pre norm, pre RoPE)
+ *   k,v [kv_headn*head_dim] raw g_m.k / g_m.v
+ *   out [q_headn*head_dim]  attention result, the reference's g_m.xb
+ * Applies QK norm (if enabled) and RoPE at `pos`, appends k,v to the cache row `pos`, and
+ * attends over positions [0, pos] with position `pos` taken from the fp32 k,v as FAST does
+ * (fast/ligguf_fast_qk.cpp:77-78,98-99).  Host pointers; returns when `out` is written. */
+int ligguf_cuda_attn_decode(ligguf_attn* h, int layer, int pos, const float* q, const float* k,
+                            const float* v, float* out);
+/* Same with device pointers, enqueued on `stream` (a cudaStream_t; NULL = legacy default). */
+int ligguf_cuda_attn_decode_async(ligguf_attn* h, int layer, int pos, const float* d_q,
+                                  const float* d_k, const float* d_v, float* d_out,
+                                  void* stream);
+
+/* Causal prefill of n tokens at positions [pos0, pos0+n) of one layer.  The reference has no
+ * batched prefill: feed_text() runs inference() once per token (fast/ligguf_fast_qk.cpp:340-356),
+ * so the result equals n decode calls at pos0..pos0+n-1.
+ *   q [n][q_headn*head_dim], k,v [n][kv_headn*head_dim] raw; out [n][q_headn*head_dim].
+ * mode: LIGGUF_MODE_SIMT (fp32) or LIGGUF_MODE_TC (bf16 tcgen05, fp32 accumulate). */
+int ligguf_cuda_attn_prefill(ligguf_attn* h, int layer, int pos0, int n, const float* q,
+                             const float* k, const float* v, float* out, int mode);
+int ligguf_cuda_attn_prefill_async(ligguf_attn* h, int layer, int pos0, int n, const float* d_q,
+                                   const float* d_k, const float* d_v, float* d_out, int mode,
+                                   void* stream);
+
+/* Cache rows [pos0, pos0+n) of one layer, in the handle's kv_type, row layout
+ * [n][kv_headn*head_dim] - with kv_type F16 this is byte-for-byte the per-layer block that
+ * save_model_state/load_model_state write and read (fast/ligguf_fast_qk.cpp:236-247,288-295). */
+int ligguf_cuda_attn_kv_download(ligguf_attn* h, int layer, int pos0, int n, void* host_k,
+                                 void* host_v);
+int ligguf_cuda_attn_kv_upload(ligguf_attn* h, int layer, int pos0, int n, const void* host_k,
+                               const void* host_v);
+/* Fills cache rows [pos0, pos0+n) of layers [layer0, layer0+n_layers) with the library's seeded
+ * synthetic generator (ligguf_cuda_synth_fill, tensor ids LIGGUF_SYNTH_K / _V), indexed by the
+ * unsharded element (row*n_kv_heads*head_dim + kv_head*head_dim + d) so that every sharding of
+ * the same model sees the same cache.  For benchmarks and tests. */
+int ligguf_cuda_attn_kv_synth(ligguf_attn* h, int layer0, int n_layers, int pos0, int n,
+                              uint64_t seed, float scale);
+/* Waits for all work the handle enqueued on its own stream (host-pointer calls). */
+int ligguf_cuda_attn_sync(ligguf_attn* h);
+
+/* ---- SARA all-gather over NVLink peer memory -------------------------------------------- */
+/* The reference's SARA run reduces per-rank partials over TCP (cpp/ligguf_distrib.cpp:1025-1047).
+ * Here every rank owns a KV-head slice and the per-head outputs are all-gathered.  These calls
+ * set up a gather buffer [n_heads*head_dim] fp32 per rank, shared through CUDA IPC; decode_gather
+ * then stores this rank's head outputs straight into every peer's buffer from the decode
+ * kernel's epilogue and raises a per-layer flag on each peer; gather_wait waits (bounded) until
+ * all ranks' slices of `layer` arrived and copies the full vector to d_out. */
+int ligguf_cuda_attn_gather_ipc_handle(ligguf_attn* h, void* handle_out /* 64 bytes */,
+                                       size_t handle_size);
+int ligguf_cuda_attn_gather_open(ligguf_attn* h, int nranks, int rank,
+                                 const void* handles /* nranks * 64 bytes */,
+                                 size_t handle_size);
+int ligguf_cuda_attn_decode_gather_async(ligguf_attn* h, int layer, int pos, const float* d_q,
+                                         const float* d_k, const float* d_v, void* stream);
+int ligguf_cuda_attn_gather_wait_async(ligguf_attn* h, int layer, float* d_out, void* stream);
+
+/* ---- BERT embedding attention ------------------------------------------------------------ */
+/* Replaces the per-sequence loop of bert_embed() (fast/vdb.cpp:189-212): bidirectional
+ * multi-head attention, no RoPE, no mask within a sequence.  Batched: `batch` sequences padded
+ * to max_len, lens[b] valid tokens each (keys at or beyond lens[b] are masked out, padded query
+ * rows are written as zeros).
+ *   q,k,v,out [batch][max_len][n_heads*head_dim] fp32 (the reference's m_brt.q/k/v/ctx rows). */
+typedef struct ligguf_bert_attn ligguf_bert_attn;
+int ligguf_cuda_bert_init(int n_heads, int head_dim, int max_batch, int max_len, int device,
+                          ligguf_bert_attn** out);
+int ligguf_cuda_bert_free(ligguf_bert_attn* b);
+int ligguf_cuda_bert_attn(ligguf_bert_attn* b, int batch, int max_len, const int* lens,
+                          const float* q, const float* k, const float* v, float* out, int mode);
+int ligguf_cuda_bert_attn_async(ligguf_bert_attn* b, int batch, int max_len, const int* d_lens,
+                                const float* d_q, const float* d_k, const float* d_v,
+                                float* d_out, int mode, void* stream);
+
+/* ---- seeded synthetic inputs ------------------------------------------------------------- */
+/* Tensor ids of the synthetic generator's streams. */
+#define LIGGUF_SYNTH_K 1
+#define LIGGUF_SYNTH_V 2
+#define LIGGUF_SYNTH_Q 3
+#define LIGGUF_SYNTH_KNEW 4
+#define LIGGUF_SYNTH_VNEW 5
+#define LIGGUF_SYNTH_QGAMMA 6
+#define LIGGUF_SYNTH_KGAMMA 7
+/* dst[i] = (float)(a+b+c+d - 131070) * mul + add, rounded to dtype (LIGGUF_KV_*), where a..d are
+ * the four 16-bit fields of splitmix64(splitmix64(seed ^ stream*0xD1B54A32D192ED03) + idx0 + i).
+ * mul = scale / 37837.23 (computed in double, rounded to float) makes the values approximately
+ * N(add, scale^2) (Irwin-Hall of 4 uniforms).  Integer arithmetic plus one fp32 multiply and
+ * one add, so the host restatement reproduces it bit for bit. */
+int ligguf_cuda_synth_fill(void* d_dst, int dtype, size_t n, uint64_t seed, uint64_t stream_id,
+                           uint64_t idx0, float scale, float add, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LIGGUF_CUDA_ATTN_H */

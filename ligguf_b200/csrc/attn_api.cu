@@ -1,0 +1,989 @@
+// attn_api.cu - the C ABI declared in include/ligguf_cuda_attn.h: handle life cycle, HBM-resident
+// KV cache, argument checking, kernel dispatch and the host-pointer convenience calls.
+//
+// Nothing here falls back to the CPU: every compute entry point launches one of the CUDA kernels
+// of this library or returns an error code.
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "ligguf_cuda_attn.h"
+#include "common.cuh"
+#include "decode.cuh"
+#include "flash_simt.cuh"
+#include "flash_tc.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+#define LG_CUDA(expr)                                                                          \
+    do {                                                                                       \
+        const cudaError_t e_ = (expr);                                                         \
+        if (e_ != cudaSuccess)                                                                 \
+            return fail(LIGGUF_ATTN_ECUDA, "%s failed: %s (%s:%d)", #expr,                     \
+                        cudaGetErrorString(e_), __FILE__, __LINE__);                           \
+    } while (0)
+
+struct DeviceGuard {
+    int prev = -1;
+    bool switched = false;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) == cudaSuccess && prev != dev) switched = cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        if (switched) cudaSetDevice(prev);
+    }
+};
+
+inline int ceil_div(long long a, long long b) { return static_cast<int>((a + b - 1) / b); }
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+size_t kv_elem_size(int kv_type) { return kv_type == LIGGUF_KV_F32 ? 4 : 2; }
+
+CUtensorMapDataType kv_tmap_type(int kv_type) {
+    return kv_type == LIGGUF_KV_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+           : kv_type == LIGGUF_KV_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                      : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+}
+
+// Per (kernel instantiation, device): raise the dynamic shared memory limit once.
+template <typename K>
+cudaError_t ensure_smem_attr(K kernel, int device, size_t bytes) {
+    static bool done[64] = {};
+    if (device >= 0 && device < 64 && done[device]) return cudaSuccess;
+    const cudaError_t e =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+    if (e == cudaSuccess && device >= 0 && device < 64) done[device] = true;
+    return e;
+}
+
+// ---------------------------------------------------------------------------- synth kernels
+template <typename T>
+__global__ void synth_fill_kernel(T* dst, size_t n, uint64_t base, uint64_t idx0, float mul, float add) {
+    for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x)
+        dst[i] = lg::KvTraits<T>::from_float(lg::synth_value(base, idx0 + i, mul, add));
+}
+
+template <typename T>
+__global__ void kv_synth_kernel(T* layer_base, int kv_dim, int kv_dim_full, int kv_off, int pos0, int n,
+                                uint64_t base, float mul) {
+    const size_t total = size_t(n) * kv_dim;
+    for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
+        const int rr = static_cast<int>(i / kv_dim), c = static_cast<int>(i % kv_dim);
+        const size_t t = size_t(pos0) + rr;
+        const uint64_t idx = uint64_t(t) * uint64_t(kv_dim_full) + uint64_t(kv_off + c);
+        layer_base[t * kv_dim + c] = lg::KvTraits<T>::from_float(lg::synth_value(base, idx, mul, 0.f));
+    }
+}
+
+float synth_mul(float scale) { return static_cast<float>(static_cast<double>(scale) / lg::kSynthSd); }
+
+// ---------------------------------------------------------------------------- gather wait
+// Waits (bounded) until every KV head's flag in `flags` shows `epoch`, then copies the gathered
+// vector to `out`.  One CTA.
+__global__ void gather_wait_kernel(const float* gathered, const int* flags, int n_flags, int epoch, float* out,
+                                   int n, int* err) {
+    __shared__ int ok_s;
+    if (threadIdx.x == 0) {
+        const uint64_t deadline = lg::globaltimer_ns() + lg::kWaitLimitNs;
+        int ok = 1;
+        for (int i = 0; i < n_flags && ok; ++i) {
+            int v;
+            while (true) {
+                asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(flags + i) : "memory");
+                if (v == epoch) break;
+                if (lg::globaltimer_ns() > deadline) {
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+        if (!ok) *reinterpret_cast<volatile int*>(err) = lg::KERR_TIMEOUT_PEER;
+        ok_s = ok;
+    }
+    __syncthreads();
+    if (!ok_s) return;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = __ldcv(gathered + i);
+}
+
+}  // namespace
+
+// ============================================================================== handle
+struct ligguf_attn {
+    ligguf_attn_cfg cfg{};
+    int nrep = 0, q_headn = 0, kv_dim = 0, kv_dim_full = 0, rope_pairs = 0, num_sms = 0;
+    size_t es = 0, layer_elems = 0;
+    void* kc = nullptr;
+    void* vc = nullptr;
+    float* freq = nullptr;
+    float* qg = nullptr;  // [n_layers][D]
+    float* kg = nullptr;
+    std::vector<uint8_t> norm_set;
+    float* part = nullptr;
+    int* counters = nullptr;
+    int* h_err = nullptr;  // mapped pinned word the kernels write on failure
+    int* d_err = nullptr;
+    cudaStream_t stream = nullptr;
+    float* d_stage = nullptr;  // device staging for the host-pointer calls
+    size_t stage_floats = 0;
+    float* qf = nullptr;  // prefill fp32 q rows
+    size_t qf_floats = 0;
+    __nv_bfloat16* qb = nullptr;  // prefill bf16 q rows
+    size_t qb_elems = 0;
+    __nv_bfloat16* kb = nullptr;  // bf16 shadows of one layer's K/V [n_context][kv_dim]
+    __nv_bfloat16* vb = nullptr;
+    alignas(64) CUtensorMap tm_k;
+    alignas(64) CUtensorMap tm_v;
+    // SARA gather over CUDA IPC
+    float* gbuf = nullptr;  // [2][n_heads*D] floats then [2][n_kv_heads] ints
+    size_t gbuf_bytes = 0;
+    int g_nranks = 0, g_rank = -1, g_epoch = 0;
+    std::vector<void*> g_opened;
+    float** d_peer_out = nullptr;  // [2][nranks]
+    int** d_peer_flag = nullptr;   // [2][nranks]
+};
+
+struct ligguf_bert_attn {
+    int n_heads = 0, head_dim = 0, max_batch = 0, max_len = 0, device = 0;
+    int* d_lens = nullptr;
+    float* d_buf = nullptr;  // q, k, v, out staging for the host-pointer call
+    __nv_bfloat16* bf = nullptr;  // bf16 q, k, v for the tensor-core path
+    int* h_err = nullptr;
+    int* d_err = nullptr;
+    cudaStream_t stream = nullptr;
+};
+
+namespace {
+
+int check_err_word(int* h_err, int* counters, size_t n_counters) {
+    if (h_err && *reinterpret_cast<volatile int*>(h_err)) {
+        const int code = *h_err;
+        *reinterpret_cast<volatile int*>(h_err) = 0;
+        if (counters) cudaMemset(counters, 0, n_counters * sizeof(int));
+        return fail(LIGGUF_ATTN_ETIMEDOUT, "a bounded in-kernel wait gave up (kernel error code %d)", code);
+    }
+    return LIGGUF_ATTN_OK;
+}
+
+int make_cache_tmap(CUtensorMap* m, void* base, const ligguf_attn* h, int tile_rows) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return fail(LIGGUF_ATTN_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    const int D = h->cfg.head_dim;
+    const int kvh = h->kv_dim / D;
+    cuuint64_t dims[3] = {cuuint64_t(D), cuuint64_t(kvh),
+                          cuuint64_t(h->cfg.n_layers) * cuuint64_t(h->cfg.n_context)};
+    cuuint64_t strides[2] = {cuuint64_t(D) * h->es, cuuint64_t(h->kv_dim) * h->es};
+    cuuint32_t box[3] = {cuuint32_t(D), 1u, cuuint32_t(tile_rows)};
+    cuuint32_t estr[3] = {1u, 1u, 1u};
+    const CUresult r = enc(m, kv_tmap_type(h->cfg.kv_type), 3, base, dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(LIGGUF_ATTN_ECUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+    return LIGGUF_ATTN_OK;
+}
+
+int decode_tile_rows(int kv_type, int D) { return lg::kDecodeTileBytes / (D * int(kv_elem_size(kv_type))); }
+
+template <typename KV, int D, int NREP>
+int launch_decode_t(ligguf_attn* h, const lg::DecodeArgs& a, cudaStream_t st) {
+    using Sm = lg::DecodeSmem<KV, D, NREP>;
+    auto kern = lg::decode_kernel<KV, D, NREP>;
+    LG_CUDA(ensure_smem_attr(kern, h->cfg.device, Sm::kTotal));
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(a.n_split, h->kv_dim / D, 1);
+    lc.blockDim = dim3(lg::kDecodeThreads, 1, 1);
+    lc.dynamicSmemBytes = Sm::kTotal;
+    lc.stream = st;
+    LG_CUDA(cudaLaunchKernelEx(&lc, kern, h->tm_k, h->tm_v, a));
+    return LIGGUF_ATTN_OK;
+}
+
+template <typename KV, int D>
+int launch_decode_d(ligguf_attn* h, const lg::DecodeArgs& a, cudaStream_t st) {
+    switch (h->nrep) {
+        case 1: return launch_decode_t<KV, D, 1>(h, a, st);
+        case 2: return launch_decode_t<KV, D, 2>(h, a, st);
+        case 4: return launch_decode_t<KV, D, 4>(h, a, st);
+        case 8: return launch_decode_t<KV, D, 8>(h, a, st);
+        default: return fail(LIGGUF_ATTN_EUNSUPPORTED, "nrep %d has no decode kernel (1, 2, 4, 8)", h->nrep);
+    }
+}
+
+template <typename KV>
+int launch_decode_k(ligguf_attn* h, const lg::DecodeArgs& a, cudaStream_t st) {
+    if (h->cfg.head_dim == 64) return launch_decode_d<KV, 64>(h, a, st);
+    if (h->cfg.head_dim == 128) return launch_decode_d<KV, 128>(h, a, st);
+    return fail(LIGGUF_ATTN_EUNSUPPORTED, "head_dim %d has no decode kernel", h->cfg.head_dim);
+}
+
+// Blocks of the decode kernel resident per SM (its __launch_bounds__ minimum).
+int decode_blocks_per_sm(int kv_type, int nrep) { return nrep * (kv_type == LIGGUF_KV_F32 ? 4 : 8) > 32 ? 1 : 2; }
+
+int decode_enqueue(ligguf_attn* h, int layer, int pos, const float* dq, const float* dk, const float* dv,
+                   float* dout, cudaStream_t st, bool gather) {
+    const ligguf_attn_cfg& c = h->cfg;
+    if (layer < 0 || layer >= c.n_layers) return fail(LIGGUF_ATTN_EINVAL, "layer %d out of range", layer);
+    if (pos < 0 || pos >= c.n_context)
+        return fail(LIGGUF_ATTN_EINVAL, "pos %d out of range [0, %d)", pos, c.n_context);
+    if (!dq || !dk || !dv || (!dout && !gather)) return fail(LIGGUF_ATTN_EINVAL, "null tensor pointer");
+    if (c.qk_norm && !h->norm_set[layer])
+        return fail(LIGGUF_ATTN_ESTATE, "QK-norm weights of layer %d were not set", layer);
+    const int D = c.head_dim;
+    lg::DecodeArgs a = {};
+    a.q = dq;
+    a.k = dk;
+    a.v = dv;
+    a.qg = c.qk_norm ? h->qg + size_t(layer) * D : nullptr;
+    a.kg = c.qk_norm ? h->kg + size_t(layer) * D : nullptr;
+    a.freq = h->freq;
+    a.kc = static_cast<char*>(h->kc) + size_t(layer) * h->layer_elems * h->es;
+    a.vc = static_cast<char*>(h->vc) + size_t(layer) * h->layer_elems * h->es;
+    a.out = dout;
+    a.part = h->part;
+    a.counters = h->counters;
+    a.err = h->d_err;
+    a.row0 = layer * c.n_context;
+    a.pos = pos;
+    const int tp = decode_tile_rows(c.kv_type, D);
+    a.n_tiles = ceil_div(pos, tp);
+    const int kvh = h->kv_dim / D;
+    const int want = std::max(1, decode_blocks_per_sm(c.kv_type, h->nrep) * h->num_sms / kvh);
+    int tps = std::max(1, ceil_div(a.n_tiles, want));
+    int ns = a.n_tiles ? ceil_div(a.n_tiles, tps) : 1;
+    while (ns > lg::kDecodeMaxSplit) {
+        ++tps;
+        ns = ceil_div(a.n_tiles, tps);
+    }
+    a.tiles_per_split = tps;
+    a.n_split = ns;
+    a.kv_dim = h->kv_dim;
+    a.rope_pairs = h->rope_pairs;
+    a.qk_norm = c.qk_norm;
+    a.scale_div = c.scale_mode == LIGGUF_SCALE_DIV;
+    a.scale = a.scale_div ? sqrtf(static_cast<float>(D)) : 1.0f / sqrtf(static_cast<float>(D));
+    a.eps = c.rms_epsilon;
+    a.kv_head0 = c.kv_head0;
+    if (gather) {
+        const int slot = h->g_epoch & 1;
+        a.peer_out = h->d_peer_out + slot * h->g_nranks;
+        a.peer_flag = h->d_peer_flag + slot * h->g_nranks;
+        a.nranks = h->g_nranks;
+        a.rank = h->g_rank;
+        a.q_off = c.kv_head0 * h->nrep * D;
+        a.flag_value = h->g_epoch;
+        // the local copy of this shard's slice lands in this rank's own gather buffer
+        a.out = reinterpret_cast<float*>(reinterpret_cast<char*>(h->gbuf) + size_t(slot) * c.n_heads * D * 4) +
+                a.q_off;
+    }
+    switch (c.kv_type) {
+        case LIGGUF_KV_F32: return launch_decode_k<float>(h, a, st);
+        case LIGGUF_KV_F16: return launch_decode_k<__half>(h, a, st);
+        default: return launch_decode_k<__nv_bfloat16>(h, a, st);
+    }
+}
+
+// ---------------------------------------------------------------------------- flash launches
+template <typename KV, int D>
+int launch_flash_simt_t(const lg::FlashArgs& f, dim3 grid, cudaStream_t st, int device) {
+    auto kern = lg::flash_simt_kernel<KV, D>;
+    LG_CUDA(ensure_smem_attr(kern, device, lg::FlashSimtSmem<D>::kBytes));
+    kern<<<grid, lg::kFlashThreads, lg::FlashSimtSmem<D>::kBytes, st>>>(f);
+    LG_CUDA(cudaGetLastError());
+    return LIGGUF_ATTN_OK;
+}
+
+template <typename KV>
+int launch_flash_simt(const lg::FlashArgs& f, int D, dim3 grid, cudaStream_t st, int device) {
+    if (D == 64) return launch_flash_simt_t<KV, 64>(f, grid, st, device);
+    if (D == 128) return launch_flash_simt_t<KV, 128>(f, grid, st, device);
+    return fail(LIGGUF_ATTN_EUNSUPPORTED, "head_dim %d has no SIMT attention kernel", D);
+}
+
+template <typename KV, int D>
+int launch_prep_t(const lg::PrepArgs& p, cudaStream_t st) {
+    lg::prefill_prep_kernel<KV, D><<<p.n, 256, 0, st>>>(p);
+    LG_CUDA(cudaGetLastError());
+    return LIGGUF_ATTN_OK;
+}
+
+template <typename KV>
+int launch_prep(const lg::PrepArgs& p, int D, cudaStream_t st) {
+    if (D == 64) return launch_prep_t<KV, 64>(p, st);
+    if (D == 128) return launch_prep_t<KV, 128>(p, st);
+    return fail(LIGGUF_ATTN_EUNSUPPORTED, "head_dim %d has no prefill kernel", D);
+}
+
+template <typename T>
+int grow(T** p, size_t* cap, size_t need) {
+    if (*cap >= need) return LIGGUF_ATTN_OK;
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+    *cap = 0;
+    if (cudaMalloc(reinterpret_cast<void**>(p), need * sizeof(T)) != cudaSuccess)
+        return fail(LIGGUF_ATTN_ENOMEM, "cudaMalloc of %zu bytes failed", need * sizeof(T));
+    *cap = need;
+    return LIGGUF_ATTN_OK;
+}
+
+int prefill_enqueue(ligguf_attn* h, int layer, int pos0, int n, const float* dq, const float* dk, const float* dv,
+                    float* dout, int mode, cudaStream_t st) {
+    const ligguf_attn_cfg& c = h->cfg;
+    if (layer < 0 || layer >= c.n_layers) return fail(LIGGUF_ATTN_EINVAL, "layer %d out of range", layer);
+    if (n < 1 || pos0 < 0 || pos0 + n > c.n_context)
+        return fail(LIGGUF_ATTN_EINVAL, "positions [%d, %d) outside [0, %d)", pos0, pos0 + n, c.n_context);
+    if (!dq || !dk || !dv || !dout) return fail(LIGGUF_ATTN_EINVAL, "null tensor pointer");
+    if (mode != LIGGUF_MODE_SIMT && mode != LIGGUF_MODE_TC) return fail(LIGGUF_ATTN_EINVAL, "mode %d", mode);
+    if (c.qk_norm && !h->norm_set[layer])
+        return fail(LIGGUF_ATTN_ESTATE, "QK-norm weights of layer %d were not set", layer);
+    const int D = c.head_dim;
+    const size_t qn = size_t(n) * h->q_headn * D;
+    lg::PrepArgs p = {};
+    p.q = dq;
+    p.k = dk;
+    p.v = dv;
+    p.qg = c.qk_norm ? h->qg + size_t(layer) * D : nullptr;
+    p.kg = c.qk_norm ? h->kg + size_t(layer) * D : nullptr;
+    p.freq = h->freq;
+    p.kc = static_cast<char*>(h->kc) + size_t(layer) * h->layer_elems * h->es;
+    p.vc = static_cast<char*>(h->vc) + size_t(layer) * h->layer_elems * h->es;
+    p.n = n;
+    p.pos0 = pos0;
+    p.q_headn = h->q_headn;
+    p.kv_headn = h->kv_dim / D;
+    p.kv_dim = h->kv_dim;
+    p.rope_pairs = h->rope_pairs;
+    p.qk_norm = c.qk_norm;
+    p.eps = c.rms_epsilon;
+    const bool div = c.scale_mode == LIGGUF_SCALE_DIV;
+    const float scale = div ? sqrtf(static_cast<float>(D)) : 1.0f / sqrtf(static_cast<float>(D));
+
+    if (mode == LIGGUF_MODE_SIMT) {
+        int rc = grow(&h->qf, &h->qf_floats, qn);
+        if (rc) return rc;
+        p.qf = h->qf;
+        switch (c.kv_type) {
+            case LIGGUF_KV_F32: rc = launch_prep<float>(p, D, st); break;
+            case LIGGUF_KV_F16: rc = launch_prep<__half>(p, D, st); break;
+            default: rc = launch_prep<__nv_bfloat16>(p, D, st); break;
+        }
+        if (rc) return rc;
+        lg::FlashArgs f = {};
+        f.q = h->qf;
+        f.q_row = h->q_headn * D;
+        f.k = p.kc;
+        f.v = p.vc;
+        f.kv_row = h->kv_dim;
+        f.out = dout;
+        f.o_row = h->q_headn * D;
+        f.n_q = n;
+        f.kv_len = pos0 + n;
+        f.causal = 1;
+        f.q_pos0 = pos0;
+        f.nrep = h->nrep;
+        f.scale_div = div;
+        f.scale = scale;
+        const dim3 grid(ceil_div(n, lg::kFlashBQ), h->q_headn, 1);
+        switch (c.kv_type) {
+            case LIGGUF_KV_F32: return launch_flash_simt<float>(f, D, grid, st, c.device);
+            case LIGGUF_KV_F16: return launch_flash_simt<__half>(f, D, grid, st, c.device);
+            default: return launch_flash_simt<__nv_bfloat16>(f, D, grid, st, c.device);
+        }
+    }
+
+    // Tensor-core path: bf16 q rows, bf16 K/V shadow rows [0, pos0+n) of this layer.
+    int rc = grow(&h->qb, &h->qb_elems, qn);
+    if (rc) return rc;
+    if (!h->kb) {
+        const size_t bytes = size_t(c.n_context) * h->kv_dim * sizeof(__nv_bfloat16);
+        if (cudaMalloc(&h->kb, bytes) != cudaSuccess || cudaMalloc(&h->vb, bytes) != cudaSuccess)
+            return fail(LIGGUF_ATTN_ENOMEM, "bf16 K/V shadow allocation failed");
+    }
+    p.qb = h->qb;
+    p.kb = h->kb;
+    p.vb = h->vb;
+    if (pos0 > 0) {  // earlier positions of the cache -> bf16 shadow
+        const size_t cnt = size_t(pos0) * h->kv_dim;
+        const int blocks = std::min(4 * h->num_sms, std::max(1, ceil_div(cnt, 256)));
+        switch (c.kv_type) {
+            case LIGGUF_KV_F32:
+                lg::cache_to_bf16_kernel<float><<<blocks, 256, 0, st>>>(static_cast<const float*>(p.kc), h->kb, cnt);
+                lg::cache_to_bf16_kernel<float><<<blocks, 256, 0, st>>>(static_cast<const float*>(p.vc), h->vb, cnt);
+                break;
+            case LIGGUF_KV_F16:
+                lg::cache_to_bf16_kernel<__half><<<blocks, 256, 0, st>>>(static_cast<const __half*>(p.kc), h->kb, cnt);
+                lg::cache_to_bf16_kernel<__half><<<blocks, 256, 0, st>>>(static_cast<const __half*>(p.vc), h->vb, cnt);
+                break;
+            default:
+                lg::cache_to_bf16_kernel<__nv_bfloat16>
+                    <<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(p.kc), h->kb, cnt);
+                lg::cache_to_bf16_kernel<__nv_bfloat16>
+                    <<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(p.vc), h->vb, cnt);
+                break;
+        }
+        LG_CUDA(cudaGetLastError());
+    }
+    switch (c.kv_type) {
+        case LIGGUF_KV_F32: rc = launch_prep<float>(p, D, st); break;
+        case LIGGUF_KV_F16: rc = launch_prep<__half>(p, D, st); break;
+        default: rc = launch_prep<__nv_bfloat16>(p, D, st); break;
+    }
+    if (rc) return rc;
+    lg::TcArgs t = {};
+    t.q = h->qb;
+    t.k = h->kb;
+    t.v = h->vb;
+    t.out = dout;
+    t.q_rows = n;
+    t.q_heads = h->q_headn;
+    t.kv_rows = pos0 + n;
+    t.kv_heads = h->kv_dim / D;
+    t.batch = 1;
+    t.q_seq = n;
+    t.kv_seq = pos0 + n;
+    t.lens = nullptr;
+    t.causal = 1;
+    t.q_pos0 = pos0;
+    t.nrep = h->nrep;
+    t.scale_log2 = (div ? 1.0f / sqrtf(static_cast<float>(D)) : scale) * 1.4426950408889634f;
+    t.err = h->d_err;
+    return lg::launch_flash_tc(t, D, st, c.device, h->num_sms) ? fail(LIGGUF_ATTN_ECUDA, "%s", lg::tc_last_error())
+                                                                : LIGGUF_ATTN_OK;
+}
+
+}  // namespace
+
+// ============================================================================== C ABI
+extern "C" {
+
+const char* ligguf_cuda_attn_strerror(int status) {
+    switch (status) {
+        case LIGGUF_ATTN_OK: return "ok";
+        case LIGGUF_ATTN_EINVAL: return "invalid argument";
+        case LIGGUF_ATTN_ECUDA: return "CUDA error";
+        case LIGGUF_ATTN_ENOMEM: return "out of memory";
+        case LIGGUF_ATTN_ETIMEDOUT: return "in-kernel wait timed out";
+        case LIGGUF_ATTN_EUNSUPPORTED: return "unsupported shape or type";
+        case LIGGUF_ATTN_ESTATE: return "invalid state for this call";
+        default: return "unknown status";
+    }
+}
+
+const char* ligguf_cuda_attn_last_error(void) { return g_last_error.c_str(); }
+
+int ligguf_cuda_attn_free(ligguf_attn* h) {
+    if (!h) return LIGGUF_ATTN_OK;
+    DeviceGuard dg(h->cfg.device);
+    if (h->stream) cudaStreamSynchronize(h->stream);
+    for (void* p : h->g_opened)
+        if (p) cudaIpcCloseMemHandle(p);
+    void* dev_ptrs[] = {h->kc, h->vc, h->freq, h->qg, h->kg, h->part, h->counters, h->d_stage, h->qf, h->qb,
+                        h->kb, h->vb, h->gbuf, h->d_peer_out, h->d_peer_flag};
+    for (void* p : dev_ptrs)
+        if (p) cudaFree(p);
+    if (h->h_err) cudaFreeHost(h->h_err);
+    if (h->stream) cudaStreamDestroy(h->stream);
+    delete h;
+    return LIGGUF_ATTN_OK;
+}
+
+int ligguf_cuda_attn_init(const ligguf_attn_cfg* cfg, ligguf_attn** out) {
+    if (!cfg || !out) return fail(LIGGUF_ATTN_EINVAL, "null cfg or out");
+    *out = nullptr;
+    ligguf_attn_cfg c = *cfg;
+    if (c.n_layers < 1 || c.n_heads < 1 || c.n_kv_heads < 1 || c.n_context < 1)
+        return fail(LIGGUF_ATTN_EINVAL, "n_layers, n_heads, n_kv_heads and n_context must be positive");
+    if (c.n_heads % c.n_kv_heads)
+        return fail(LIGGUF_ATTN_EINVAL, "n_heads %d is not a multiple of n_kv_heads %d", c.n_heads, c.n_kv_heads);
+    if (c.head_dim != 64 && c.head_dim != 128)
+        return fail(LIGGUF_ATTN_EUNSUPPORTED, "head_dim %d (supported: 64, 128)", c.head_dim);
+    if (c.kv_type < LIGGUF_KV_F32 || c.kv_type > LIGGUF_KV_BF16) return fail(LIGGUF_ATTN_EINVAL, "kv_type %d", c.kv_type);
+    if (c.scale_mode != LIGGUF_SCALE_MUL && c.scale_mode != LIGGUF_SCALE_DIV)
+        return fail(LIGGUF_ATTN_EINVAL, "scale_mode %d", c.scale_mode);
+    if (c.kv_headn == 0) {
+        if (c.kv_head0 != 0) return fail(LIGGUF_ATTN_EINVAL, "kv_head0 without kv_headn");
+        c.kv_headn = c.n_kv_heads;
+    }
+    if (c.kv_head0 < 0 || c.kv_headn < 1 || c.kv_head0 + c.kv_headn > c.n_kv_heads)
+        return fail(LIGGUF_ATTN_EINVAL, "shard [%d, %d) outside the %d KV heads", c.kv_head0, c.kv_head0 + c.kv_headn,
+                    c.n_kv_heads);
+    const int nrep = c.n_heads / c.n_kv_heads;
+    if (nrep != 1 && nrep != 2 && nrep != 4 && nrep != 8)
+        return fail(LIGGUF_ATTN_EUNSUPPORTED, "n_heads/n_kv_heads = %d (supported: 1, 2, 4, 8)", nrep);
+    if (c.rope_dim < 0) return fail(LIGGUF_ATTN_EINVAL, "rope_dim %d", c.rope_dim);
+    if (static_cast<long long>(c.n_layers) * c.n_context > (1ll << 31) - 1)
+        return fail(LIGGUF_ATTN_EINVAL, "n_layers * n_context exceeds 2^31");
+    int ndev = 0;
+    LG_CUDA(cudaGetDeviceCount(&ndev));
+    if (c.device < 0 || c.device >= ndev) return fail(LIGGUF_ATTN_EINVAL, "device %d of %d", c.device, ndev);
+
+    DeviceGuard dg(c.device);
+    ligguf_attn* h = new ligguf_attn();
+    h->cfg = c;
+    h->cfg.rope_freq = nullptr;
+    h->nrep = nrep;
+    h->q_headn = c.kv_headn * nrep;
+    h->kv_dim = c.kv_headn * c.head_dim;
+    h->kv_dim_full = c.n_kv_heads * c.head_dim;
+    int rd = c.rope_dim > c.head_dim ? c.head_dim : c.rope_dim;  // fast/lil_math.cpp:904-906
+    if (rd & 1) rd--;
+    h->rope_pairs = rd / 2;
+    h->es = kv_elem_size(c.kv_type);
+    h->layer_elems = size_t(c.n_context) * h->kv_dim;
+    h->norm_set.assign(c.n_layers, 0);
+    int rc = LIGGUF_ATTN_OK;
+    auto bail = [&](int code) {
+        ligguf_cuda_attn_free(h);
+        return code;
+    };
+    if (cudaDeviceGetAttribute(&h->num_sms, cudaDevAttrMultiProcessorCount, c.device) != cudaSuccess)
+        return bail(fail(LIGGUF_ATTN_ECUDA, "cudaDeviceGetAttribute failed"));
+    if (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess)
+        return bail(fail(LIGGUF_ATTN_ECUDA, "cudaStreamCreate failed"));
+    const size_t cache_bytes = size_t(c.n_layers) * h->layer_elems * h->es;
+    if (cudaMalloc(&h->kc, cache_bytes) != cudaSuccess || cudaMalloc(&h->vc, cache_bytes) != cudaSuccess)
+        return bail(fail(LIGGUF_ATTN_ENOMEM, "KV cache of 2 x %zu bytes does not fit", cache_bytes));
+    if (cudaMemset(h->kc, 0, cache_bytes) != cudaSuccess || cudaMemset(h->vc, 0, cache_bytes) != cudaSuccess)
+        return bail(fail(LIGGUF_ATTN_ECUDA, "cudaMemset of the cache failed"));
+    // RoPE table: the caller's, else powf(base, -2i/rope_dim) as fast/common.cpp:38-39.
+    const int nfreq = std::max(1, c.rope_dim / 2);
+    std::vector<float> freq(nfreq, 0.f);
+    for (int i = 0; i < c.rope_dim / 2; i++)
+        freq[i] = cfg->rope_freq ? cfg->rope_freq[i]
+                                 : powf(c.rope_base, -2.0f * static_cast<float>(i) / static_cast<float>(c.rope_dim));
+    const size_t pd = size_t(c.n_layers) * c.head_dim;
+    const size_t part_floats = size_t(c.kv_headn) * lg::kDecodeMaxSplit * nrep * (c.head_dim + 2);
+    if (cudaMalloc(&h->freq, nfreq * 4) != cudaSuccess || cudaMalloc(&h->qg, pd * 4) != cudaSuccess ||
+        cudaMalloc(&h->kg, pd * 4) != cudaSuccess || cudaMalloc(&h->part, part_floats * 4) != cudaSuccess ||
+        cudaMalloc(&h->counters, c.kv_headn * sizeof(int)) != cudaSuccess)
+        return bail(fail(LIGGUF_ATTN_ENOMEM, "handle buffers"));
+    if (cudaMemcpy(h->freq, freq.data(), nfreq * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemset(h->counters, 0, c.kv_headn * sizeof(int)) != cudaSuccess)
+        return bail(fail(LIGGUF_ATTN_ECUDA, "handle initialisation copies"));
+    if (cudaHostAlloc(&h->h_err, 64, cudaHostAllocMapped) != cudaSuccess ||
+        cudaHostGetDevicePointer(reinterpret_cast<void**>(&h->d_err), h->h_err, 0) != cudaSuccess)
+        return bail(fail(LIGGUF_ATTN_ENOMEM, "mapped error word"));
+    *h->h_err = 0;
+    const int tp = decode_tile_rows(c.kv_type, c.head_dim);
+    if ((rc = make_cache_tmap(&h->tm_k, h->kc, h, tp)) != LIGGUF_ATTN_OK) return bail(rc);
+    if ((rc = make_cache_tmap(&h->tm_v, h->vc, h, tp)) != LIGGUF_ATTN_OK) return bail(rc);
+    *out = h;
+    return LIGGUF_ATTN_OK;
+}
+
+int ligguf_cuda_attn_set_qk_norm(ligguf_attn* h, int layer, const float* q_gamma, const float* k_gamma) {
+    if (!h || !q_gamma || !k_gamma) return fail(LIGGUF_ATTN_EINVAL, "null argument");
+    if (layer < 0 || layer >= h->cfg.n_layers) return fail(LIGGUF_ATTN_EINVAL, "layer %d out of range", layer);
+    DeviceGuard dg(h->cfg.device);
+    const size_t D = h->cfg.head_dim;
+    LG_CUDA(cudaMemcpy(h->qg + layer * D, q_gamma, D * 4, cudaMemcpyHostToDevice));
+    LG_CUDA(cudaMemcpy(h->kg + layer * D, k_gamma, D * 4, cudaMemcpyHostToDevice));
+    h->norm_set[layer] = 1;
+    return LIGGUF_ATTN_OK;
+}
+
+int ligguf_cuda_attn_decode_async(ligguf_attn* h, int layer, int pos, const float* d_q, const float* d_k,
+                                  const float* d_v, float* d_out, void* stream) {
+    if (!h) return fail(LIGGUF_ATTN_EINVAL, "null handle");
+    DeviceGuard dg(h->cfg.device);
+    return decode_enqueue(h, layer, pos, d_q, d_k, d_v, d_out, static_cast<cudaStream_t>(stream), false);
+}
+
+int ligguf_cuda_attn_decode(ligguf_attn* h, int layer, int pos, const float* q, const float* k, const float* v,
+                            float* out) {
+    if (!h) return fail(LIGGUF_ATTN_EINVAL, "null handle");
+    if (!q || !k || !v || !out) return fail(LIGGUF_ATTN_EINVAL, "null tensor pointer");
+    DeviceGuard dg(h->cfg.device);
+    const size_t nq = size_t(h->q_headn) * h->cfg.head_dim, nk = h->kv_dim;
+    int rc = grow(&h->d_stage, &h->stage_floats, 2 * nq + 2 * nk);
+    if (rc) return rc;
+    float* dq = h->d_stage;
+    float* dk = dq + nq;
+    float* dv = dk + nk;
+    float* dout = dv + nk;
+    LG_CUDA(cudaMemcpyAsync(dq, q, nq * 4, cudaMemcpyHostToDevice, h->stream));
+    LG_CUDA(cudaMemcpyAsync(dk, k, nk * 4, cudaMemcpyHostToDevice, h->stream));
+    LG_CUDA(cudaMemcpyAsync(dv, v, nk * 4, cudaMemcpyHostToDevice, h->stream));
+    if ((rc = decode_enqueue(h, layer, pos, dq, dk, dv, dout, h->stream, false))) return rc;
+    LG_CUDA(cudaMemcpyAsync(out, dout, nq * 4, cudaMemcpyDeviceToHost, h->stream));
+    LG_CUDA(cudaStreamSynchronize(h->stream));
+    return check_err_word(h->h_err, h->counters, h->kv_dim / h->cfg.head_dim);
+}
+
+int ligguf_cuda_attn_prefill_async(ligguf_attn* h, int layer, int pos0, int n, const float* d_q, const float* d_k,
+                                   const float* d_v, float* d_out, int mode, void* stream) {
+    if (!h) return fail(LIGGUF_ATTN_EINVAL, "null handle");
+    DeviceGuard dg(h->cfg.device);
+    return prefill_enqueue(h, layer, pos0, n, d_q, d_k, d_v, d_out, mode, static_cast<cudaStream_t>(stream));
+}
+
+int ligguf_cuda_attn_prefill(ligguf_attn* h, int layer, int pos0, int n, const float* q, const float* k,
+                             const float* v, float* out, int mode) {
+    if (!h) return fail(LIGGUF_ATTN_EINVAL, "null handle");
+    if (!q || !k || !v || !out || n < 1) return fail(LIGGUF_ATTN_EINVAL, "null tensor pointer or n < 1");
+    DeviceGuard dg(h->cfg.device);
+    const size_t nq = size_t(n) * h->q_headn * h->cfg.head_dim, nk = size_t(n) * h->kv_dim;
+    int rc = grow(&h->d_stage, &h->stage_floats, 2 * nq + 2 * nk);
+    if (rc) return rc;
+    float* dq = h->d_stage;
+    float* dk = dq + nq;
+    float* dv = dk + nk;
+    float* dout = dv + nk;
+    LG_CUDA(cudaMemcpyAsync(dq, q, nq * 4, cudaMemcpyHostToDevice, h->stream));
+    LG_CUDA(cudaMemcpyAsync(dk, k, nk * 4, cudaMemcpyHostToDevice, h->stream));
+    LG_CUDA(cudaMemcpyAsync(dv, v, nk * 4, cudaMemcpyHostToDevice, h->stream));
+    if ((rc = prefill_enqueue(h, layer, pos0, n, dq, dk, dv, dout, mode, h->stream))) return rc;
+    LG_CUDA(cudaMemcpyAsync(out, dout, nq * 4, cudaMemcpyDeviceToHost, h->stream));
+    LG_CUDA(cudaStreamSynchronize(h->stream));
+    return check_err_word(h->h_err, h->counters, h->kv_dim / h->cfg.head_dim);
+}
+
+int ligguf_cuda_attn_kv_download(ligguf_attn* h, int layer, int pos0, int n, void* host_k, void* host_v) {
+    if (!h || !host_k || !host_v) return fail(LIGGUF_ATTN_EINVAL, "null argument");
+    if (layer < 0 || layer >= h->cfg.n_layers || pos0 < 0 || n < 0 || pos0 + n > h->cfg.n_context)
+        return fail(LIGGUF_ATTN_EINVAL, "layer %d rows [%d, %d) out of range", layer, pos0, pos0 + n);
+    DeviceGuard dg(h->cfg.device);
+    const size_t off = (size_t(layer) * h->layer_elems + size_t(pos0) * h->kv_dim) * h->es;
+    const size_t bytes = size_t(n) * h->kv_dim * h->es;
+    LG_CUDA(cudaStreamSynchronize(h->stream));
+    LG_CUDA(cudaMemcpy(host_k, static_cast<char*>(h->kc) + off, bytes, cudaMemcpyDeviceToHost));
+    LG_CUDA(cudaMemcpy(host_v, static_cast<char*>(h->vc) + off, bytes, cudaMemcpyDeviceToHost));
+    return LIGGUF_ATTN_OK;
+}
+
+int ligguf_cuda_attn_kv_upload(ligguf_attn* h, int layer, int pos0, int n, const void* host_k, const void* host_v) {
+    if (!h || !host_k || !host_v) return fail(LIGGUF_ATTN_EINVAL, "null argument");
+    if (layer < 0 || layer >= h->cfg.n_layers || pos0 < 0 || n < 0 || pos0 + n > h->cfg.n_context)
+        return fail(LIGGUF_ATTN_EINVAL, "layer %d rows [%d, %d) out of range", layer, pos0, pos0 + n);
+    DeviceGuard dg(h->cfg.device);
+    const size_t off = (size_t(layer) * h->layer_elems + size_t(pos0) * h->kv_dim) * h->es;
+    const size_t bytes = size_t(n) * h->kv_dim * h->es;
+    LG_CUDA(cudaStreamSynchronize(h->stream));
+    LG_CUDA(cudaMemcpy(static_cast<char*>(h->kc) + off, host_k, bytes, cudaMemcpyHostToDevice));
+    LG_CUDA(cudaMemcpy(static_cast<char*>(h->vc) + off, host_v, bytes, cudaMemcpyHostToDevice));
+    return LIGGUF_ATTN_OK;
+}
+
+int ligguf_cuda_attn_kv_synth(ligguf_attn* h, int layer0, int n_layers, int pos0, int n, uint64_t seed,
+                              float scale) {
+    if (!h) return fail(LIGGUF_ATTN_EINVAL, "null handle");
+    if (layer0 < 0 || n_layers < 0 || layer0 + n_layers > h->cfg.n_layers || pos0 < 0 || n < 0 ||
+        pos0 + n > h->cfg.n_context)
+        return fail(LIGGUF_ATTN_EINVAL, "synthetic fill range out of bounds");
+    DeviceGuard dg(h->cfg.device);
+    const float mul = synth_mul(scale);
+    const int kv_off = h->cfg.kv_head0 * h->cfg.head_dim;
+    const size_t total = size_t(n) * h->kv_dim;
+    const int blocks = std::min(8 * h->num_sms, std::max(1, ceil_div(total, 256)));
+    for (int l = layer0; l < layer0 + n_layers && n > 0; ++l) {
+        for (int tensor = LIGGUF_SYNTH_K; tensor <= LIGGUF_SYNTH_V; ++tensor) {
+            void* base = static_cast<char*>(tensor == LIGGUF_SYNTH_K ? h->kc : h->vc) + size_t(l) * h->layer_elems * h->es;
+            const uint64_t sb = lg::synth_base(seed, (uint64_t(tensor) << 32) | uint32_t(l));
+            switch (h->cfg.kv_type) {
+                case LIGGUF_KV_F32:
+                    kv_synth_kernel<float><<<blocks, 256, 0, h->stream>>>(static_cast<float*>(base), h->kv_dim,
+                                                                          h->kv_dim_full, kv_off, pos0, n, sb, mul);
+                    break;
+                case LIGGUF_KV_F16:
+                    kv_synth_kernel<__half><<<blocks, 256, 0, h->stream>>>(static_cast<__half*>(base), h->kv_dim,
+                                                                           h->kv_dim_full, kv_off, pos0, n, sb, mul);
+                    break;
+                default:
+                    kv_synth_kernel<__nv_bfloat16><<<blocks, 256, 0, h->stream>>>(
+                        static_cast<__nv_bfloat16*>(base), h->kv_dim, h->kv_dim_full, kv_off, pos0, n, sb, mul);
+                    break;
+            }
+            LG_CUDA(cudaGetLastError());
+        }
+    }
+    LG_CUDA(cudaStreamSynchronize(h->stream));
+    return LIGGUF_ATTN_OK;
+}
+
+int ligguf_cuda_attn_sync(ligguf_attn* h) {
+    if (!h) return fail(LIGGUF_ATTN_EINVAL, "null handle");
+    DeviceGuard dg(h->cfg.device);
+    LG_CUDA(cudaStreamSynchronize(h->stream));
+    LG_CUDA(cudaDeviceSynchronize());
+    return check_err_word(h->h_err, h->counters, h->kv_dim / h->cfg.head_dim);
+}
+
+// ---------------------------------------------------------------------------- SARA gather
+int ligguf_cuda_attn_gather_ipc_handle(ligguf_attn* h, void* handle_out, size_t handle_size) {
+    if (!h || !handle_out) return fail(LIGGUF_ATTN_EINVAL, "null argument");
+    if (handle_size < sizeof(cudaIpcMemHandle_t))
+        return fail(LIGGUF_ATTN_EINVAL, "handle buffer of %zu bytes (need %zu)", handle_size, sizeof(cudaIpcMemHandle_t));
+    DeviceGuard dg(h->cfg.device);
+    if (!h->gbuf) {
+        h->gbuf_bytes = 2 * size_t(h->cfg.n_heads) * h->cfg.head_dim * 4 + 2 * size_t(h->cfg.n_kv_heads) * 4;
+        if (cudaMalloc(reinterpret_cast<void**>(&h->gbuf), h->gbuf_bytes) != cudaSuccess)
+            return fail(LIGGUF_ATTN_ENOMEM, "gather buffer");
+        LG_CUDA(cudaMemset(h->gbuf, 0, h->gbuf_bytes));
+    }
+    cudaIpcMemHandle_t hd;
+    LG_CUDA(cudaIpcGetMemHandle(&hd, h->gbuf));
+    memcpy(handle_out, &hd, sizeof(hd));
+    return LIGGUF_ATTN_OK;
+}
+
+int ligguf_cuda_attn_gather_open(ligguf_attn* h, int nranks, int rank, const void* handles, size_t handle_size) {
+    if (!h || !handles) return fail(LIGGUF_ATTN_EINVAL, "null argument");
+    if (handle_size < sizeof(cudaIpcMemHandle_t)) return fail(LIGGUF_ATTN_EINVAL, "handle stride %zu", handle_size);
+    if (nranks < 1 || rank < 0 || rank >= nranks) return fail(LIGGUF_ATTN_EINVAL, "rank %d of %d", rank, nranks);
+    if (!h->gbuf) return fail(LIGGUF_ATTN_ESTATE, "call ligguf_cuda_attn_gather_ipc_handle first");
+    if (h->g_nranks) return fail(LIGGUF_ATTN_ESTATE, "gather already open");
+    DeviceGuard dg(h->cfg.device);
+    const size_t vec = size_t(h->cfg.n_heads) * h->cfg.head_dim;
+    std::vector<float*> outs(2 * nranks);
+    std::vector<int*> flags(2 * nranks);
+    h->g_opened.assign(nranks, nullptr);
+    for (int r = 0; r < nranks; ++r) {
+        char* base;
+        if (r == rank) {
+            base = reinterpret_cast<char*>(h->gbuf);
+        } else {
+            cudaIpcMemHandle_t hd;
+            memcpy(&hd, static_cast<const char*>(handles) + size_t(r) * handle_size, sizeof(hd));
+            void* p = nullptr;
+            LG_CUDA(cudaIpcOpenMemHandle(&p, hd, cudaIpcMemLazyEnablePeerAccess));
+            h->g_opened[r] = p;
+            base = static_cast<char*>(p);
+        }
+        for (int slot = 0; slot < 2; ++slot) {
+            outs[slot * nranks + r] = reinterpret_cast<float*>(base) + slot * vec;
+            flags[slot * nranks + r] = reinterpret_cast<int*>(base + 2 * vec * 4) + slot * h->cfg.n_kv_heads;
+        }
+    }
+    LG_CUDA(cudaMalloc(reinterpret_cast<void**>(&h->d_peer_out), outs.size() * sizeof(float*)));
+    LG_CUDA(cudaMalloc(reinterpret_cast<void**>(&h->d_peer_flag), flags.size() * sizeof(int*)));
+    LG_CUDA(cudaMemcpy(h->d_peer_out, outs.data(), outs.size() * sizeof(float*), cudaMemcpyHostToDevice));
+    LG_CUDA(cudaMemcpy(h->d_peer_flag, flags.data(), flags.size() * sizeof(int*), cudaMemcpyHostToDevice));
+    h->g_nranks = nranks;
+    h->g_rank = rank;
+    h->g_epoch = 0;
+    return LIGGUF_ATTN_OK;
+}
+
+int ligguf_cuda_attn_decode_gather_async(ligguf_attn* h, int layer, int pos, const float* d_q, const float* d_k,
+                                         const float* d_v, void* stream) {
+    if (!h) return fail(LIGGUF_ATTN_EINVAL, "null handle");
+    if (!h->g_nranks) return fail(LIGGUF_ATTN_ESTATE, "gather not open");
+    DeviceGuard dg(h->cfg.device);
+    ++h->g_epoch;
+    const int rc = decode_enqueue(h, layer, pos, d_q, d_k, d_v, nullptr, static_cast<cudaStream_t>(stream), true);
+    if (rc) --h->g_epoch;
+    return rc;
+}
+
+int ligguf_cuda_attn_gather_wait_async(ligguf_attn* h, int layer, float* d_out, void* stream) {
+    if (!h || !d_out) return fail(LIGGUF_ATTN_EINVAL, "null argument");
+    if (!h->g_nranks || h->g_epoch == 0) return fail(LIGGUF_ATTN_ESTATE, "no gathered decode in flight");
+    if (layer < 0 || layer >= h->cfg.n_layers) return fail(LIGGUF_ATTN_EINVAL, "layer %d out of range", layer);
+    DeviceGuard dg(h->cfg.device);
+    const int slot = h->g_epoch & 1;
+    const size_t vec = size_t(h->cfg.n_heads) * h->cfg.head_dim;
+    const float* gathered = h->gbuf + slot * vec;
+    const int* flags = reinterpret_cast<const int*>(reinterpret_cast<const char*>(h->gbuf) + 2 * vec * 4) +
+                       slot * h->cfg.n_kv_heads;
+    gather_wait_kernel<<<1, 256, 0, static_cast<cudaStream_t>(stream)>>>(gathered, flags, h->cfg.n_kv_heads,
+                                                                         h->g_epoch, d_out, int(vec), h->d_err);
+    LG_CUDA(cudaGetLastError());
+    return LIGGUF_ATTN_OK;
+}
+
+// ---------------------------------------------------------------------------- BERT
+int ligguf_cuda_bert_free(ligguf_bert_attn* b) {
+    if (!b) return LIGGUF_ATTN_OK;
+    DeviceGuard dg(b->device);
+    if (b->stream) cudaStreamSynchronize(b->stream);
+    if (b->d_lens) cudaFree(b->d_lens);
+    if (b->d_buf) cudaFree(b->d_buf);
+    if (b->bf) cudaFree(b->bf);
+    if (b->h_err) cudaFreeHost(b->h_err);
+    if (b->stream) cudaStreamDestroy(b->stream);
+    delete b;
+    return LIGGUF_ATTN_OK;
+}
+
+int ligguf_cuda_bert_init(int n_heads, int head_dim, int max_batch, int max_len, int device, ligguf_bert_attn** out) {
+    if (!out) return fail(LIGGUF_ATTN_EINVAL, "null out");
+    *out = nullptr;
+    if (n_heads < 1 || max_batch < 1 || max_len < 1) return fail(LIGGUF_ATTN_EINVAL, "non-positive size");
+    if (head_dim != 64 && head_dim != 128) return fail(LIGGUF_ATTN_EUNSUPPORTED, "head_dim %d", head_dim);
+    int ndev = 0;
+    LG_CUDA(cudaGetDeviceCount(&ndev));
+    if (device < 0 || device >= ndev) return fail(LIGGUF_ATTN_EINVAL, "device %d of %d", device, ndev);
+    DeviceGuard dg(device);
+    ligguf_bert_attn* b = new ligguf_bert_attn();
+    b->n_heads = n_heads;
+    b->head_dim = head_dim;
+    b->max_batch = max_batch;
+    b->max_len = max_len;
+    b->device = device;
+    const size_t elems = size_t(max_batch) * max_len * n_heads * head_dim;
+    if (cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMalloc(&b->d_lens, max_batch * sizeof(int)) != cudaSuccess ||
+        cudaHostAlloc(&b->h_err, 64, cudaHostAllocMapped) != cudaSuccess ||
+        cudaHostGetDevicePointer(reinterpret_cast<void**>(&b->d_err), b->h_err, 0) != cudaSuccess) {
+        ligguf_cuda_bert_free(b);
+        return fail(LIGGUF_ATTN_ENOMEM, "BERT handle buffers");
+    }
+    (void)elems;
+    *b->h_err = 0;
+    *out = b;
+    return LIGGUF_ATTN_OK;
+}
+
+int ligguf_cuda_bert_attn_async(ligguf_bert_attn* b, int batch, int max_len, const int* d_lens, const float* d_q,
+                                const float* d_k, const float* d_v, float* d_out, int mode, void* stream) {
+    if (!b || !d_lens || !d_q || !d_k || !d_v || !d_out) return fail(LIGGUF_ATTN_EINVAL, "null argument");
+    if (batch < 1 || batch > b->max_batch || max_len < 1 || max_len > b->max_len)
+        return fail(LIGGUF_ATTN_EINVAL, "batch %d / max_len %d beyond the handle's %d / %d", batch, max_len,
+                    b->max_batch, b->max_len);
+    if (mode != LIGGUF_MODE_SIMT && mode != LIGGUF_MODE_TC) return fail(LIGGUF_ATTN_EINVAL, "mode %d", mode);
+    DeviceGuard dg(b->device);
+    const int D = b->head_dim, E = b->n_heads * D;
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (mode == LIGGUF_MODE_SIMT) {
+        lg::FlashArgs f = {};
+        f.q = d_q;
+        f.q_row = E;
+        f.q_batch = static_cast<long long>(max_len) * E;
+        f.k = d_k;
+        f.v = d_v;
+        f.kv_row = E;
+        f.kv_batch = static_cast<long long>(max_len) * E;
+        f.out = d_out;
+        f.o_row = E;
+        f.o_batch = static_cast<long long>(max_len) * E;
+        f.lens = d_lens;
+        f.n_q = max_len;
+        f.kv_len = max_len;
+        f.causal = 0;
+        f.q_pos0 = 0;
+        f.nrep = 1;
+        f.scale_div = 0;
+        f.scale = 1.0f / sqrtf(static_cast<float>(D));  // fast/vdb.cpp:133
+        return launch_flash_simt<float>(f, D, dim3(ceil_div(max_len, lg::kFlashBQ), b->n_heads, batch), st, b->device);
+    }
+    const size_t elems = size_t(batch) * max_len * E;
+    size_t cap = b->bf ? size_t(b->max_batch) * b->max_len * E * 3 : 0;
+    if (!b->bf) {
+        cap = size_t(b->max_batch) * b->max_len * E * 3;
+        if (cudaMalloc(&b->bf, cap * sizeof(__nv_bfloat16)) != cudaSuccess)
+            return fail(LIGGUF_ATTN_ENOMEM, "BERT bf16 operand buffers");
+    }
+    lg::TcArgs t = {};
+    t.q = b->bf;
+    t.k = b->bf + elems;
+    t.v = b->bf + 2 * elems;
+    int threads = 256;
+    const int blocks = std::min(1184, std::max(1, ceil_div(elems, threads)));
+    lg::to_bf16_kernel<<<blocks, threads, 0, st>>>(d_q, b->bf, elems);
+    lg::to_bf16_kernel<<<blocks, threads, 0, st>>>(d_k, b->bf + elems, elems);
+    lg::to_bf16_kernel<<<blocks, threads, 0, st>>>(d_v, b->bf + 2 * elems, elems);
+    LG_CUDA(cudaGetLastError());
+    t.out = d_out;
+    t.q_rows = batch * max_len;
+    t.q_heads = b->n_heads;
+    t.kv_rows = batch * max_len;
+    t.kv_heads = b->n_heads;
+    t.batch = batch;
+    t.q_seq = max_len;
+    t.kv_seq = max_len;
+    t.lens = d_lens;
+    t.causal = 0;
+    t.q_pos0 = 0;
+    t.nrep = 1;
+    t.scale_log2 = (1.0f / sqrtf(static_cast<float>(D))) * 1.4426950408889634f;
+    t.err = b->d_err;
+    int nsm = 148;
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, b->device);
+    return lg::launch_flash_tc(t, D, st, b->device, nsm) ? fail(LIGGUF_ATTN_ECUDA, "%s", lg::tc_last_error())
+                                                          : LIGGUF_ATTN_OK;
+}
+
+int ligguf_cuda_bert_attn(ligguf_bert_attn* b, int batch, int max_len, const int* lens, const float* q,
+                          const float* k, const float* v, float* out, int mode) {
+    if (!b || !lens || !q || !k || !v || !out) return fail(LIGGUF_ATTN_EINVAL, "null argument");
+    if (batch < 1 || batch > b->max_batch || max_len < 1 || max_len > b->max_len)
+        return fail(LIGGUF_ATTN_EINVAL, "batch %d / max_len %d beyond the handle's %d / %d", batch, max_len,
+                    b->max_batch, b->max_len);
+    for (int i = 0; i < batch; ++i)
+        if (lens[i] < 0 || lens[i] > max_len) return fail(LIGGUF_ATTN_EINVAL, "lens[%d] = %d", i, lens[i]);
+    DeviceGuard dg(b->device);
+    const size_t elems = size_t(batch) * max_len * b->n_heads * b->head_dim;
+    if (!b->d_buf) {
+        const size_t cap = size_t(b->max_batch) * b->max_len * b->n_heads * b->head_dim * 4;
+        if (cudaMalloc(&b->d_buf, cap * sizeof(float)) != cudaSuccess)
+            return fail(LIGGUF_ATTN_ENOMEM, "BERT staging buffers");
+    }
+    float* dq = b->d_buf;
+    float* dk = dq + elems;
+    float* dv = dk + elems;
+    float* dout = dv + elems;
+    LG_CUDA(cudaMemcpyAsync(b->d_lens, lens, batch * sizeof(int), cudaMemcpyHostToDevice, b->stream));
+    LG_CUDA(cudaMemcpyAsync(dq, q, elems * 4, cudaMemcpyHostToDevice, b->stream));
+    LG_CUDA(cudaMemcpyAsync(dk, k, elems * 4, cudaMemcpyHostToDevice, b->stream));
+    LG_CUDA(cudaMemcpyAsync(dv, v, elems * 4, cudaMemcpyHostToDevice, b->stream));
+    int rc = ligguf_cuda_bert_attn_async(b, batch, max_len, b->d_lens, dq, dk, dv, dout, mode, b->stream);
+    if (rc) return rc;
+    LG_CUDA(cudaMemcpyAsync(out, dout, elems * 4, cudaMemcpyDeviceToHost, b->stream));
+    LG_CUDA(cudaStreamSynchronize(b->stream));
+    return check_err_word(b->h_err, nullptr, 0);
+}
+
+// ---------------------------------------------------------------------------- synth
+int ligguf_cuda_synth_fill(void* d_dst, int dtype, size_t n, uint64_t seed, uint64_t stream_id, uint64_t idx0,
+                           float scale, float add, void* stream) {
+    if (!d_dst && n) return fail(LIGGUF_ATTN_EINVAL, "null destination");
+    if (dtype < LIGGUF_KV_F32 || dtype > LIGGUF_KV_BF16) return fail(LIGGUF_ATTN_EINVAL, "dtype %d", dtype);
+    if (!n) return LIGGUF_ATTN_OK;
+    const uint64_t base = lg::synth_base(seed, stream_id);
+    const float mul = synth_mul(scale);
+    const int blocks = static_cast<int>(std::min<size_t>(4096, (n + 255) / 256));
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    switch (dtype) {
+        case LIGGUF_KV_F32:
+            synth_fill_kernel<float><<<blocks, 256, 0, st>>>(static_cast<float*>(d_dst), n, base, idx0, mul, add);
+            break;
+        case LIGGUF_KV_F16:
+            synth_fill_kernel<__half><<<blocks, 256, 0, st>>>(static_cast<__half*>(d_dst), n, base, idx0, mul, add);
+            break;
+        default:
+            synth_fill_kernel<__nv_bfloat16>
+                <<<blocks, 256, 0, st>>>(static_cast<__nv_bfloat16*>(d_dst), n, base, idx0, mul, add);
+            break;
+    }
+    LG_CUDA(cudaGetLastError());
+    return LIGGUF_ATTN_OK;
+}
+
+}  // extern "C"

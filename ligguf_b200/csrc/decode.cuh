@@ -1,0 +1,538 @@
+// decode.cuh - single-token decode attention over the HBM-resident KV cache (split-KV
+// flash-decoding), one launch per layer.
+//
+// Replaces fast/ligguf_fast_qk.cpp:42-105 (FAST, fp16 cache) and cpp/ligguf.cpp:674-718 /
+// cpp/ligguf_distrib.cpp:724-747 (fp32 cache):
+//   q, k <- RMSNorm per head (Qwen3, fast/ligguf_fast_qk.cpp:42-51; fast/lil_math.cpp:931-937)
+//   q, k <- RoPE on adjacent pairs at `pos` (fast/lil_math.cpp:901-920)
+//   cache[pos] <- k, v (fast/ligguf_fast_qk.cpp:57-62)
+//   for each q head h (kv head h/nrep): s_t = q.k_t * scale, softmax over t in [0,pos],
+//   out_h = sum_t p_t v_t, with t == pos taken from the fp32 k, v (:77-78, :98-99).
+//
+// Grid (n_split, kv_headn).  CTA (split, g) owns KV head g and a contiguous run of 16 KB tiles of
+// cached positions [0, pos); it computes all nrep q heads of the group so each K/V byte is read
+// from HBM once.  Warp 8 is the producer: one lane streams K and V tiles of the run with TMA into a
+// 3-stage shared-memory ring.  Warps 0..7 consume: scores (each lane dots 16 B of a row with
+// the nrep q vectors, a transposed butterfly reduces nrep*4 dot products with one shuffle per
+// result), an online softmax per tile, P.V accumulation in registers.  The last CTA of a KV head
+// (atomic ticket) merges the splits' (max, sum, o) partials and writes the output, so the whole
+// layer is one launch.  The CTA holding position pos-1 also folds in the current token.
+//
+// Every wait is bounded (kWaitLimitNs): a wait that gives up raises a shared abort flag, writes the
+// error word and lets the kernel finish without writing its output.
+#pragma once
+
+#include "common.cuh"
+
+namespace lg {
+
+constexpr int kDecodeConsumerWarps = 8;
+constexpr int kDecodeConsumers = kDecodeConsumerWarps * 32;
+constexpr int kDecodeThreads = kDecodeConsumers + 32;
+constexpr int kDecodeStages = 3;
+constexpr int kDecodeTileBytes = 16384;
+constexpr int kDecodeMaxSplit = 1024;
+
+struct DecodeArgs {
+    const float* q;     // [q_headn][D] raw q of this layer
+    const float* k;     // [kv_headn][D] raw k
+    const float* v;     // [kv_headn][D] raw v
+    const float* qg;    // [D] q norm weight (qk_norm) or null
+    const float* kg;    // [D]
+    const float* freq;  // RoPE inverse frequencies
+    void* kc;           // this layer's K cache block [n_context][kv_dim]
+    void* vc;
+    float* out;         // [q_headn][D]
+    float* part;        // [kv_headn][kDecodeMaxSplit][nrep*(D+2)] split partials
+    int* counters;      // [kv_headn] tickets, zero between launches
+    int* err;           // error word (mapped host memory)
+    float* const* peer_out;  // multi-GPU gather: [nranks] gather buffers (or null)
+    int* const* peer_flag;   // [nranks] flag arrays [nranks*kv_headn]
+    int nranks;
+    int rank;
+    int q_off;          // element offset of this shard's heads in the gathered vector
+    int kv_head0;       // global index of this shard's first KV head (gather flag slot)
+    int flag_value;
+    int row0;           // tensor-map row of (this layer, position 0) = layer * n_context
+    int pos;
+    int n_tiles;        // tiles covering [0, pos)
+    int tiles_per_split;
+    int n_split;
+    int kv_dim;
+    int rope_pairs;
+    int qk_norm;
+    int scale_div;
+    float scale;        // multiplier (FAST) or divisor (cpp/SARA engines)
+    float eps;
+};
+
+template <typename KV, int D>
+struct DecodeShape {
+    static constexpr int kRowBytes = D * static_cast<int>(sizeof(KV));
+    static constexpr int kTileRows = kDecodeTileBytes / kRowBytes;
+    static constexpr int kLanesPerRow = kRowBytes / 16;
+    static constexpr int kRowsPerInstr = 32 / kLanesPerRow;
+    static constexpr int kEpl = 16 / static_cast<int>(sizeof(KV));
+    static constexpr int kInstr = kTileRows / (kDecodeConsumerWarps * kRowsPerInstr);
+    static constexpr int kLog2Lpr = kLanesPerRow == 32 ? 5 : kLanesPerRow == 16 ? 4 : 3;
+    static_assert(kRowBytes >= 128 && kRowBytes <= 512, "one head row must be 128..512 bytes");
+    static_assert(kInstr == 4, "tile mapping expects 4 row loads per warp per tile");
+};
+
+template <typename KV, int D, int NREP>
+struct DecodeSmem {
+    using Sh = DecodeShape<KV, D>;
+    static constexpr size_t kStageBytes = 2 * kDecodeTileBytes;  // K tile + V tile
+    static constexpr size_t kTilesBytes = kDecodeStages * kStageBytes;
+    static constexpr size_t kScoreOff = kTilesBytes;
+    static constexpr size_t kScoreBytes = 2 * NREP * Sh::kTileRows * 4;
+    static constexpr size_t kQOff = kScoreOff + kScoreBytes;
+    static constexpr size_t kOOff = kQOff + NREP * D * 4;
+    static constexpr size_t kKnOff = kOOff + NREP * D * 4;
+    static constexpr size_t kVnOff = kKnOff + D * 4;
+    static constexpr size_t kMiscOff = kVnOff + D * 4;  // corr, m, l [NREP] + 4 ints
+    static constexpr size_t kBarOff = (kMiscOff + 3 * NREP * 4 + 16 + 7) & ~size_t(7);
+    static constexpr size_t kTotal = kBarOff + 3 * kDecodeStages * 8;
+    static_assert(kDecodeConsumerWarps * NREP * D * 4 <= kTilesBytes, "reduction buffer alias");
+    static_assert(kDecodeMaxSplit * NREP * 4 <= kTilesBytes, "combine weights alias");
+};
+
+// One warp: optional RMSNorm then RoPE of one head (D floats) from global `src` into `dst`.
+// Lane owns the adjacent pairs m = lane + 32u, i.e. elements (2m, 2m+1).
+template <int D>
+__device__ __forceinline__ void norm_rope_head(const float* __restrict__ src,
+                                               const float* __restrict__ gamma, int norm,
+                                               float eps, const float* __restrict__ freq,
+                                               int rope_pairs, int pos, float* dst, int lane) {
+    constexpr int kPairs = D / 64;
+    float2 x[kPairs];
+#pragma unroll
+    for (int u = 0; u < kPairs; ++u) x[u] = reinterpret_cast<const float2*>(src)[lane + 32 * u];
+    if (norm) {
+        float ss = 0.f;
+#pragma unroll
+        for (int u = 0; u < kPairs; ++u) {
+            ss = fmaf(x[u].x, x[u].x, ss);
+            ss = fmaf(x[u].y, x[u].y, ss);
+        }
+        ss = warp_sum(ss);
+        const float rs = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
+#pragma unroll
+        for (int u = 0; u < kPairs; ++u) {
+            const int m = lane + 32 * u;
+            x[u].x = (x[u].x * rs) * gamma[2 * m];
+            x[u].y = (x[u].y * rs) * gamma[2 * m + 1];
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < kPairs; ++u) {
+        const int m = lane + 32 * u;
+        if (m < rope_pairs) {
+            float sn, cs;
+            sincosf(static_cast<float>(pos) * freq[m], &sn, &cs);
+            const float x0 = x[u].x, x1 = x[u].y;
+            x[u].x = x0 * cs - x1 * sn;
+            x[u].y = x0 * sn + x1 * cs;
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < kPairs; ++u) reinterpret_cast<float2*>(dst)[lane + 32 * u] = x[u];
+}
+
+// Sums V per-lane values over the 2^S lanes that share the upper lane bits, leaving each lane
+// with max(1, V >> S) sums: lane j (low S bits) holds value indices [j*VF, j*VF+VF) when V >= 2^S,
+// else index j / (2^S / V).  One shuffle per produced sum instead of S per sum.
+template <int V, int S>
+__device__ __forceinline__ void transposed_reduce(float (&x)[V], int lane) {
+#pragma unroll
+    for (int k = 0; k < S; ++k) {
+        const int o = 1 << (S - 1 - k);
+        const int n = V >> k;
+        if (n >= 2) {
+            const bool upper = (lane & o) != 0;
+#pragma unroll
+            for (int t = 0; t < V / 2; ++t) {
+                if (t < n / 2) {
+                    const float send = upper ? x[t] : x[t + n / 2];
+                    const float keep = upper ? x[t + n / 2] : x[t];
+                    x[t] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+                }
+            }
+        } else {
+            x[0] += __shfl_xor_sync(0xffffffffu, x[0], o);
+        }
+    }
+}
+
+template <typename KV, int D, int NREP>
+__global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kEpl > 32) ? 1 : 2)
+    decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                  const DecodeArgs a) {
+    using Sh = DecodeShape<KV, D>;
+    using Sm = DecodeSmem<KV, D, NREP>;
+    constexpr int TP = Sh::kTileRows;
+    constexpr int LPR = Sh::kLanesPerRow;
+    constexpr int RPI = Sh::kRowsPerInstr;
+    constexpr int EPL = Sh::kEpl;
+    constexpr int NI = Sh::kInstr;
+    constexpr int RB = Sh::kRowBytes;
+    constexpr int S = Sh::kLog2Lpr;
+    constexpr int NV = NI * NREP;
+
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint8_t* tiles = smem;
+    float* sc = reinterpret_cast<float*>(smem + Sm::kScoreOff);  // [2][NREP][TP]
+    float* q_s = reinterpret_cast<float*>(smem + Sm::kQOff);     // [NREP][D]
+    float* o_s = reinterpret_cast<float*>(smem + Sm::kOOff);     // [NREP][D]
+    float* kn_s = reinterpret_cast<float*>(smem + Sm::kKnOff);   // current token k (normed, roped)
+    float* vn_s = reinterpret_cast<float*>(smem + Sm::kVnOff);   // current token v
+    float* corr_s = reinterpret_cast<float*>(smem + Sm::kMiscOff);
+    float* m_s = corr_s + NREP;
+    float* l_s = m_s + NREP;
+    volatile int* abort_s = reinterpret_cast<volatile int*>(l_s + NREP);
+    volatile int* last_s = abort_s + 1;
+    volatile int* stop_s = abort_s + 2;
+    uint64_t* full_k = reinterpret_cast<uint64_t*>(smem + Sm::kBarOff);
+    uint64_t* full_v = full_k + kDecodeStages;
+    uint64_t* empty = full_v + kDecodeStages;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int split = blockIdx.x, g = blockIdx.y;
+    const uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
+    const int tile0 = split * a.tiles_per_split;
+    const int tile1 = min(tile0 + a.tiles_per_split, a.n_tiles);
+    const int my_tiles = max(0, tile1 - tile0);
+    const int t_end = min(tile1 * TP, a.pos);
+    const bool owner = split == a.n_split - 1;
+
+    if (tid == 0) {
+#pragma unroll
+        for (int s = 0; s < kDecodeStages; ++s) {
+            mbar_init(&full_k[s], 1);
+            mbar_init(&full_v[s], 1);
+            mbar_init(&empty[s], kDecodeConsumerWarps);
+        }
+        *abort_s = 0;
+        *last_s = 0;
+        *stop_s = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    // ------------------------------------------------------------------ producer warp
+    if (warp == kDecodeConsumerWarps) {
+        if (lane == 0 && my_tiles > 0) {
+            int issued = 0;
+            for (int it = 0; it < my_tiles; ++it) {
+                const int s = it % kDecodeStages;
+                if (it >= kDecodeStages &&
+                    !mbar_wait_bounded(&empty[s], ((it / kDecodeStages) - 1) & 1, deadline, abort_s)) {
+                    *abort_s = 1;
+                    *reinterpret_cast<volatile int*>(a.err) = KERR_TIMEOUT_EMPTY;
+                    break;
+                }
+                const int row = a.row0 + (tile0 + it) * TP;
+                uint8_t* kdst = tiles + s * Sm::kStageBytes;
+                mbar_arrive_expect_tx(&full_k[s], kDecodeTileBytes);
+                tma_load_3d(kdst, &tm_k, &full_k[s], 0, g, row);
+                mbar_arrive_expect_tx(&full_v[s], kDecodeTileBytes);
+                tma_load_3d(kdst + kDecodeTileBytes, &tm_v, &full_v[s], 0, g, row);
+                ++issued;
+            }
+            // Our copies must land before this CTA may exit: wait for the last ring's worth
+            // (ignoring the abort flag, bounded by a later deadline).
+            const uint64_t drain_deadline = deadline + kWaitLimitNs / 2;
+            for (int it = max(0, issued - kDecodeStages); it < issued; ++it) {
+                const int s = it % kDecodeStages;
+                const uint32_t par = (it / kDecodeStages) & 1;
+                while (!mbar_try_wait(&full_k[s], par) && globaltimer_ns() < drain_deadline) {
+                }
+                while (!mbar_try_wait(&full_v[s], par) && globaltimer_ns() < drain_deadline) {
+                }
+            }
+        }
+        return;
+    }
+
+    // ------------------------------------------------------------------ consumers: prologue
+    {
+        const int njobs = NREP + (owner ? 2 : 0);
+        for (int job = warp; job < njobs; job += kDecodeConsumerWarps) {
+            if (job < NREP) {
+                const int hq = g * NREP + job;
+                norm_rope_head<D>(a.q + static_cast<size_t>(hq) * D, a.qg, a.qk_norm, a.eps, a.freq,
+                                  a.rope_pairs, a.pos, q_s + job * D, lane);
+            } else if (job == NREP) {
+                norm_rope_head<D>(a.k + static_cast<size_t>(g) * D, a.kg, a.qk_norm, a.eps, a.freq,
+                                  a.rope_pairs, a.pos, kn_s, lane);
+            } else {
+                for (int d = lane; d < D; d += 32) vn_s[d] = a.v[static_cast<size_t>(g) * D + d];
+            }
+        }
+    }
+    named_bar_sync(1, kDecodeConsumers);
+    if (owner) {
+        KV* krow = reinterpret_cast<KV*>(a.kc) + static_cast<size_t>(a.pos) * a.kv_dim + g * D;
+        KV* vrow = reinterpret_cast<KV*>(a.vc) + static_cast<size_t>(a.pos) * a.kv_dim + g * D;
+        for (int d = tid; d < D; d += kDecodeConsumers) {
+            krow[d] = KvTraits<KV>::from_float(kn_s[d]);
+            vrow[d] = KvTraits<KV>::from_float(vn_s[d]);
+        }
+    }
+
+    const int r = lane / LPR, j = lane % LPR;
+    float qr[NREP][EPL];
+#pragma unroll
+    for (int h = 0; h < NREP; ++h)
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) qr[h][e] = q_s[h * D + j * EPL + e];
+
+    float acc[NREP][EPL];
+#pragma unroll
+    for (int h = 0; h < NREP; ++h)
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) acc[h][e] = 0.f;
+    float m_run = -INFINITY, l_run = 0.f;  // used by warps < NREP (warp == head)
+    bool ok = true;
+    const bool div = a.scale_div != 0;
+    const float scale = a.scale;
+
+    for (int it = 0; it < my_tiles; ++it) {
+        const int s = it % kDecodeStages;
+        const uint32_t par = (it / kDecodeStages) & 1;
+        float* scb = sc + (it & 1) * NREP * TP;
+        const int tbase = (tile0 + it) * TP;
+        const uint8_t* kt = tiles + s * Sm::kStageBytes;
+        const uint8_t* vt = kt + kDecodeTileBytes;
+
+        if (ok) {
+            ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full_k[s], par, deadline, abort_s));
+            if (!ok && lane == 0) {
+                *abort_s = 1;
+                *reinterpret_cast<volatile int*>(a.err) = KERR_TIMEOUT_FULL;
+            }
+        }
+        if (ok) {
+            float part[NV];
+#pragma unroll
+            for (int i = 0; i < NI; ++i) {
+                const int row = (warp * NI + i) * RPI + r;
+                const uint4 raw = lds128(kt + row * RB + j * 16);
+                float kx[EPL];
+                KvTraits<KV>::unpack(raw, kx);
+#pragma unroll
+                for (int h = 0; h < NREP; ++h) {
+                    float d0 = 0.f;
+#pragma unroll
+                    for (int e = 0; e < EPL; ++e) d0 = fmaf(kx[e], qr[h][e], d0);
+                    part[i * NREP + h] = d0;
+                }
+            }
+            transposed_reduce<NV, S>(part, lane);
+            if constexpr (NV >= (1 << S)) {
+                constexpr int VF = NV >> S;
+#pragma unroll
+                for (int u = 0; u < VF; ++u) {
+                    const int vi = j * VF + u;
+                    const int i = vi / NREP, h = vi % NREP;
+                    const int row = (warp * NI + i) * RPI + r;
+                    const float sv = div ? part[u] / scale : part[u] * scale;
+                    scb[h * TP + row] = (tbase + row < t_end) ? sv : -INFINITY;
+                }
+            } else {
+                constexpr int DUP = (1 << S) / NV;
+                if (j % DUP == 0) {
+                    const int vi = j / DUP;
+                    const int i = vi / NREP, h = vi % NREP;
+                    const int row = (warp * NI + i) * RPI + r;
+                    const float sv = div ? part[0] / scale : part[0] * scale;
+                    scb[h * TP + row] = (tbase + row < t_end) ? sv : -INFINITY;
+                }
+            }
+        }
+        named_bar_sync(1, kDecodeConsumers);
+        if (ok && warp < NREP) {  // online softmax of this tile for head `warp`
+            constexpr int PU = TP / 32;
+            float sv[PU];
+            float mx = -INFINITY;
+#pragma unroll
+            for (int u = 0; u < PU; ++u) {
+                sv[u] = scb[warp * TP + lane + 32 * u];
+                mx = fmaxf(mx, sv[u]);
+            }
+            mx = warp_max(mx);
+            const float m_new = fmaxf(m_run, mx);
+            float corr = 1.f, psum = 0.f;
+            if (m_new == -INFINITY) {
+#pragma unroll
+                for (int u = 0; u < PU; ++u) scb[warp * TP + lane + 32 * u] = 0.f;
+            } else {
+                corr = expf(m_run - m_new);
+#pragma unroll
+                for (int u = 0; u < PU; ++u) {
+                    const float p = expf(sv[u] - m_new);
+                    scb[warp * TP + lane + 32 * u] = p;
+                    psum += p;
+                }
+            }
+            psum = warp_sum(psum);
+            l_run = l_run * corr + psum;
+            m_run = m_new;
+            if (lane == 0) corr_s[warp] = corr;
+        }
+        named_bar_sync(1, kDecodeConsumers);
+        if (ok) {
+            ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full_v[s], par, deadline, abort_s));
+            if (!ok && lane == 0) {
+                *abort_s = 1;
+                *reinterpret_cast<volatile int*>(a.err) = KERR_TIMEOUT_FULL;
+            }
+        }
+        if (ok) {
+#pragma unroll
+            for (int h = 0; h < NREP; ++h) {
+                const float c = corr_s[h];
+#pragma unroll
+                for (int e = 0; e < EPL; ++e) acc[h][e] *= c;
+            }
+#pragma unroll
+            for (int i = 0; i < NI; ++i) {
+                const int row = (warp * NI + i) * RPI + r;
+                const uint4 raw = lds128(vt + row * RB + j * 16);
+                if (tbase + row < t_end) {
+                    float vx[EPL];
+                    KvTraits<KV>::unpack(raw, vx);
+#pragma unroll
+                    for (int h = 0; h < NREP; ++h) {
+                        const float p = scb[h * TP + row];
+#pragma unroll
+                        for (int e = 0; e < EPL; ++e) acc[h][e] = fmaf(p, vx[e], acc[h][e]);
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+
+    // ------------------------------------------------------------------ CTA reduction
+#pragma unroll
+    for (int o = LPR; o < 32; o <<= 1)
+#pragma unroll
+        for (int h = 0; h < NREP; ++h)
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) acc[h][e] += __shfl_xor_sync(0xffffffffu, acc[h][e], o);
+    named_bar_sync(1, kDecodeConsumers);  // every warp is done with the tiles before `red` aliases them
+    float* red = reinterpret_cast<float*>(tiles);
+    if (lane < LPR) {
+#pragma unroll
+        for (int h = 0; h < NREP; ++h)
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) red[(warp * NREP + h) * D + j * EPL + e] = acc[h][e];
+    }
+    if (warp < NREP && lane == 0) {
+        m_s[warp] = m_run;
+        l_s[warp] = l_run;
+    }
+    named_bar_sync(1, kDecodeConsumers);
+    for (int idx = tid; idx < NREP * D; idx += kDecodeConsumers) {
+        float sum = 0.f;
+#pragma unroll
+        for (int w = 0; w < kDecodeConsumerWarps; ++w) sum += red[w * NREP * D + idx];
+        o_s[idx] = sum;
+    }
+    named_bar_sync(1, kDecodeConsumers);
+
+    // ------------------------------------------------------------------ current token (t == pos)
+    if (owner) {
+        if (warp < NREP) {
+            const int h = warp;
+            float d0 = 0.f;
+            for (int d = lane; d < D; d += 32) d0 = fmaf(q_s[h * D + d], kn_s[d], d0);
+            d0 = warp_sum(d0);
+            const float sv = div ? d0 / scale : d0 * scale;
+            const float m_old = m_s[h];
+            const float m_new = fmaxf(m_old, sv);
+            const float ca = expf(m_old - m_new), cb = expf(sv - m_new);
+            for (int d = lane; d < D; d += 32) o_s[h * D + d] = o_s[h * D + d] * ca + cb * vn_s[d];
+            __syncwarp();
+            if (lane == 0) {
+                m_s[h] = m_new;
+                l_s[h] = l_s[h] * ca + cb;
+            }
+        }
+        named_bar_sync(1, kDecodeConsumers);
+    }
+    if (tid == 0) *stop_s = *abort_s;
+    named_bar_sync(1, kDecodeConsumers);
+    if (*stop_s) return;
+
+    const int head0 = g * NREP;
+    if (a.n_split == 1) {
+        for (int idx = tid; idx < NREP * D; idx += kDecodeConsumers) {
+            const int h = idx / D;
+            const float val = o_s[idx] / l_s[h];
+            a.out[static_cast<size_t>(head0) * D + idx] = val;
+            if (a.peer_out) {
+                for (int rr = 0; rr < a.nranks; ++rr)
+                    a.peer_out[rr][a.q_off + head0 * D + idx] = val;
+            }
+        }
+    } else {
+        constexpr int PS = NREP * (D + 2);
+        float* pp = a.part + (static_cast<size_t>(g) * kDecodeMaxSplit + split) * PS;
+        for (int idx = tid; idx < NREP * D; idx += kDecodeConsumers) pp[idx] = o_s[idx];
+        if (tid < NREP) {
+            pp[NREP * D + tid] = m_s[tid];
+            pp[NREP * D + NREP + tid] = l_s[tid];
+        }
+        __threadfence();
+        named_bar_sync(1, kDecodeConsumers);
+        if (tid == 0) *last_s = (atomicAdd(&a.counters[g], 1) == a.n_split - 1) ? 1 : 0;
+        named_bar_sync(1, kDecodeConsumers);
+        if (!*last_s) return;
+        __threadfence();
+        // The last CTA of this KV head merges all splits (tiles are free: alias weights there).
+        float* wts = reinterpret_cast<float*>(tiles);  // [n_split][NREP]
+        const float* pg = a.part + static_cast<size_t>(g) * kDecodeMaxSplit * PS;
+        if (warp < NREP) {
+            const int h = warp;
+            float M = -INFINITY;
+            for (int s = lane; s < a.n_split; s += 32) M = fmaxf(M, __ldcg(pg + s * PS + NREP * D + h));
+            M = warp_max(M);
+            float L = 0.f;
+            for (int s = lane; s < a.n_split; s += 32) {
+                const float w = expf(__ldcg(pg + s * PS + NREP * D + h) - M);
+                L = fmaf(__ldcg(pg + s * PS + NREP * D + NREP + h), w, L);
+                wts[s * NREP + h] = w;
+            }
+            L = warp_sum(L);
+            if (lane == 0) l_s[h] = L;
+        }
+        named_bar_sync(1, kDecodeConsumers);
+        for (int idx = tid; idx < NREP * D; idx += kDecodeConsumers) {
+            const int h = idx / D;
+            float O = 0.f;
+#pragma unroll 8
+            for (int s = 0; s < a.n_split; ++s) O = fmaf(__ldcg(pg + s * PS + idx), wts[s * NREP + h], O);
+            const float val = O / l_s[h];
+            a.out[static_cast<size_t>(head0) * D + idx] = val;
+            if (a.peer_out) {
+                for (int rr = 0; rr < a.nranks; ++rr)
+                    a.peer_out[rr][a.q_off + head0 * D + idx] = val;
+            }
+        }
+        if (tid == 0) a.counters[g] = 0;
+    }
+    if (a.peer_out) {
+        // Publish: every store of this head group is visible system-wide before the flags.
+        __threadfence_system();
+        named_bar_sync(1, kDecodeConsumers);
+        if (tid < a.nranks) {
+            volatile int* f = a.peer_flag[tid] + a.kv_head0 + g;
+            *f = a.flag_value;
+        }
+    }
+}
+
+}  // namespace lg

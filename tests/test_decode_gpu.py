@@ -1,0 +1,209 @@
+"""Decode attention on the GPU (through the C ABI) against the CPU checkers.
+
+Tolerance (from the north star): max |gpu - ref| <= 1e-4 * max |ref| for the fp32 arithmetic paths.
+The cache is filled on the device by the library's generator and on the host by the restatement;
+the two are bit-identical, which test_kv_synth_matches_host checks first.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+import cases
+from oracle import oracle as orc
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-4
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def make_handle(c, n_layers=None, layer=None, kv_head0=None, kv_headn=None):
+    from ligguf_b200 import AttnConfig, CudaAttention
+    layer = c["layer"] if layer is None else layer
+    n_layers = (layer + 1) if n_layers is None else n_layers
+    cfg = AttnConfig(n_layers=n_layers, n_heads=c["H"], n_kv_heads=c["Hk"], head_dim=c["D"], n_context=c["n_ctx"],
+                     rope_dim=c["rope_dim"], rope_base=c["theta"], rms_epsilon=c["eps"], qk_norm=bool(c["qk_norm"]),
+                     kv_type=c["kv_type"], scale_mode=c["scale_mode"],
+                     kv_head0=c["kv_head0"] if kv_head0 is None else kv_head0,
+                     kv_headn=(c["kv_headn"] if c["kv_headn"] != c["Hk"] else 0) if kv_headn is None else kv_headn)
+    h = CudaAttention(cfg)
+    if c["qk_norm"]:
+        for l in range(n_layers):
+            h.set_qk_norm(l, c["qg"], c["kg"])
+    return h
+
+
+def gpu_decode(c, h=None):
+    h = h or make_handle(c)
+    if c["qk_norm"]:
+        h.set_qk_norm(c["layer"], c["qg"], c["kg"])
+    if c["pos"] > 0:
+        h.kv_synth(c["layer"], 1, 0, c["pos"], c["seed"], c["scale"])
+    out = h.decode(c["layer"], c["pos"], c["q"], c["k"], c["v"])
+    k, v = h.kv_download(c["layer"], c["pos"], 1)
+    return out, k[0], v[0], h
+
+
+def test_kv_synth_matches_host(gpu):
+    for kv_type in (0, 1, 2):
+        c = cases.decode_case(H=8, Hk=2, D=128, n_ctx=80, kv_type=kv_type, pos=77, seed=99, layer=2, scale=0.7)
+        h = make_handle(c)
+        h.kv_synth(2, 1, 0, 77, 99, 0.7)
+        k, v = h.kv_download(2, 0, 77)
+        assert np.array_equal(k, c["kc"][:77]) and np.array_equal(v, c["vc"][:77]), kv_type
+        h.close()
+
+
+@pytest.mark.parametrize("key", ["decode_f32_tinyllama_like", "decode_f16_fast_qwen3", "decode_f32_div_gqa4",
+                                 "decode_f16_rope_partial"])
+def test_decode_vs_reference_golden(gpu, key):
+    spec = dict(json.load(open(os.path.join(GOLDEN, "golden.json")))[key])
+    pos_list = spec.pop("pos_list")
+    gold = np.load(os.path.join(GOLDEN, key + ".npz"))
+    for pos in pos_list:
+        c = cases.decode_case(pos=pos, **spec)
+        out, krow, vrow, h = gpu_decode(c)
+        assert cases.rel_err(out, gold[f"out_{pos}"]) <= TOL, (key, pos)
+        assert np.array_equal(vrow, gold[f"vrow_{pos}"]), (key, pos)
+        kt = spec.get("kv_type", 0)
+        ka, kb = orc.to_f32(krow, kt), orc.to_f32(gold[f"krow_{pos}"], kt)
+        assert np.abs(ka - kb).max() <= (2.0 ** -10 if kt == 1 else 4e-6) * np.abs(kb).max(), (key, pos)
+        h.close()
+
+
+SHAPES = [(32, 4, 64), (32, 8, 128), (8, 8, 64), (16, 8, 128), (16, 2, 128)]
+
+
+@pytest.mark.parametrize("kv_type", [0, 1, 2])
+@pytest.mark.parametrize("shape", SHAPES)
+def test_decode_sweep_vs_port(gpu, kv_type, shape):
+    H, Hk, D = shape
+    port = orc.Checker("port")
+    h = None
+    for pos in (0, 1, 31, 32, 33, 127, 511, 1000):
+        c = cases.decode_case(H=H, Hk=Hk, D=D, n_ctx=1024, theta=1e6, qk_norm=int(D == 128), kv_type=kv_type,
+                              pos=pos, seed=1000 + pos, scale=1.0 if D == 128 else 0.125, layer=1)
+        h = h or make_handle(c, n_layers=2)
+        out, krow, vrow, _ = gpu_decode(c, h)
+        ref, kref, vref = cases.run_decode(port, c)
+        assert cases.rel_err(out, ref) <= TOL, (shape, kv_type, pos)
+        assert np.array_equal(vrow, vref), (shape, kv_type, pos)
+    h.close()
+
+
+def test_decode_scale_div_and_rope_partial(gpu):
+    port = orc.Checker("port")
+    c = cases.decode_case(H=32, Hk=8, D=128, n_ctx=700, rope_dim=96, theta=5e5, qk_norm=1, scale_mode=1, pos=650,
+                          seed=5, scale=1.0)
+    out, _, _, h = gpu_decode(c)
+    ref, _, _ = cases.run_decode(port, c)
+    assert cases.rel_err(out, ref) <= TOL
+    h.close()
+
+
+@pytest.mark.parametrize("name,pos,layer", [("qwen3_8b_decode_4k", 4096, 35), ("qwen3_8b_decode_32k", 32768, 7),
+                                            ("tinyllama_decode_512", 512, 21)])
+def test_decode_full_size_layer(gpu, name, pos, layer):
+    """Full BASELINE configuration sizes (one layer each) against the port."""
+    from ligguf_b200.workloads import DECODE_WORKLOADS
+    w = DECODE_WORKLOADS[name]
+    c = cases.decode_case(H=w.n_heads, Hk=w.n_kv_heads, D=w.head_dim, n_ctx=w.n_context, theta=w.rope_base,
+                          qk_norm=int(w.qk_norm), eps=w.eps, pos=pos, seed=w.seed, scale=w.scale, layer=layer)
+    out, _, _, h = gpu_decode(c)
+    ref, _, _ = cases.run_decode(orc.Checker("port"), c)
+    assert cases.rel_err(out, ref) <= TOL
+    h.close()
+
+
+def test_decode_repeat_is_deterministic_and_layers_independent(gpu):
+    c = cases.decode_case(H=32, Hk=8, D=128, n_ctx=5000, theta=1e6, qk_norm=1, pos=4500, seed=8, layer=2)
+    h = make_handle(c, n_layers=4)
+    h.kv_synth(0, 4, 0, 4500, c["seed"], 1.0)
+    a = h.decode(2, 4500, c["q"], c["k"], c["v"])
+    b = h.decode(2, 4500, c["q"], c["k"], c["v"])
+    assert np.array_equal(a, b)
+    other = h.decode(1, 4500, c["q"], c["k"], c["v"])  # different cache contents -> different result
+    assert not np.array_equal(a, other)
+    c1 = cases.decode_case(H=32, Hk=8, D=128, n_ctx=5000, theta=1e6, qk_norm=1, pos=4500, seed=8, layer=1)
+    c1["q"], c1["k"], c1["v"] = c["q"], c["k"], c["v"]
+    ref1, _, _ = cases.run_decode(orc.Checker("port"), c1)
+    assert cases.rel_err(other, ref1) <= TOL
+    h.close()
+
+
+def test_decode_async_device_tensors(gpu):
+    import torch
+    from ligguf_b200 import synth_fill
+    from ligguf_b200.workloads import SYNTH_KNEW, SYNTH_Q, SYNTH_VNEW, stream_id
+    c = cases.decode_case(H=32, Hk=8, D=128, n_ctx=2100, theta=1e6, qk_norm=1, pos=2049, seed=21, layer=0)
+    h = make_handle(c)
+    h.kv_synth(0, 1, 0, 2049, 21, 1.0)
+    dev = torch.device("cuda", 0)
+    q = torch.empty(32 * 128, device=dev)
+    k = torch.empty(8 * 128, device=dev)
+    v = torch.empty(8 * 128, device=dev)
+    out = torch.empty(32 * 128, device=dev)
+    synth_fill(q, q.numel(), 21, stream_id(SYNTH_Q, 0), 0, 1.0)
+    synth_fill(k, k.numel(), 21, stream_id(SYNTH_KNEW, 0), 0, 1.0)
+    synth_fill(v, v.numel(), 21, stream_id(SYNTH_VNEW, 0), 0, 1.0)
+    assert np.array_equal(q.cpu().numpy(), c["q"])
+    h.decode_async(0, 2049, q, k, v, out)
+    torch.cuda.synchronize()
+    h.sync()
+    ref, _, _ = cases.run_decode(orc.Checker("port"), c)
+    assert cases.rel_err(out.cpu().numpy(), ref) <= TOL
+    h.close()
+
+
+@pytest.mark.parametrize("nranks", [2, 4, 8])
+def test_sharded_decode_matches_unsharded(gpu, nranks):
+    """SARA split by KV head (cpp/ligguf_distrib.cpp:665-679): the shards' outputs, concatenated in
+    rank order, equal the unsharded result (one GPU hosts every shard here)."""
+    from ligguf_b200 import shard_of
+    port = orc.Checker("port")
+    full = cases.decode_case(H=32, Hk=8, D=128, n_ctx=3000, theta=1e6, qk_norm=1, pos=2900, seed=77, layer=0)
+    ref, _, _ = cases.run_decode(port, full)
+    parts = []
+    for r in range(nranks):
+        s = shard_of(8, 32, r, nranks)
+        c = cases.decode_case(H=32, Hk=8, D=128, n_ctx=3000, theta=1e6, qk_norm=1, pos=2900, seed=77, layer=0,
+                              kv_head0=s["kv_head0"], kv_headn=s["kv_headn"])
+        h = make_handle(c, kv_head0=s["kv_head0"], kv_headn=s["kv_headn"])
+        out, _, _, _ = gpu_decode(c, h)
+        parts.append(out)
+        h.close()
+    assert cases.rel_err(np.concatenate(parts), ref) <= TOL
+
+
+def test_kv_roundtrip_fp16_state_layout(gpu):
+    """kv_download/upload move the fast/ligguf_fast_qk.cpp:236-247 per-layer fp16 rows byte for byte."""
+    c = cases.decode_case(H=8, Hk=2, D=64, n_ctx=64, kv_type=1, pos=40, seed=3)
+    h = make_handle(c, n_layers=3)
+    rows_k = orc.from_f32(orc.synth_f32(40 * 128, 1, 1, 0, 1.0), 1).reshape(40, 128)
+    rows_v = orc.from_f32(orc.synth_f32(40 * 128, 1, 2, 0, 1.0), 1).reshape(40, 128)
+    h.kv_upload(2, 0, rows_k, rows_v)
+    k, v = h.kv_download(2, 0, 40)
+    assert np.array_equal(k, rows_k) and np.array_equal(v, rows_v)
+    k0, _ = h.kv_download(1, 0, 40)
+    assert not np.any(k0)  # other layers untouched (zero-initialised like kc.resize(...,0))
+    h.close()
+
+
+def test_errors_are_reported_not_fatal(gpu):
+    from ligguf_b200 import LigGufAttnError
+    c = cases.decode_case(H=8, Hk=2, D=64, n_ctx=16, qk_norm=1, pos=3)
+    from ligguf_b200 import AttnConfig, CudaAttention
+    h = CudaAttention(AttnConfig(n_layers=1, n_heads=8, n_kv_heads=2, head_dim=64, n_context=16, rope_dim=64,
+                                 qk_norm=True))
+    with pytest.raises(LigGufAttnError) as e:  # QK-norm weights not set
+        h.decode(0, 3, c["q"], c["k"], c["v"])
+    assert e.value.status == -6
+    h.set_qk_norm(0, c["qg"], c["kg"])
+    with pytest.raises(LigGufAttnError) as e:
+        h.decode(0, 16, c["q"], c["k"], c["v"])  # pos == n_context
+    assert e.value.status == -1
+    with pytest.raises(LigGufAttnError):
+        h.decode(1, 3, c["q"], c["k"], c["v"])  # layer out of range
+    h.decode(0, 3, c["q"], c["k"], c["v"])  # still usable
+    h.close()
