@@ -35,9 +35,11 @@ int fail(int code, const char* fmt, ...) {
 #define LG_CUDA(expr)                                                                          \
     do {                                                                                       \
         const cudaError_t e_ = (expr);                                                         \
-        if (e_ != cudaSuccess)                                                                 \
+        if (e_ != cudaSuccess) {                                                               \
+            (void)cudaGetLastError(); /* do not leave it pending for unrelated calls */       \
             return fail(LIGGUF_ATTN_ECUDA, "%s failed: %s (%s:%d)", #expr,                     \
                         cudaGetErrorString(e_), __FILE__, __LINE__);                           \
+        }                                                                                      \
     } while (0)
 
 struct DeviceGuard {
@@ -74,10 +76,11 @@ CUtensorMapDataType kv_tmap_type(int kv_type) {
                                       : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
 }
 
-// Per (kernel instantiation, device): raise the dynamic shared memory limit once.
+// Raises the dynamic shared memory limit of `kernel` once per device.  `done` is the caller's
+// per-instantiation flag array (function-pointer types are shared by all instantiations of a
+// template kernel, so the flags cannot live here).
 template <typename K>
-cudaError_t ensure_smem_attr(K kernel, int device, size_t bytes) {
-    static bool done[64] = {};
+cudaError_t ensure_smem_attr(K kernel, int device, size_t bytes, bool* done) {
     if (device >= 0 && device < 64 && done[device]) return cudaSuccess;
     const cudaError_t e =
         cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
@@ -216,7 +219,8 @@ template <typename KV, int D, int NREP>
 int launch_decode_t(ligguf_attn* h, const lg::DecodeArgs& a, cudaStream_t st) {
     using Sm = lg::DecodeSmem<KV, D, NREP>;
     auto kern = lg::decode_kernel<KV, D, NREP>;
-    LG_CUDA(ensure_smem_attr(kern, h->cfg.device, Sm::kTotal));
+    static bool attr_done[64] = {};
+    LG_CUDA(ensure_smem_attr(kern, h->cfg.device, Sm::kTotal, attr_done));
     cudaLaunchConfig_t lc = {};
     lc.gridDim = dim3(a.n_split, h->kv_dim / D, 1);
     lc.blockDim = dim3(lg::kDecodeThreads, 1, 1);
@@ -314,7 +318,8 @@ int decode_enqueue(ligguf_attn* h, int layer, int pos, const float* dq, const fl
 template <typename KV, int D>
 int launch_flash_simt_t(const lg::FlashArgs& f, dim3 grid, cudaStream_t st, int device) {
     auto kern = lg::flash_simt_kernel<KV, D>;
-    LG_CUDA(ensure_smem_attr(kern, device, lg::FlashSimtSmem<D>::kBytes));
+    static bool attr_done[64] = {};
+    LG_CUDA(ensure_smem_attr(kern, device, lg::FlashSimtSmem<D>::kBytes, attr_done));
     kern<<<grid, lg::kFlashThreads, lg::FlashSimtSmem<D>::kBytes, st>>>(f);
     LG_CUDA(cudaGetLastError());
     return LIGGUF_ATTN_OK;
@@ -351,6 +356,43 @@ int grow(T** p, size_t* cap, size_t need) {
         return fail(LIGGUF_ATTN_ENOMEM, "cudaMalloc of %zu bytes failed", need * sizeof(T));
     *cap = need;
     return LIGGUF_ATTN_OK;
+}
+
+// ---------------------------------------------------------------------------- tensor-core launch
+int make_bf16_tmap(CUtensorMap* m, const void* base, int D, int heads, int rows) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return fail(LIGGUF_ATTN_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    cuuint64_t dims[3] = {cuuint64_t(D), cuuint64_t(heads), cuuint64_t(rows)};
+    cuuint64_t strides[2] = {cuuint64_t(D) * 2, cuuint64_t(heads) * D * 2};
+    cuuint32_t box[3] = {64u, 1u, cuuint32_t(lg::kTcRows)};
+    cuuint32_t estr[3] = {1u, 1u, 1u};
+    const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(LIGGUF_ATTN_ECUDA, "cuTensorMapEncodeTiled (bf16 operand) failed (%d)", int(r));
+    return LIGGUF_ATTN_OK;
+}
+
+template <int D>
+int launch_flash_tc_t(const lg::TcArgs& t, cudaStream_t st, int device) {
+    alignas(64) CUtensorMap tq, tk, tv;
+    int rc;
+    if ((rc = make_bf16_tmap(&tq, t.q, D, t.q_heads, t.q_rows))) return rc;
+    if ((rc = make_bf16_tmap(&tk, t.k, D, t.kv_heads, t.kv_rows))) return rc;
+    if ((rc = make_bf16_tmap(&tv, t.v, D, t.kv_heads, t.kv_rows))) return rc;
+    auto kern = lg::flash_tc_kernel<D>;
+    static bool attr_done[64] = {};
+    LG_CUDA(ensure_smem_attr(kern, device, lg::TcSmem<D>::kTotal, attr_done));
+    const dim3 grid((t.q_seq + lg::kTcRows - 1) / lg::kTcRows, t.q_heads, t.batch);
+    kern<<<grid, lg::kTcThreads, lg::TcSmem<D>::kTotal, st>>>(tq, tk, tv, t);
+    LG_CUDA(cudaGetLastError());
+    return LIGGUF_ATTN_OK;
+}
+
+int launch_flash_tc(const lg::TcArgs& t, int D, cudaStream_t st, int device) {
+    if (D == 64) return launch_flash_tc_t<64>(t, st, device);
+    if (D == 128) return launch_flash_tc_t<128>(t, st, device);
+    return fail(LIGGUF_ATTN_EUNSUPPORTED, "head_dim %d has no tensor-core attention kernel", D);
 }
 
 int prefill_enqueue(ligguf_attn* h, int layer, int pos0, int n, const float* dq, const float* dk, const float* dv,
@@ -474,8 +516,7 @@ int prefill_enqueue(ligguf_attn* h, int layer, int pos0, int n, const float* dq,
     t.nrep = h->nrep;
     t.scale_log2 = (div ? 1.0f / sqrtf(static_cast<float>(D)) : scale) * 1.4426950408889634f;
     t.err = h->d_err;
-    return lg::launch_flash_tc(t, D, st, c.device, h->num_sms) ? fail(LIGGUF_ATTN_ECUDA, "%s", lg::tc_last_error())
-                                                                : LIGGUF_ATTN_OK;
+    return launch_flash_tc(t, D, st, c.device);
 }
 
 }  // namespace
@@ -924,10 +965,7 @@ int ligguf_cuda_bert_attn_async(ligguf_bert_attn* b, int batch, int max_len, con
     t.nrep = 1;
     t.scale_log2 = (1.0f / sqrtf(static_cast<float>(D))) * 1.4426950408889634f;
     t.err = b->d_err;
-    int nsm = 148;
-    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, b->device);
-    return lg::launch_flash_tc(t, D, st, b->device, nsm) ? fail(LIGGUF_ATTN_ECUDA, "%s", lg::tc_last_error())
-                                                          : LIGGUF_ATTN_OK;
+    return launch_flash_tc(t, D, st, b->device);
 }
 
 int ligguf_cuda_bert_attn(ligguf_bert_attn* b, int batch, int max_len, const int* lens, const float* q,
