@@ -38,6 +38,8 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extra", action="store_true", help="skip the other configurations at N=1")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--case", choices=["decode-layer", "prefill-layer", "bert-layer"], default=None,
+                    help="run one small case a few times and exit (the command the ncu summaries use)")
     return ap.parse_args()
 
 
@@ -478,10 +480,64 @@ def run_extras(peaks):
     return extra
 
 
+def run_case(case: str, reps: int = 3):
+    """Small single-GPU cases for profiling: the kernel of one layer of the named configuration,
+    `reps` launches, a few hundred MB on the device."""
+    import numpy as np
+    import torch
+    from ligguf_b200 import AttnConfig, CudaAttention, CudaBertAttention, synth_fill
+    from ligguf_b200.workloads import BERT_BASE, QWEN3_DECODE_32K, QWEN3_PREFILL
+    dev = torch.device("cuda", 0)
+    g = np.ones(128, dtype=np.float32)
+    if case == "decode-layer":  # qwen3_8b_decode_32k shapes, 2 layers of cache (537 MB), layer 0
+        w = QWEN3_DECODE_32K
+        h = CudaAttention(AttnConfig(n_layers=2, n_heads=w.n_heads, n_kv_heads=w.n_kv_heads, head_dim=w.head_dim,
+                                     n_context=w.n_context, rope_dim=w.rope_dim, rope_base=w.rope_base,
+                                     rms_epsilon=w.eps, qk_norm=True))
+        h.set_qk_norm(0, g, g)
+        h.kv_synth(0, 1, 0, w.pos, w.seed, w.scale)
+        q, k, v = torch.empty(w.q_dim, device=dev), torch.empty(w.kv_dim, device=dev), torch.empty(w.kv_dim, device=dev)
+        out = torch.empty(w.q_dim, device=dev)
+        for t, x in ((3, q), (4, k), (5, v)):
+            synth_fill(x, x.numel(), w.seed, t << 32, 0, w.scale)
+        for _ in range(reps):
+            h.decode_async(0, w.pos, q, k, v, out)
+    elif case == "prefill-layer":  # qwen3_8b_prefill_2048, one layer, tensor-core path
+        w = QWEN3_PREFILL
+        h = CudaAttention(AttnConfig(n_layers=1, n_heads=w.n_heads, n_kv_heads=w.n_kv_heads, head_dim=w.head_dim,
+                                     n_context=w.n_context, rope_dim=w.rope_dim, rope_base=w.rope_base,
+                                     rms_epsilon=w.eps, qk_norm=True))
+        h.set_qk_norm(0, g, g)
+        n = w.n_tokens
+        q = torch.empty(n, w.n_heads * w.head_dim, device=dev)
+        k = torch.empty(n, w.n_kv_heads * w.head_dim, device=dev)
+        v, out = torch.empty_like(k), torch.empty_like(q)
+        for t, x in ((3, q), (4, k), (5, v)):
+            synth_fill(x, x.numel(), w.seed, t << 32, 0, w.scale)
+        for _ in range(reps):
+            h.prefill_async(0, 0, n, q, k, v, out, 1)
+    else:  # bert_base_attn, one layer, tensor-core path
+        w = BERT_BASE
+        n = w.batch * w.max_len * w.n_heads * w.head_dim
+        q, k, v, out = (torch.empty(n, device=dev) for _ in range(4))
+        for t, x in ((3, q), (1, k), (2, v)):
+            synth_fill(x, n, w.seed, t << 32, 0, w.scale)
+        lens = torch.tensor(w.lens(), dtype=torch.int32, device=dev)
+        h = CudaBertAttention(w.n_heads, w.head_dim, w.batch, w.max_len, 0)
+        for _ in range(reps):
+            h.attn_async(w.batch, w.max_len, lens, q, k, v, out, 1)
+    torch.cuda.synchronize()
+    h.close()
+    print(f"case {case}: ok")
+    return 0
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.case:
+        return run_case(args.case)
     import torch
     from ligguf_b200 import load
     from ligguf_b200.workloads import DECODE_WORKLOADS

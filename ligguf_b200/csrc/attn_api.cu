@@ -279,15 +279,12 @@ int decode_enqueue(ligguf_attn* h, int layer, int pos, const float* dq, const fl
     const int tp = decode_tile_rows(c.kv_type, D);
     a.n_tiles = ceil_div(pos, tp);
     const int kvh = h->kv_dim / D;
+    // One resident wave: blocks_per_sm * SMs CTAs shared by the KV heads.  Each CTA starts on one
+    // static chunk and then grabs chunks of its head dynamically, about 12 grabs per CTA.
     const int want = std::max(1, decode_blocks_per_sm(c.kv_type, h->nrep) * h->num_sms / kvh);
-    int tps = std::max(1, ceil_div(a.n_tiles, want));
-    int ns = a.n_tiles ? ceil_div(a.n_tiles, tps) : 1;
-    while (ns > lg::kDecodeMaxSplit) {
-        ++tps;
-        ns = ceil_div(a.n_tiles, tps);
-    }
-    a.tiles_per_split = tps;
-    a.n_split = ns;
+    a.n_split = std::max(1, std::min(want, a.n_tiles));
+    a.chunk = std::max(1, a.n_tiles / (a.n_split * 12));
+    a.chunk_ctr = h->counters + kvh;
     a.kv_dim = h->kv_dim;
     a.rope_pairs = h->rope_pairs;
     a.qk_norm = c.qk_norm;
@@ -383,7 +380,7 @@ int launch_flash_tc_t(const lg::TcArgs& t, cudaStream_t st, int device) {
     auto kern = lg::flash_tc_kernel<D>;
     static bool attr_done[64] = {};
     LG_CUDA(ensure_smem_attr(kern, device, lg::TcSmem<D>::kTotal, attr_done));
-    const dim3 grid((t.q_seq + lg::kTcRows - 1) / lg::kTcRows, t.q_heads, t.batch);
+    const dim3 grid(t.q_heads, (t.q_seq + lg::kTcRows - 1) / lg::kTcRows, t.batch);
     kern<<<grid, lg::kTcThreads, lg::TcSmem<D>::kTotal, st>>>(tq, tk, tv, t);
     LG_CUDA(cudaGetLastError());
     return LIGGUF_ATTN_OK;
@@ -623,10 +620,10 @@ int ligguf_cuda_attn_init(const ligguf_attn_cfg* cfg, ligguf_attn** out) {
     const size_t part_floats = size_t(c.kv_headn) * lg::kDecodeMaxSplit * nrep * (c.head_dim + 2);
     if (cudaMalloc(&h->freq, nfreq * 4) != cudaSuccess || cudaMalloc(&h->qg, pd * 4) != cudaSuccess ||
         cudaMalloc(&h->kg, pd * 4) != cudaSuccess || cudaMalloc(&h->part, part_floats * 4) != cudaSuccess ||
-        cudaMalloc(&h->counters, c.kv_headn * sizeof(int)) != cudaSuccess)
+        cudaMalloc(&h->counters, 2 * c.kv_headn * sizeof(int)) != cudaSuccess)
         return bail(fail(LIGGUF_ATTN_ENOMEM, "handle buffers"));
     if (cudaMemcpy(h->freq, freq.data(), nfreq * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemset(h->counters, 0, c.kv_headn * sizeof(int)) != cudaSuccess)
+        cudaMemset(h->counters, 0, 2 * c.kv_headn * sizeof(int)) != cudaSuccess)
         return bail(fail(LIGGUF_ATTN_ECUDA, "handle initialisation copies"));
     if (cudaHostAlloc(&h->h_err, 64, cudaHostAllocMapped) != cudaSuccess ||
         cudaHostGetDevicePointer(reinterpret_cast<void**>(&h->d_err), h->h_err, 0) != cudaSuccess)
@@ -675,7 +672,7 @@ int ligguf_cuda_attn_decode(ligguf_attn* h, int layer, int pos, const float* q, 
     if ((rc = decode_enqueue(h, layer, pos, dq, dk, dv, dout, h->stream, false))) return rc;
     LG_CUDA(cudaMemcpyAsync(out, dout, nq * 4, cudaMemcpyDeviceToHost, h->stream));
     LG_CUDA(cudaStreamSynchronize(h->stream));
-    return check_err_word(h->h_err, h->counters, h->kv_dim / h->cfg.head_dim);
+    return check_err_word(h->h_err, h->counters, 2 * h->kv_dim / h->cfg.head_dim);
 }
 
 int ligguf_cuda_attn_prefill_async(ligguf_attn* h, int layer, int pos0, int n, const float* d_q, const float* d_k,
@@ -703,7 +700,7 @@ int ligguf_cuda_attn_prefill(ligguf_attn* h, int layer, int pos0, int n, const f
     if ((rc = prefill_enqueue(h, layer, pos0, n, dq, dk, dv, dout, mode, h->stream))) return rc;
     LG_CUDA(cudaMemcpyAsync(out, dout, nq * 4, cudaMemcpyDeviceToHost, h->stream));
     LG_CUDA(cudaStreamSynchronize(h->stream));
-    return check_err_word(h->h_err, h->counters, h->kv_dim / h->cfg.head_dim);
+    return check_err_word(h->h_err, h->counters, 2 * h->kv_dim / h->cfg.head_dim);
 }
 
 int ligguf_cuda_attn_kv_download(ligguf_attn* h, int layer, int pos0, int n, void* host_k, void* host_v) {
@@ -773,7 +770,7 @@ int ligguf_cuda_attn_sync(ligguf_attn* h) {
     DeviceGuard dg(h->cfg.device);
     LG_CUDA(cudaStreamSynchronize(h->stream));
     LG_CUDA(cudaDeviceSynchronize());
-    return check_err_word(h->h_err, h->counters, h->kv_dim / h->cfg.head_dim);
+    return check_err_word(h->h_err, h->counters, 2 * h->kv_dim / h->cfg.head_dim);
 }
 
 // ---------------------------------------------------------------------------- SARA gather

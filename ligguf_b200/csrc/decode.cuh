@@ -56,7 +56,9 @@ struct DecodeArgs {
     int row0;           // tensor-map row of (this layer, position 0) = layer * n_context
     int pos;
     int n_tiles;        // tiles covering [0, pos)
-    int tiles_per_split;
+    int chunk;          // tiles per grab: CTA `split` starts with tiles [split*chunk, +chunk), then takes
+                        // further chunks from chunk_ctr[g] (first dynamic chunk = n_split*chunk)
+    int* chunk_ctr;     // [kv_headn] grab counters, zero between launches (reset with the tickets)
     int n_split;
     int kv_dim;
     int rope_pairs;
@@ -90,8 +92,8 @@ struct DecodeSmem {
     static constexpr size_t kOOff = kQOff + NREP * D * 4;
     static constexpr size_t kKnOff = kOOff + NREP * D * 4;
     static constexpr size_t kVnOff = kKnOff + D * 4;
-    static constexpr size_t kMiscOff = kVnOff + D * 4;  // corr, m, l [NREP] + 4 ints
-    static constexpr size_t kBarOff = (kMiscOff + 3 * NREP * 4 + 16 + 7) & ~size_t(7);
+    static constexpr size_t kMiscOff = kVnOff + D * 4;  // corr, m, l [NREP] + 4 ints + stage tile ids
+    static constexpr size_t kBarOff = (kMiscOff + 3 * NREP * 4 + 16 + 4 * kDecodeStages + 7) & ~size_t(7);
     static constexpr size_t kTotal = kBarOff + 3 * kDecodeStages * 8;
     static_assert(kDecodeConsumerWarps * NREP * D * 4 <= kTilesBytes, "reduction buffer alias");
     static_assert(kDecodeMaxSplit * NREP * 4 <= kTilesBytes, "combine weights alias");
@@ -133,6 +135,47 @@ __device__ __forceinline__ void norm_rope_head(const float* __restrict__ src,
             const float x0 = x[u].x, x1 = x[u].y;
             x[u].x = x0 * cs - x1 * sn;
             x[u].y = x0 * sn + x1 * cs;
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < kPairs; ++u) reinterpret_cast<float2*>(dst)[lane + 32 * u] = x[u];
+}
+
+// Same as norm_rope_head with the rotation taken from per-position tables cs/sn[rope_pairs]
+// (shared by every head of one token).
+template <int D>
+__device__ __forceinline__ void norm_rope_head_tab(const float* __restrict__ src,
+                                                   const float* __restrict__ gamma, int norm, float eps,
+                                                   const float* cs, const float* sn, int rope_pairs,
+                                                   float* dst, int lane) {
+    constexpr int kPairs = D / 64;
+    float2 x[kPairs];
+#pragma unroll
+    for (int u = 0; u < kPairs; ++u) x[u] = reinterpret_cast<const float2*>(src)[lane + 32 * u];
+    if (norm) {
+        float ss = 0.f;
+#pragma unroll
+        for (int u = 0; u < kPairs; ++u) {
+            ss = fmaf(x[u].x, x[u].x, ss);
+            ss = fmaf(x[u].y, x[u].y, ss);
+        }
+        ss = warp_sum(ss);
+        const float rs = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
+#pragma unroll
+        for (int u = 0; u < kPairs; ++u) {
+            const int m = lane + 32 * u;
+            x[u].x = (x[u].x * rs) * gamma[2 * m];
+            x[u].y = (x[u].y * rs) * gamma[2 * m + 1];
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < kPairs; ++u) {
+        const int m = lane + 32 * u;
+        if (m < rope_pairs) {
+            const float c = cs[m], sn_ = sn[m];
+            const float x0 = x[u].x, x1 = x[u].y;
+            x[u].x = x0 * c - x1 * sn_;
+            x[u].y = x0 * sn_ + x1 * c;
         }
     }
 #pragma unroll
@@ -192,6 +235,8 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
     volatile int* abort_s = reinterpret_cast<volatile int*>(l_s + NREP);
     volatile int* last_s = abort_s + 1;
     volatile int* stop_s = abort_s + 2;
+    volatile int* decide_s = abort_s + 3;   // consumers' uniform loop-exit decision
+    volatile int* tile_id_s = abort_s + 4;  // [kDecodeStages]: tile held by each stage, -1 = end
     uint64_t* full_k = reinterpret_cast<uint64_t*>(smem + Sm::kBarOff);
     uint64_t* full_v = full_k + kDecodeStages;
     uint64_t* empty = full_v + kDecodeStages;
@@ -199,10 +244,7 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int split = blockIdx.x, g = blockIdx.y;
     const uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
-    const int tile0 = split * a.tiles_per_split;
-    const int tile1 = min(tile0 + a.tiles_per_split, a.n_tiles);
-    const int my_tiles = max(0, tile1 - tile0);
-    const int t_end = min(tile1 * TP, a.pos);
+    const int t_end = a.pos;  // cached positions are [0, pos); the current token is folded in last
     const bool owner = split == a.n_split - 1;
 
     if (tid == 0) {
@@ -221,30 +263,53 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
 
     // ------------------------------------------------------------------ producer warp
     if (warp == kDecodeConsumerWarps) {
-        if (lane == 0 && my_tiles > 0) {
-            int issued = 0;
-            for (int it = 0; it < my_tiles; ++it) {
+        if (lane == 0) {
+            int it = 0;        // stage uses so far
+            int issued = 0;    // stage uses that carry copies
+            bool fail = false;
+            int base = split * a.chunk;  // first chunk: static
+            const int first_dyn = a.n_split * a.chunk;
+            while (!fail && base < a.n_tiles) {
+                // Fetch the next chunk now; its latency overlaps this chunk's waits and copies.
+                const int next = a.n_split > 1 ? first_dyn + atomicAdd(&a.chunk_ctr[g], a.chunk) : a.n_tiles;
+                const int lim = min(base + a.chunk, a.n_tiles);
+                for (int t = base; t < lim; ++t, ++it) {
+                    const int s = it % kDecodeStages;
+                    if (it >= kDecodeStages &&
+                        !mbar_wait_bounded(&empty[s], ((it / kDecodeStages) - 1) & 1, deadline, abort_s)) {
+                        *abort_s = 1;
+                        *reinterpret_cast<volatile int*>(a.err) = KERR_TIMEOUT_EMPTY;
+                        fail = true;
+                        break;
+                    }
+                    tile_id_s[s] = t;
+                    const int row = a.row0 + t * TP;
+                    uint8_t* kdst = tiles + s * Sm::kStageBytes;
+                    mbar_arrive_expect_tx(&full_k[s], kDecodeTileBytes);
+                    tma_load_3d(kdst, &tm_k, &full_k[s], 0, g, row);
+                    mbar_arrive_expect_tx(&full_v[s], kDecodeTileBytes);
+                    tma_load_3d(kdst + kDecodeTileBytes, &tm_v, &full_v[s], 0, g, row);
+                    ++issued;
+                }
+                base = next;
+            }
+            if (!fail) {  // end marker: a stage whose K barrier completes without data
                 const int s = it % kDecodeStages;
                 if (it >= kDecodeStages &&
                     !mbar_wait_bounded(&empty[s], ((it / kDecodeStages) - 1) & 1, deadline, abort_s)) {
                     *abort_s = 1;
                     *reinterpret_cast<volatile int*>(a.err) = KERR_TIMEOUT_EMPTY;
-                    break;
+                } else {
+                    tile_id_s[s] = -1;
+                    mbar_arrive(&full_k[s]);
                 }
-                const int row = a.row0 + (tile0 + it) * TP;
-                uint8_t* kdst = tiles + s * Sm::kStageBytes;
-                mbar_arrive_expect_tx(&full_k[s], kDecodeTileBytes);
-                tma_load_3d(kdst, &tm_k, &full_k[s], 0, g, row);
-                mbar_arrive_expect_tx(&full_v[s], kDecodeTileBytes);
-                tma_load_3d(kdst + kDecodeTileBytes, &tm_v, &full_v[s], 0, g, row);
-                ++issued;
             }
             // Our copies must land before this CTA may exit: wait for the last ring's worth
             // (ignoring the abort flag, bounded by a later deadline).
             const uint64_t drain_deadline = deadline + kWaitLimitNs / 2;
-            for (int it = max(0, issued - kDecodeStages); it < issued; ++it) {
-                const int s = it % kDecodeStages;
-                const uint32_t par = (it / kDecodeStages) & 1;
+            for (int u = max(0, issued - kDecodeStages); u < issued; ++u) {
+                const int s = u % kDecodeStages;
+                const uint32_t par = (u / kDecodeStages) & 1;
                 while (!mbar_try_wait(&full_k[s], par) && globaltimer_ns() < drain_deadline) {
                 }
                 while (!mbar_try_wait(&full_v[s], par) && globaltimer_ns() < drain_deadline) {
@@ -297,11 +362,10 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
     const bool div = a.scale_div != 0;
     const float scale = a.scale;
 
-    for (int it = 0; it < my_tiles; ++it) {
+    for (int it = 0;; ++it) {
         const int s = it % kDecodeStages;
         const uint32_t par = (it / kDecodeStages) & 1;
         float* scb = sc + (it & 1) * NREP * TP;
-        const int tbase = (tile0 + it) * TP;
         const uint8_t* kt = tiles + s * Sm::kStageBytes;
         const uint8_t* vt = kt + kDecodeTileBytes;
 
@@ -312,7 +376,9 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
                 *reinterpret_cast<volatile int*>(a.err) = KERR_TIMEOUT_FULL;
             }
         }
-        if (ok) {
+        const int tile = ok ? tile_id_s[s] : -1;  // -1: the producer's end marker
+        const int tbase = tile * TP;
+        if (ok && tile >= 0) {
             float part[NV];
 #pragma unroll
             for (int i = 0; i < NI; ++i) {
@@ -351,7 +417,10 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
             }
         }
         named_bar_sync(1, kDecodeConsumers);
-        if (ok && warp < NREP) {  // online softmax of this tile for head `warp`
+        // Loop exit is decided once for all consumer warps (so every warp runs the same number of
+        // named barriers): written here by thread 0, read by everyone after the next barrier.
+        if (tid == 0) *decide_s = (*abort_s != 0 || tile_id_s[s] < 0) ? 1 : 0;
+        if (ok && tile >= 0 && warp < NREP) {  // online softmax of this tile for head `warp`
             constexpr int PU = TP / 32;
             float sv[PU];
             float mx = -INFINITY;
@@ -381,6 +450,7 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
             if (lane == 0) corr_s[warp] = corr;
         }
         named_bar_sync(1, kDecodeConsumers);
+        if (*decide_s) break;
         if (ok) {
             ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full_v[s], par, deadline, abort_s));
             if (!ok && lane == 0) {
@@ -522,7 +592,10 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
                     a.peer_out[rr][a.q_off + head0 * D + idx] = val;
             }
         }
-        if (tid == 0) a.counters[g] = 0;
+        if (tid == 0) {  // every CTA of this head took its ticket after its last grab: reset both
+            a.counters[g] = 0;
+            a.chunk_ctr[g] = 0;
+        }
     }
     if (a.peer_out) {
         // Publish: every store of this head group is visible system-wide before the flags.

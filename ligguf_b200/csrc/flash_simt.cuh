@@ -246,15 +246,19 @@ struct PrepArgs {
 template <typename KV, int D>
 __global__ void __launch_bounds__(256) prefill_prep_kernel(const PrepArgs a) {
     __shared__ float rowbuf[8][D];
+    __shared__ float cs[D / 2], sn[D / 2];  // RoPE rotation of this token, shared by all heads
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int i = blockIdx.x;
     const int pos = a.pos0 + i;
+    for (int m = threadIdx.x; m < a.rope_pairs; m += blockDim.x)
+        sincosf(static_cast<float>(pos) * a.freq[m], &sn[m], &cs[m]);
+    __syncthreads();
     const int jobs = a.q_headn + 2 * a.kv_headn;
     float* buf = rowbuf[warp];
     for (int job = warp; job < jobs; job += 8) {
         if (job < a.q_headn) {
-            norm_rope_head<D>(a.q + (static_cast<size_t>(i) * a.q_headn + job) * D, a.qg, a.qk_norm,
-                              a.eps, a.freq, a.rope_pairs, pos, buf, lane);
+            norm_rope_head_tab<D>(a.q + (static_cast<size_t>(i) * a.q_headn + job) * D, a.qg, a.qk_norm,
+                                  a.eps, cs, sn, a.rope_pairs, buf, lane);
             __syncwarp();
             const size_t o = (static_cast<size_t>(i) * a.q_headn + job) * D;
             for (int d = lane; d < D; d += 32) {
@@ -266,7 +270,7 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const PrepArgs a) {
             const int gi = is_k ? job - a.q_headn : job - a.q_headn - a.kv_headn;
             const float* src = (is_k ? a.k : a.v) + (static_cast<size_t>(i) * a.kv_headn + gi) * D;
             if (is_k) {
-                norm_rope_head<D>(src, a.kg, a.qk_norm, a.eps, a.freq, a.rope_pairs, pos, buf, lane);
+                norm_rope_head_tab<D>(src, a.kg, a.qk_norm, a.eps, cs, sn, a.rope_pairs, buf, lane);
             } else {
                 for (int d = lane; d < D; d += 32) buf[d] = src[d];
             }

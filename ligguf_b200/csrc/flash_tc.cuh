@@ -122,6 +122,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         : "r"(taddr)
         : "memory");
 }
+// Same, into 32 consecutive elements of a larger register array (no wait: batch several, then
+// tmem_wait_ld once).
+__device__ __forceinline__ void tmem_ld32p(uint32_t taddr, uint32_t* r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+        "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : LG_R32(r)
+        : "r"(taddr)
+        : "memory");
+}
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
@@ -181,8 +191,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_qt = (a.q_seq + kTcRows - 1) / kTcRows;
-    const int qt = n_qt - 1 - static_cast<int>(blockIdx.x);  // longest causal rows first
-    const int h = blockIdx.y, b = blockIdx.z;
+    // Blocks start in linear order (x fastest): x = head, y = query tile from the last (longest under
+    // the causal mask) to the first, so every wave takes the heaviest remaining tiles of all heads.
+    const int h = blockIdx.x, b = blockIdx.z;
+    const int qt = n_qt - 1 - static_cast<int>(blockIdx.y);
     const int g = h / a.nrep;
     const int r0 = qt * kTcRows;
     const int nq_valid = a.lens ? min(a.lens[b], a.q_seq) : a.q_seq;
@@ -335,43 +347,50 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                                      KERR_TIMEOUT_MMA));
             if (!ok) break;
             tc_fence_after();
-            float sv[kTcKeys];
+            uint32_t raw[kTcKeys];
 #pragma unroll
-            for (int ch = 0; ch < kTcKeys / 32; ++ch) {
-                tmem_ld32(tmem_s0 + bf * kTcKeys + ch * 32 + lane_off, x);
-                tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 32; ++i) sv[ch * 32 + i] = __uint_as_float(x[i]);
-            }
+            for (int ch = 0; ch < kTcKeys / 32; ++ch)
+                tmem_ld32p(tmem_s0 + bf * kTcKeys + ch * 32 + lane_off, raw + ch * 32);
+            tmem_wait_ld();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&s_free[bf]);
+            float sv[kTcKeys];
+#pragma unroll
+            for (int c = 0; c < kTcKeys; ++c) sv[c] = __uint_as_float(raw[c]);
 
             const int k0 = j * kTcKeys;  // key position of column 0 (sequence-relative)
             const bool edge = (k0 + kTcKeys > kv_len) || (a.causal && k0 + kTcKeys - 1 > a.q_pos0 + r0);
-            float mx = -INFINITY;
             if (edge) {
                 const int lim_c = kv_len - k0;
                 const int lim_r = a.causal ? a.q_pos0 + qr - k0 : kTcKeys;
 #pragma unroll
-                for (int c = 0; c < kTcKeys; ++c) {
-                    const bool valid = c < lim_c && c <= lim_r;
-                    sv[c] = valid ? sv[c] : -INFINITY;
-                    mx = fmaxf(mx, sv[c]);
-                }
-            } else {
-#pragma unroll
-                for (int c = 0; c < kTcKeys; ++c) mx = fmaxf(mx, sv[c]);
+                for (int c = 0; c < kTcKeys; ++c) sv[c] = (c < lim_c && c <= lim_r) ? sv[c] : -INFINITY;
             }
-            const float m_new = fmaxf(m, mx * c2);
+            // Row max and sum with 8 independent chains (a single chain serialises 128 dependent ops).
+            float mx8[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) mx8[u] = sv[u];
+#pragma unroll
+            for (int c = 8; c < kTcKeys; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], sv[c]);
+            const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                   fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+            // The running max (log2 units) only moves when the tile max exceeds it by more than 8:
+            // p = 2^(s*c2 - m) then stays <= 256 and O/l are rescaled rarely; the normalisation at
+            // the end uses the same m, so the result is unchanged.
+            const float mt = mx * c2;
+            const float m_new = (m == -INFINITY || mt > m + 8.0f) ? mt : m;
             const float ms = m_new == -INFINITY ? 0.f : m_new;
-            const float corr = m_new == -INFINITY ? 1.f : fast_exp2(m - m_new);
-            float rs = 0.f;
+            const float corr = (m == m_new || m_new == -INFINITY) ? 1.f : fast_exp2(m - m_new);
+            float rs8[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) rs8[u] = 0.f;
 #pragma unroll
             for (int c = 0; c < kTcKeys; ++c) {
                 sv[c] = fast_exp2(fmaf(sv[c], c2, -ms));
-                rs += sv[c];
+                rs8[c & 7] += sv[c];
             }
+            const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
             l = l * corr + rs;
             m = m_new;
             if (j >= 1) {  // O holds PV(0..j-1): wait for it, then rescale if the max moved
@@ -379,8 +398,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                                          KERR_TIMEOUT_MMA));
                 if (!ok) break;
                 tc_fence_after();
-                if (__any_sync(0xffffffffu, corr != 1.f)) {
-#pragma unroll
+                if (__any_sync(0xffffffffu, corr != 1.f)) {  // rare: the max moved by more than 2^8
+#pragma unroll 1
                     for (int ch = 0; ch < D / 32; ++ch) {
                         tmem_ld32(tmem_o + ch * 32 + lane_off, x);
                         tmem_wait_ld();

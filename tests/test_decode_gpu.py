@@ -127,6 +127,7 @@ def test_decode_repeat_is_deterministic_and_layers_independent(gpu):
     assert not np.array_equal(a, other)
     c1 = cases.decode_case(H=32, Hk=8, D=128, n_ctx=5000, theta=1e6, qk_norm=1, pos=4500, seed=8, layer=1)
     c1["q"], c1["k"], c1["v"] = c["q"], c["k"], c["v"]
+    c1["qg"], c1["kg"] = c["qg"], c["kg"]  # make_handle gave every layer layer 2's norm weights
     ref1, _, _ = cases.run_decode(orc.Checker("port"), c1)
     assert cases.rel_err(other, ref1) <= TOL
     h.close()
