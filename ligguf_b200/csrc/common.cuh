@@ -1,6 +1,6 @@
 // common.cuh - device helpers shared by the attention kernels (sm_100a only).
 //
-// mbarrier / TMA (cp.async.bulk.tensor, no multicast) wrappers, bounded waits that give up after
+// mbarrier / TMA (cp.async.bulk.tensor into this CTA only) wrappers, bounded waits that give up after
 // a deadline on %globaltimer and report through an error word instead of hanging, KV element
 // traits, warp reductions and the seeded synthetic generator.
 #pragma once
@@ -76,7 +76,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 
 // ---------------------------------------------------------------------------------- TMA
 // 3-D tiled load global -> shared, completion counted on `bar`.  Destination is this CTA's own
-// shared memory; no multicast.
+// shared memory only.
 __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
                                             int c0, int c1, int c2) {
     asm volatile(

@@ -9,10 +9,12 @@
 //   for each q head h (kv head h/nrep): s_t = q.k_t * scale, softmax over t in [0,pos],
 //   out_h = sum_t p_t v_t, with t == pos taken from the fp32 k, v (:77-78, :98-99).
 //
-// Grid (n_split, kv_headn).  CTA (split, g) owns KV head g and a contiguous run of 16 KB tiles of
-// cached positions [0, pos); it computes all nrep q heads of the group so each K/V byte is read
-// from HBM once.  Warp 8 is the producer: one lane streams K and V tiles of the run with TMA into a
-// 3-stage shared-memory ring.  Warps 0..7 consume: scores (each lane dots 16 B of a row with
+// Grid (n_split, kv_headn), one resident wave.  CTA (split, g) works on KV head g: it starts on a
+// static chunk of 16 KB tiles of cached positions [0, pos) and then takes further chunks of the
+// head from an atomic counter (so CTAs that stream faster take more tiles; one static wave left SMs
+// idle for a fifth of the kernel).  It computes all nrep q heads of the group, so each K/V byte is
+// read from HBM once.  Warp 8 is the producer: one lane grabs chunks and streams their K and V tiles
+// with TMA into a 3-stage shared-memory ring, publishing each stage's tile index in shared memory.  Warps 0..7 consume: scores (each lane dots 16 B of a row with
 // the nrep q vectors, a transposed butterfly reduces nrep*4 dot products with one shuffle per
 // result), an online softmax per tile, P.V accumulation in registers.  The last CTA of a KV head
 // (atomic ticket) merges the splits' (max, sum, o) partials and writes the output, so the whole
@@ -271,8 +273,8 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
             const int first_dyn = a.n_split * a.chunk;
             while (!fail && base < a.n_tiles) {
                 // Fetch the next chunk now; its latency overlaps this chunk's waits and copies.
-                const int next = a.n_split > 1 ? first_dyn + atomicAdd(&a.chunk_ctr[g], a.chunk) : a.n_tiles;
                 const int lim = min(base + a.chunk, a.n_tiles);
+                const int next = a.n_split > 1 ? first_dyn + atomicAdd(&a.chunk_ctr[g], a.chunk) : lim;
                 for (int t = base; t < lim; ++t, ++it) {
                     const int s = it % kDecodeStages;
                     if (it >= kDecodeStages &&
@@ -293,6 +295,7 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
                 }
                 base = next;
             }
+            bool marker = false;
             if (!fail) {  // end marker: a stage whose K barrier completes without data
                 const int s = it % kDecodeStages;
                 if (it >= kDecodeStages &&
@@ -302,12 +305,15 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
                 } else {
                     tile_id_s[s] = -1;
                     mbar_arrive(&full_k[s]);
+                    marker = true;
                 }
             }
-            // Our copies must land before this CTA may exit: wait for the last ring's worth
-            // (ignoring the abort flag, bounded by a later deadline).
+            // Our copies must land before this CTA may exit: wait for the uses not yet known to be
+            // consumed (ignoring the abort flag, bounded by a later deadline).  When the end marker
+            // went in, its stage's previous use was consumed (we waited on its empty barrier) and
+            // that stage's K barrier is one phase ahead, so the drain starts one use later.
             const uint64_t drain_deadline = deadline + kWaitLimitNs / 2;
-            for (int u = max(0, issued - kDecodeStages); u < issued; ++u) {
+            for (int u = max(0, issued - kDecodeStages + (marker ? 1 : 0)); u < issued; ++u) {
                 const int s = u % kDecodeStages;
                 const uint32_t par = (u / kDecodeStages) & 1;
                 while (!mbar_try_wait(&full_k[s], par) && globaltimer_ns() < drain_deadline) {

@@ -116,13 +116,16 @@ def test_decode_full_size_layer(gpu, name, pos, layer):
     h.close()
 
 
-def test_decode_repeat_is_deterministic_and_layers_independent(gpu):
+def test_decode_repeat_and_layers_independent(gpu):
+    """Repeated calls agree to fp32 rounding (tiles are handed out dynamically, so the merge order of
+    the split partials - not the set of terms - can change between calls), and layers are separate."""
     c = cases.decode_case(H=32, Hk=8, D=128, n_ctx=5000, theta=1e6, qk_norm=1, pos=4500, seed=8, layer=2)
     h = make_handle(c, n_layers=4)
     h.kv_synth(0, 4, 0, 4500, c["seed"], 1.0)
     a = h.decode(2, 4500, c["q"], c["k"], c["v"])
-    b = h.decode(2, 4500, c["q"], c["k"], c["v"])
-    assert np.array_equal(a, b)
+    for _ in range(5):
+        b = h.decode(2, 4500, c["q"], c["k"], c["v"])
+        assert cases.rel_err(b, a) <= 1e-6
     other = h.decode(1, 4500, c["q"], c["k"], c["v"])  # different cache contents -> different result
     assert not np.array_equal(a, other)
     c1 = cases.decode_case(H=32, Hk=8, D=128, n_ctx=5000, theta=1e6, qk_norm=1, pos=4500, seed=8, layer=1)
