@@ -98,7 +98,7 @@ struct DecodeSmem {
     static constexpr size_t kBarOff = (kMiscOff + 3 * NREP * 4 + 16 + 4 * kDecodeStages + 7) & ~size_t(7);
     static constexpr size_t kTotal = kBarOff + 3 * kDecodeStages * 8;
     static_assert(kDecodeConsumerWarps * NREP * D * 4 <= kTilesBytes, "reduction buffer alias");
-    static_assert(kDecodeMaxSplit * NREP * 4 <= kTilesBytes, "combine weights alias");
+    static_assert(2 * kDecodeMaxSplit * NREP * 4 <= kTilesBytes, "combine maxima/weights alias");
 };
 
 // One warp: optional RMSNorm then RoPE of one head (D floats) from global `src` into `dst`.
@@ -184,6 +184,65 @@ __device__ __forceinline__ void norm_rope_head_tab(const float* __restrict__ src
     for (int u = 0; u < kPairs; ++u) reinterpret_cast<float2*>(dst)[lane + 32 * u] = x[u];
 }
 
+// Prologue inputs of one head, loaded early so their latency overlaps the kernel's set-up.
+template <int D>
+struct HeadIn {
+    float2 x[D / 64];
+    float2 gm[D / 64];
+    float cs[D / 64], sn[D / 64];
+};
+
+template <int D>
+__device__ __forceinline__ void head_prefetch(HeadIn<D>& in, const float* __restrict__ src,
+                                              const float* __restrict__ gamma, int norm,
+                                              const float* __restrict__ freq, int rope_pairs, int pos,
+                                              int lane) {
+#pragma unroll
+    for (int u = 0; u < D / 64; ++u) {
+        const int m = lane + 32 * u;
+        in.x[u] = reinterpret_cast<const float2*>(src)[m];
+        in.gm[u] = norm ? reinterpret_cast<const float2*>(gamma)[m] : make_float2(1.f, 1.f);
+        in.cs[u] = 1.f;
+        in.sn[u] = 0.f;
+        if (m < rope_pairs) sincosf(static_cast<float>(pos) * freq[m], &in.sn[u], &in.cs[u]);
+    }
+}
+
+// The arithmetic of norm_rope_head on prefetched inputs.
+template <int D>
+__device__ __forceinline__ void head_finish(const HeadIn<D>& in, int norm, float eps, int rope_pairs,
+                                            float* dst, int lane) {
+    constexpr int kPairs = D / 64;
+    float2 x[kPairs];
+#pragma unroll
+    for (int u = 0; u < kPairs; ++u) x[u] = in.x[u];
+    if (norm) {
+        float ss = 0.f;
+#pragma unroll
+        for (int u = 0; u < kPairs; ++u) {
+            ss = fmaf(x[u].x, x[u].x, ss);
+            ss = fmaf(x[u].y, x[u].y, ss);
+        }
+        ss = warp_sum(ss);
+        const float rs = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
+#pragma unroll
+        for (int u = 0; u < kPairs; ++u) {
+            x[u].x = (x[u].x * rs) * in.gm[u].x;
+            x[u].y = (x[u].y * rs) * in.gm[u].y;
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < kPairs; ++u) {
+        if (lane + 32 * u < rope_pairs) {
+            const float x0 = x[u].x, x1 = x[u].y;
+            x[u].x = x0 * in.cs[u] - x1 * in.sn[u];
+            x[u].y = x0 * in.sn[u] + x1 * in.cs[u];
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < kPairs; ++u) reinterpret_cast<float2*>(dst)[lane + 32 * u] = x[u];
+}
+
 // Sums V per-lane values over the 2^S lanes that share the upper lane bits, leaving each lane
 // with max(1, V >> S) sums: lane j (low S bits) holds value indices [j*VF, j*VF+VF) when V >= 2^S,
 // else index j / (2^S / V).  One shuffle per produced sum instead of S per sum.
@@ -249,6 +308,21 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
     const int t_end = a.pos;  // cached positions are [0, pos); the current token is folded in last
     const bool owner = split == a.n_split - 1;
 
+    // Consumer warps start loading their first prologue job (q head, and k / v of the current token
+    // on the owner CTA) right away; the norm and rotation happen after the set-up barrier.
+    const int njobs = NREP + (owner ? 2 : 0);
+    HeadIn<D> pin;
+    if (warp < kDecodeConsumerWarps && warp < njobs) {
+        if (warp < NREP)
+            head_prefetch<D>(pin, a.q + static_cast<size_t>(g * NREP + warp) * D, a.qg, a.qk_norm, a.freq,
+                             a.rope_pairs, a.pos, lane);
+        else if (warp == NREP)
+            head_prefetch<D>(pin, a.k + static_cast<size_t>(g) * D, a.kg, a.qk_norm, a.freq, a.rope_pairs,
+                             a.pos, lane);
+        else
+            head_prefetch<D>(pin, a.v + static_cast<size_t>(g) * D, nullptr, 0, a.freq, 0, a.pos, lane);
+    }
+
     if (tid == 0) {
 #pragma unroll
         for (int s = 0; s < kDecodeStages; ++s) {
@@ -272,9 +346,8 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
             int base = split * a.chunk;  // first chunk: static
             const int first_dyn = a.n_split * a.chunk;
             while (!fail && base < a.n_tiles) {
-                // Fetch the next chunk now; its latency overlaps this chunk's waits and copies.
                 const int lim = min(base + a.chunk, a.n_tiles);
-                const int next = a.n_split > 1 ? first_dyn + atomicAdd(&a.chunk_ctr[g], a.chunk) : lim;
+                int next = lim;
                 for (int t = base; t < lim; ++t, ++it) {
                     const int s = it % kDecodeStages;
                     if (it >= kDecodeStages &&
@@ -292,6 +365,9 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
                     mbar_arrive_expect_tx(&full_v[s], kDecodeTileBytes);
                     tma_load_3d(kdst + kDecodeTileBytes, &tm_v, &full_v[s], 0, g, row);
                     ++issued;
+                    // Fetch the next chunk once this chunk's first copy is on its way: the grab's
+                    // latency overlaps the remaining waits and copies instead of delaying them.
+                    if (t == base && a.n_split > 1) next = first_dyn + atomicAdd(&a.chunk_ctr[g], a.chunk);
                 }
                 base = next;
             }
@@ -327,9 +403,11 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
 
     // ------------------------------------------------------------------ consumers: prologue
     {
-        const int njobs = NREP + (owner ? 2 : 0);
         for (int job = warp; job < njobs; job += kDecodeConsumerWarps) {
-            if (job < NREP) {
+            if (job == warp) {  // first round: inputs already in registers
+                float* dst = job < NREP ? q_s + job * D : (job == NREP ? kn_s : vn_s);
+                head_finish<D>(pin, job <= NREP ? a.qk_norm : 0, a.eps, job <= NREP ? a.rope_pairs : 0, dst, lane);
+            } else if (job < NREP) {
                 const int hq = g * NREP + job;
                 norm_rope_head<D>(a.q + static_cast<size_t>(hq) * D, a.qg, a.qk_norm, a.eps, a.freq,
                                   a.rope_pairs, a.pos, q_s + job * D, lane);
@@ -568,34 +646,68 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
         named_bar_sync(1, kDecodeConsumers);
         if (!*last_s) return;
         __threadfence();
-        // The last CTA of this KV head merges all splits (tiles are free: alias weights there).
-        float* wts = reinterpret_cast<float*>(tiles);  // [n_split][NREP]
+        // The last CTA of this KV head merges all splits (the tiles are free: alias them).  Every
+        // load is issued in parallel batches: this merge is the kernel's tail.
+        float* m_all = reinterpret_cast<float*>(tiles);  // [n_split][NREP] split maxima
+        float* w_all = m_all + kDecodeMaxSplit * NREP;   // [n_split][NREP] split sums, then weights
         const float* pg = a.part + static_cast<size_t>(g) * kDecodeMaxSplit * PS;
+        for (int i = tid; i < a.n_split * NREP; i += kDecodeConsumers) {
+            const int sp = i / NREP, h = i % NREP;
+            m_all[i] = __ldcg(pg + sp * PS + NREP * D + h);
+            w_all[i] = __ldcg(pg + sp * PS + NREP * D + NREP + h);
+        }
+        named_bar_sync(1, kDecodeConsumers);
         if (warp < NREP) {
             const int h = warp;
             float M = -INFINITY;
-            for (int s = lane; s < a.n_split; s += 32) M = fmaxf(M, __ldcg(pg + s * PS + NREP * D + h));
+            for (int sp = lane; sp < a.n_split; sp += 32) M = fmaxf(M, m_all[sp * NREP + h]);
             M = warp_max(M);
             float L = 0.f;
-            for (int s = lane; s < a.n_split; s += 32) {
-                const float w = expf(__ldcg(pg + s * PS + NREP * D + h) - M);
-                L = fmaf(__ldcg(pg + s * PS + NREP * D + NREP + h), w, L);
-                wts[s * NREP + h] = w;
+            for (int sp = lane; sp < a.n_split; sp += 32) {
+                const float w = expf(m_all[sp * NREP + h] - M);
+                L = fmaf(w_all[sp * NREP + h], w, L);
+                w_all[sp * NREP + h] = w;
             }
             L = warp_sum(L);
             if (lane == 0) l_s[h] = L;
         }
         named_bar_sync(1, kDecodeConsumers);
-        for (int idx = tid; idx < NREP * D; idx += kDecodeConsumers) {
-            const int h = idx / D;
-            float O = 0.f;
-#pragma unroll 8
-            for (int s = 0; s < a.n_split; ++s) O = fmaf(__ldcg(pg + s * PS + idx), wts[s * NREP + h], O);
-            const float val = O / l_s[h];
-            a.out[static_cast<size_t>(head0) * D + idx] = val;
-            if (a.peer_out) {
-                for (int rr = 0; rr < a.nranks; ++rr)
-                    a.peer_out[rr][a.q_off + head0 * D + idx] = val;
+        constexpr int CPT = (NREP * D + kDecodeConsumers - 1) / kDecodeConsumers;  // columns per thread
+        constexpr int BATCH = 16;
+        float acc[CPT][4];
+#pragma unroll
+        for (int c = 0; c < CPT; ++c)
+#pragma unroll
+            for (int u = 0; u < 4; ++u) acc[c][u] = 0.f;
+        for (int s0 = 0; s0 < a.n_split; s0 += BATCH) {
+            float v[CPT][BATCH];
+#pragma unroll
+            for (int c = 0; c < CPT; ++c) {
+                const int idx = tid + c * kDecodeConsumers;
+#pragma unroll
+                for (int u = 0; u < BATCH; ++u)
+                    v[c][u] = (idx < NREP * D && s0 + u < a.n_split) ? __ldcg(pg + (s0 + u) * PS + idx) : 0.f;
+            }
+#pragma unroll
+            for (int c = 0; c < CPT; ++c) {
+                const int idx = tid + c * kDecodeConsumers;
+                const int h = min(idx, NREP * D - 1) / D;
+#pragma unroll
+                for (int u = 0; u < BATCH; ++u)
+                    if (s0 + u < a.n_split) acc[c][u & 3] = fmaf(v[c][u], w_all[(s0 + u) * NREP + h], acc[c][u & 3]);
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < CPT; ++c) {
+            const int idx = tid + c * kDecodeConsumers;
+            if (idx < NREP * D) {
+                const int h = idx / D;
+                const float val = ((acc[c][0] + acc[c][1]) + (acc[c][2] + acc[c][3])) / l_s[h];
+                a.out[static_cast<size_t>(head0) * D + idx] = val;
+                if (a.peer_out) {
+                    for (int rr = 0; rr < a.nranks; ++rr)
+                        a.peer_out[rr][a.q_off + head0 * D + idx] = val;
+                }
             }
         }
         if (tid == 0) {  // every CTA of this head took its ticket after its last grab: reset both
