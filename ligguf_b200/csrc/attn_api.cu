@@ -280,10 +280,11 @@ int decode_enqueue(ligguf_attn* h, int layer, int pos, const float* dq, const fl
     a.n_tiles = ceil_div(pos, tp);
     const int kvh = h->kv_dim / D;
     // One resident wave: blocks_per_sm * SMs CTAs shared by the KV heads.  Each CTA starts on one
-    // static chunk and then grabs chunks of its head dynamically, about 12 grabs per CTA.
+    // static chunk and then grabs chunks of its head dynamically: single tiles up to ~48 tiles per
+    // CTA (finish times then differ by about one tile), larger chunks beyond.
     const int want = std::max(1, decode_blocks_per_sm(c.kv_type, h->nrep) * h->num_sms / kvh);
     a.n_split = std::max(1, std::min(want, a.n_tiles));
-    a.chunk = std::max(1, a.n_tiles / (a.n_split * 12));
+    a.chunk = std::max(1, a.n_tiles / (a.n_split * 48));
     a.chunk_ctr = h->counters + kvh;
     a.kv_dim = h->kv_dim;
     a.rope_pairs = h->rope_pairs;

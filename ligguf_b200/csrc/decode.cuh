@@ -189,7 +189,7 @@ template <int D>
 struct HeadIn {
     float2 x[D / 64];
     float2 gm[D / 64];
-    float cs[D / 64], sn[D / 64];
+    float fr[D / 64];  // inverse frequency of each pair (0 where no rotation)
 };
 
 template <int D>
@@ -202,15 +202,14 @@ __device__ __forceinline__ void head_prefetch(HeadIn<D>& in, const float* __rest
         const int m = lane + 32 * u;
         in.x[u] = reinterpret_cast<const float2*>(src)[m];
         in.gm[u] = norm ? reinterpret_cast<const float2*>(gamma)[m] : make_float2(1.f, 1.f);
-        in.cs[u] = 1.f;
-        in.sn[u] = 0.f;
-        if (m < rope_pairs) sincosf(static_cast<float>(pos) * freq[m], &in.sn[u], &in.cs[u]);
+        in.fr[u] = m < rope_pairs ? freq[m] : 0.f;
     }
+    (void)pos;
 }
 
 // The arithmetic of norm_rope_head on prefetched inputs.
 template <int D>
-__device__ __forceinline__ void head_finish(const HeadIn<D>& in, int norm, float eps, int rope_pairs,
+__device__ __forceinline__ void head_finish(const HeadIn<D>& in, int norm, float eps, int rope_pairs, int pos,
                                             float* dst, int lane) {
     constexpr int kPairs = D / 64;
     float2 x[kPairs];
@@ -234,9 +233,11 @@ __device__ __forceinline__ void head_finish(const HeadIn<D>& in, int norm, float
 #pragma unroll
     for (int u = 0; u < kPairs; ++u) {
         if (lane + 32 * u < rope_pairs) {
+            float sn, cs;
+            sincosf(static_cast<float>(pos) * in.fr[u], &sn, &cs);
             const float x0 = x[u].x, x1 = x[u].y;
-            x[u].x = x0 * in.cs[u] - x1 * in.sn[u];
-            x[u].y = x0 * in.sn[u] + x1 * in.cs[u];
+            x[u].x = x0 * cs - x1 * sn;
+            x[u].y = x0 * sn + x1 * cs;
         }
     }
 #pragma unroll
@@ -406,7 +407,8 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
         for (int job = warp; job < njobs; job += kDecodeConsumerWarps) {
             if (job == warp) {  // first round: inputs already in registers
                 float* dst = job < NREP ? q_s + job * D : (job == NREP ? kn_s : vn_s);
-                head_finish<D>(pin, job <= NREP ? a.qk_norm : 0, a.eps, job <= NREP ? a.rope_pairs : 0, dst, lane);
+                head_finish<D>(pin, job <= NREP ? a.qk_norm : 0, a.eps, job <= NREP ? a.rope_pairs : 0, a.pos,
+                               dst, lane);
             } else if (job < NREP) {
                 const int hq = g * NREP + job;
                 norm_rope_head<D>(a.q + static_cast<size_t>(hq) * D, a.qg, a.qk_norm, a.eps, a.freq,
@@ -646,34 +648,15 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
         named_bar_sync(1, kDecodeConsumers);
         if (!*last_s) return;
         __threadfence();
-        // The last CTA of this KV head merges all splits (the tiles are free: alias them).  Every
-        // load is issued in parallel batches: this merge is the kernel's tail.
+        // The last CTA of this KV head merges all splits (the tiles are free: alias them).  This
+        // merge is the kernel's tail, so its loads are issued in batches before any is used: the o
+        // columns of up to 24 splits per thread together with the maxima and sums (two round trips
+        // to L2 for the 37 splits of a 148-SM wave).
         float* m_all = reinterpret_cast<float*>(tiles);  // [n_split][NREP] split maxima
         float* w_all = m_all + kDecodeMaxSplit * NREP;   // [n_split][NREP] split sums, then weights
         const float* pg = a.part + static_cast<size_t>(g) * kDecodeMaxSplit * PS;
-        for (int i = tid; i < a.n_split * NREP; i += kDecodeConsumers) {
-            const int sp = i / NREP, h = i % NREP;
-            m_all[i] = __ldcg(pg + sp * PS + NREP * D + h);
-            w_all[i] = __ldcg(pg + sp * PS + NREP * D + NREP + h);
-        }
-        named_bar_sync(1, kDecodeConsumers);
-        if (warp < NREP) {
-            const int h = warp;
-            float M = -INFINITY;
-            for (int sp = lane; sp < a.n_split; sp += 32) M = fmaxf(M, m_all[sp * NREP + h]);
-            M = warp_max(M);
-            float L = 0.f;
-            for (int sp = lane; sp < a.n_split; sp += 32) {
-                const float w = expf(m_all[sp * NREP + h] - M);
-                L = fmaf(w_all[sp * NREP + h], w, L);
-                w_all[sp * NREP + h] = w;
-            }
-            L = warp_sum(L);
-            if (lane == 0) l_s[h] = L;
-        }
-        named_bar_sync(1, kDecodeConsumers);
         constexpr int CPT = (NREP * D + kDecodeConsumers - 1) / kDecodeConsumers;  // columns per thread
-        constexpr int BATCH = 16;
+        constexpr int BATCH = 24;  // splits held in registers at once (no spills at nrep 4, D 128)
         float acc[CPT][4];
 #pragma unroll
         for (int c = 0; c < CPT; ++c)
@@ -687,6 +670,29 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
 #pragma unroll
                 for (int u = 0; u < BATCH; ++u)
                     v[c][u] = (idx < NREP * D && s0 + u < a.n_split) ? __ldcg(pg + (s0 + u) * PS + idx) : 0.f;
+            }
+            if (s0 == 0) {
+                for (int i = tid; i < a.n_split * NREP; i += kDecodeConsumers) {
+                    const int sp = i / NREP, h = i % NREP;
+                    m_all[i] = __ldcg(pg + sp * PS + NREP * D + h);
+                    w_all[i] = __ldcg(pg + sp * PS + NREP * D + NREP + h);
+                }
+                named_bar_sync(1, kDecodeConsumers);
+                if (warp < NREP) {
+                    const int h = warp;
+                    float M = -INFINITY;
+                    for (int sp = lane; sp < a.n_split; sp += 32) M = fmaxf(M, m_all[sp * NREP + h]);
+                    M = warp_max(M);
+                    float L = 0.f;
+                    for (int sp = lane; sp < a.n_split; sp += 32) {
+                        const float w = expf(m_all[sp * NREP + h] - M);
+                        L = fmaf(w_all[sp * NREP + h], w, L);
+                        w_all[sp * NREP + h] = w;
+                    }
+                    L = warp_sum(L);
+                    if (lane == 0) l_s[h] = L;
+                }
+                named_bar_sync(1, kDecodeConsumers);
             }
 #pragma unroll
             for (int c = 0; c < CPT; ++c) {
