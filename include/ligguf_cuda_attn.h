@@ -174,6 +174,30 @@ int ligguf_cuda_bert_attn_async(ligguf_bert_attn* b, int batch, int max_len, con
                                 const float* d_q, const float* d_k, const float* d_v,
                                 float* d_out, int mode, void* stream);
 
+/* ---- BERT attention without device allocation ------------------------------------------- */
+/* No counterpart in the reference: an addition for callers that may not allocate device memory.
+ * Such callers include hosts that route every device allocation through their own memory pool and
+ * forbid libraries from calling cudaMalloc, and latency-critical loops where cudaMalloc's implicit
+ * device-wide synchronisation and unbounded cost are not acceptable.
+ *
+ * Same computation as ligguf_cuda_bert_attn_async with LIGGUF_MODE_TC (bf16 operands on the
+ * tcgen05 tensor cores, fp32 accumulation), but with no handle and no allocation: the bf16 copies
+ * of q, k and v live in a fixed array inside the library, reserved on every GPU that loads it
+ * (24 MiB + 256 B, held until the process exits).  Device pointers, enqueued on `stream`, on the
+ * current device; layouts as ligguf_cuda_bert_attn.
+ *   - Limit: batch*max_len*n_heads*head_dim <= LIGGUF_NOALLOC_MAX_ELEMS per tensor; larger calls
+ *     return LIGGUF_ATTN_EINVAL without touching the GPU.
+ *   - The first call on a device looks up the array's device address (cudaGetSymbolAddress); make
+ *     that first call before any stream capture.
+ *   - Every call reuses the same array: calls whose work overlaps on the GPU (other streams, other
+ *     host threads) race and corrupt each other; serialise them.  The kernel's error word is cleared
+ *     at the start of each call; a bounded in-kernel wait that gives up leaves `d_out` unwritten and
+ *     is not reported back through this call. */
+#define LIGGUF_NOALLOC_MAX_ELEMS (1 << 22)
+int ligguf_cuda_bert_attn_tc_noalloc(int n_heads, int head_dim, int batch, int max_len, const int* d_lens,
+                                     const float* d_q, const float* d_k, const float* d_v, float* d_out,
+                                     void* stream);
+
 /* ---- seeded synthetic inputs ------------------------------------------------------------- */
 /* Tensor ids of the synthetic generator's streams. */
 #define LIGGUF_SYNTH_K 1

@@ -16,6 +16,7 @@ KV_F32, KV_F16, KV_BF16 = 0, 1, 2
 SCALE_MUL, SCALE_DIV = 0, 1
 MODE_SIMT, MODE_TC = 0, 1
 SYNTH_K, SYNTH_V, SYNTH_Q, SYNTH_KNEW, SYNTH_VNEW, SYNTH_QGAMMA, SYNTH_KGAMMA = 1, 2, 3, 4, 5, 6, 7
+NOALLOC_MAX_ELEMS = 1 << 22  # LIGGUF_NOALLOC_MAX_ELEMS
 
 _i, _f, _u64, _sz, _vp, _cp = ctypes.c_int, ctypes.c_float, ctypes.c_uint64, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_char_p
 
@@ -70,6 +71,7 @@ _PROTOS = {
     "ligguf_cuda_bert_free": [_vp],
     "ligguf_cuda_bert_attn": [_vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _i],
     "ligguf_cuda_bert_attn_async": [_vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _i, _vp],
+    "ligguf_cuda_bert_attn_tc_noalloc": [_i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp],
     "ligguf_cuda_synth_fill": [_vp, _i, _sz, _u64, _u64, _u64, _f, _f, _vp],
 }
 

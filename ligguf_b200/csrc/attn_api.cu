@@ -9,6 +9,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -519,6 +520,39 @@ int prefill_enqueue(ligguf_attn* h, int layer, int pos0, int n, const float* dq,
 
 }  // namespace
 
+// ============================================================================== no-allocation scratch
+// Scratch of ligguf_cuda_bert_attn_tc_noalloc, reserved in every GPU that loads this library for as
+// long as the process lives: the bf16 copies of q, k and v (LIGGUF_NOALLOC_MAX_ELEMS elements
+// each, 8 MiB apiece) followed by 256 bytes holding the kernel's error word.  Host code must not
+// hand the symbol itself to a kernel (on the host it is only a stand-in for the device array); the
+// device address comes from cudaGetSymbolAddress, once per device.
+constexpr size_t kNoallocOperandBytes = size_t(LIGGUF_NOALLOC_MAX_ELEMS) * sizeof(__nv_bfloat16);
+constexpr size_t kNoallocBytes = 3 * kNoallocOperandBytes + 256;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocBytes];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {};
+
+// Device address of g_noalloc_scratch on the current device (looked up on the first call there).
+int noalloc_scratch(int device, unsigned char** out) {
+    if (device < 0 || device >= 64) return fail(LIGGUF_ATTN_EINVAL, "device %d", device);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_addr[device]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p) {
+            (void)cudaGetLastError();
+            return fail(LIGGUF_ATTN_ECUDA, "cudaGetSymbolAddress of the no-allocation scratch failed: %s",
+                        cudaGetErrorString(e));
+        }
+        g_noalloc_addr[device] = p;
+    }
+    *out = static_cast<unsigned char*>(g_noalloc_addr[device]);
+    return LIGGUF_ATTN_OK;
+}
+}  // namespace
+
 // ============================================================================== C ABI
 extern "C" {
 
@@ -994,6 +1028,56 @@ int ligguf_cuda_bert_attn(ligguf_bert_attn* b, int batch, int max_len, const int
     LG_CUDA(cudaMemcpyAsync(out, dout, elems * 4, cudaMemcpyDeviceToHost, b->stream));
     LG_CUDA(cudaStreamSynchronize(b->stream));
     return check_err_word(b->h_err, nullptr, 0);
+}
+
+// ---------------------------------------------------------------------------- BERT, no allocation
+int ligguf_cuda_bert_attn_tc_noalloc(int n_heads, int head_dim, int batch, int max_len, const int* d_lens,
+                                     const float* d_q, const float* d_k, const float* d_v, float* d_out,
+                                     void* stream) {
+    if (!d_lens || !d_q || !d_k || !d_v || !d_out) return fail(LIGGUF_ATTN_EINVAL, "null argument");
+    if (n_heads < 1 || batch < 1 || max_len < 1) return fail(LIGGUF_ATTN_EINVAL, "non-positive size");
+    if (head_dim != 64 && head_dim != 128) return fail(LIGGUF_ATTN_EUNSUPPORTED, "head_dim %d", head_dim);
+    const size_t elems = size_t(batch) * max_len * n_heads * head_dim;
+    if (elems > size_t(LIGGUF_NOALLOC_MAX_ELEMS))
+        return fail(LIGGUF_ATTN_EINVAL,
+                    "batch*max_len*n_heads*head_dim = %zu exceeds the no-allocation limit of %d elements per "
+                    "tensor (LIGGUF_NOALLOC_MAX_ELEMS); use ligguf_cuda_bert_attn_async",
+                    elems, LIGGUF_NOALLOC_MAX_ELEMS);
+    int device = 0;
+    LG_CUDA(cudaGetDevice(&device));
+    unsigned char* base = nullptr;
+    int rc = noalloc_scratch(device, &base);
+    if (rc) return rc;
+    __nv_bfloat16* bq = reinterpret_cast<__nv_bfloat16*>(base);
+    __nv_bfloat16* bk = reinterpret_cast<__nv_bfloat16*>(base + kNoallocOperandBytes);
+    __nv_bfloat16* bv = reinterpret_cast<__nv_bfloat16*>(base + 2 * kNoallocOperandBytes);
+    int* err = reinterpret_cast<int*>(base + 3 * kNoallocOperandBytes);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    LG_CUDA(cudaMemsetAsync(err, 0, sizeof(int), st));  // the previous call's error word must not leak
+    const int blocks = std::min(1184, std::max(1, ceil_div(elems, 256)));
+    lg::to_bf16_kernel<<<blocks, 256, 0, st>>>(d_q, bq, elems);
+    lg::to_bf16_kernel<<<blocks, 256, 0, st>>>(d_k, bk, elems);
+    lg::to_bf16_kernel<<<blocks, 256, 0, st>>>(d_v, bv, elems);
+    LG_CUDA(cudaGetLastError());
+    lg::TcArgs t = {};
+    t.q = bq;
+    t.k = bk;
+    t.v = bv;
+    t.out = d_out;
+    t.q_rows = batch * max_len;
+    t.q_heads = n_heads;
+    t.kv_rows = batch * max_len;
+    t.kv_heads = n_heads;
+    t.batch = batch;
+    t.q_seq = max_len;
+    t.kv_seq = max_len;
+    t.lens = d_lens;
+    t.causal = 0;
+    t.q_pos0 = 0;
+    t.nrep = 1;
+    t.scale_log2 = (1.0f / sqrtf(static_cast<float>(head_dim))) * 1.4426950408889634f;
+    t.err = err;
+    return launch_flash_tc(t, head_dim, st, device);
 }
 
 // ---------------------------------------------------------------------------- synth
