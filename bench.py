@@ -38,6 +38,8 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extra", action="store_true", help="skip the other configurations at N=1")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--gather", choices=["p2p", "nccl"], default="p2p",
+                    help="N>1: all-gather of head outputs by the decode kernel's peer stores (p2p) or NCCL")
     ap.add_argument("--case", choices=["decode-layer", "prefill-layer", "bert-layer"], default=None,
                     help="run one small case a few times and exit (the command the ncu summaries use)")
     return ap.parse_args()
@@ -243,55 +245,74 @@ def bench_decode(args, w, rank, world, local, pg, peaks):
     full = torch.empty(w.n_layers, w.n_heads * D, device=dev) if world > 1 else out
     L = w.n_layers
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L * args.steps)]
+    if world > 1:  # the fused gather: decode epilogues store into every peer's buffer (CUDA IPC)
+        mine = h.gather_ipc_handle()
+        handles = [None] * world
+        pg.all_gather_object(handles, mine)
+        h.gather_open(rank, handles)
 
-    def step(i=None):
+    def step(i=None, gather=args.gather):
         for l in range(L):
             if i is not None:
                 ev[i * L + l][0].record()
-            h.decode_async(l, w.pos, q[l], k[l], v[l], out[l])
+            if world > 1 and gather == "p2p":
+                h.decode_gather_async(l, w.pos, q[l], k[l], v[l])
+            else:
+                h.decode_async(l, w.pos, q[l], k[l], v[l], out[l])
             if i is not None:
                 ev[i * L + l][1].record()
             if world > 1:
-                pg.all_gather_into_tensor(full[l], out[l])
+                if gather == "p2p":
+                    h.gather_wait_async(l, full[l])
+                else:
+                    pg.all_gather_into_tensor(full[l], out[l])
 
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    h.sync()
-    if world > 1:
-        pg.barrier()
-    torch.cuda.synchronize()
+    def timed(n, gather, with_events):
+        for _ in range(args.warmup):
+            step(gather=gather)
+        torch.cuda.synchronize()
+        h.sync()
+        if world > 1:
+            pg.barrier()
+        torch.cuda.synchronize()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for i in range(n):
+            step(i if with_events else None, gather=gather)
+        t1.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            pg.barrier()
+            torch.cuda.synchronize()
+        h.sync()
+        ms = t0.elapsed_time(t1)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms / n
+
     clk = ClockSampler(local)
     clk.start()
     time.sleep(0.3)
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    t0.record()
-    for i in range(args.steps):
-        step(i)
-    t1.record()
-    torch.cuda.synchronize()
-    if world > 1:
-        pg.barrier()
-        torch.cuda.synchronize()
+    ms_per_step = timed(args.steps, args.gather, True)
     clocks = clk.stop()
-    h.sync()
-    elapsed_ms = t0.elapsed_time(t1)
-    kern_ms = [a.elapsed_time(b) for a, b in ev]
-    if world > 1:
-        t = torch.tensor([elapsed_ms], device=dev)
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        elapsed_ms = float(t.item())
-    ms_per_step = elapsed_ms / args.steps
     tok_s = 1e3 / ms_per_step
+    kern_ms = [a.elapsed_time(b) for a, b in ev]
     kern_avg_ms = statistics.mean(kern_ms)
     bytes_launch = 2 * (w.pos + 1) * s["kv_headn"] * D * 4 + (s["q_headn"] * 2 + s["kv_headn"] * 2) * D * 4
     achieved = bytes_launch / (kern_avg_ms * 1e-3) / 1e9
+    other = None
+    if world > 1:  # the other gather, for comparison
+        alt = "nccl" if args.gather == "p2p" else "p2p"
+        other = {"gather": alt, "tokens_s": 1e3 / timed(max(3, args.steps // 2), alt, False)}
 
-    # end to end through the host-pointer C call (pinned host buffers, copies inside the timed region)
+    # end to end through the public API (pinned host buffers, copies inside the timed region)
     e2e = bench_decode_e2e(args, w, h, s, q, k, v, world, local, pg)
     h.close()
     traffic = load_profile_traffic("decode_kernel")
+    per_layer = 2 if (world > 1 and args.gather == "p2p") else 1
     return {
         "value": tok_s, "ms_per_step": ms_per_step, "clocks": clocks,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -299,8 +320,8 @@ def bench_decode(args, w, rank, world, local, pg, peaks):
                      "kernel": "decode_kernel<float,128,4>", "kernel_avg_us": kern_avg_ms * 1e3,
                      "algorithmic_bytes_per_launch": bytes_launch,
                      "peak_source": f"{peaks['source']} hbm_gbs (copy)"},
-        "hbm_gbs_step": w.kv_bytes_per_token() / world * tok_s / 1e9 * world,
-        "e2e": e2e, "gpu_launches": args.steps * L,
+        "hbm_gbs_step": w.kv_bytes_per_token() * tok_s / 1e9,
+        "e2e": e2e, "gpu_launches": args.steps * L * per_layer, "other_gather": other,
     }
 
 
@@ -336,8 +357,12 @@ def bench_decode_e2e(args, w, h, s, q, k, v, world, local, pg):
                 qd.copy_(qh[l], non_blocking=True)
                 kd.copy_(kh[l], non_blocking=True)
                 vd.copy_(vh[l], non_blocking=True)
-                h.decode_async(l, w.pos, qd, kd, vd, od)
-                pg.all_gather_into_tensor(full, od)
+                if args.gather == "p2p":
+                    h.decode_gather_async(l, w.pos, qd, kd, vd)
+                    h.gather_wait_async(l, full)
+                else:
+                    h.decode_async(l, w.pos, qd, kd, vd, od)
+                    pg.all_gather_into_tensor(full, od)
                 outh[l].copy_(full, non_blocking=True)
             torch.cuda.current_stream().synchronize()
         h2d = L * (qh.shape[1] + 2 * kh.shape[1]) * 4
@@ -358,7 +383,8 @@ def bench_decode_e2e(args, w, h, s, q, k, v, world, local, pg):
         el = float(t.item())
     return {"value": steps / el, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "steps": steps, "api": "ligguf_cuda_attn_decode (host pointers)" if world == 1 else
-            "ligguf_cuda_attn_decode_async + NCCL all-gather, pinned host copies"}
+            (f"ligguf_cuda_attn_decode_gather_async + gather_wait_async (NVLink peer stores), pinned host copies"
+             if args.gather == "p2p" else "ligguf_cuda_attn_decode_async + NCCL all-gather, pinned host copies")}
 
 
 # ------------------------------------------------------------------------------ other configurations
@@ -561,13 +587,16 @@ def main():
             "data": "synthetic (seeded generator, ~N(0,1)); random-init QK-norm weights",
             "config": {"workload": WORKLOAD, "layers": w.n_layers, "ctx": w.pos + 1, "kv": "fp32",
                        "heads": [w.n_heads, w.n_kv_heads, w.head_dim],
-                       "parallelism": f"kv-head shards x{world} + NCCL all-gather per layer" if world > 1
-                       else "single GPU",
+                       "parallelism": (f"kv-head shards x{world} + per-layer all-gather of head outputs "
+                                       f"({'decode-kernel NVLink peer stores' if args.gather == 'p2p' else 'NCCL'})")
+                       if world > 1 else "single GPU",
                        "l2": "inputs larger than L2 (KV bytes per step >> 126 MB); no flush"},
             "hbm_gbs": res["hbm_gbs_step"],
             "roofline": res["roofline"], "clocks": res["clocks"], "e2e": res["e2e"],
             "gpu_launches": res["gpu_launches"],
         }
+        if res.get("other_gather"):
+            line["other_gather"] = res["other_gather"]
         if cb is not None:
             line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
         if extra:

@@ -152,6 +152,7 @@ struct ligguf_attn {
     float* kg = nullptr;
     std::vector<uint8_t> norm_set;
     float* part = nullptr;
+    float* gpart = nullptr;
     int* counters = nullptr;
     int* h_err = nullptr;  // mapped pinned word the kernels write on failure
     int* d_err = nullptr;
@@ -273,6 +274,7 @@ int decode_enqueue(ligguf_attn* h, int layer, int pos, const float* dq, const fl
     a.vc = static_cast<char*>(h->vc) + size_t(layer) * h->layer_elems * h->es;
     a.out = dout;
     a.part = h->part;
+    a.gpart = h->gpart;
     a.counters = h->counters;
     a.err = h->d_err;
     a.row0 = layer * c.n_context;
@@ -577,7 +579,7 @@ int ligguf_cuda_attn_free(ligguf_attn* h) {
     if (h->stream) cudaStreamSynchronize(h->stream);
     for (void* p : h->g_opened)
         if (p) cudaIpcCloseMemHandle(p);
-    void* dev_ptrs[] = {h->kc, h->vc, h->freq, h->qg, h->kg, h->part, h->counters, h->d_stage, h->qf, h->qb,
+    void* dev_ptrs[] = {h->kc, h->vc, h->freq, h->qg, h->kg, h->part, h->gpart, h->counters, h->d_stage, h->qf, h->qb,
                         h->kb, h->vb, h->gbuf, h->d_peer_out, h->d_peer_flag};
     for (void* p : dev_ptrs)
         if (p) cudaFree(p);
@@ -653,12 +655,15 @@ int ligguf_cuda_attn_init(const ligguf_attn_cfg* cfg, ligguf_attn** out) {
                                  : powf(c.rope_base, -2.0f * static_cast<float>(i) / static_cast<float>(c.rope_dim));
     const size_t pd = size_t(c.n_layers) * c.head_dim;
     const size_t part_floats = size_t(c.kv_headn) * lg::kDecodeMaxSplit * nrep * (c.head_dim + 2);
+    const size_t gpart_floats = size_t(c.kv_headn) * lg::kDecodeMaxGroups * nrep * (c.head_dim + 2);
+    const size_t n_counters = size_t(c.kv_headn) * (2 + lg::kDecodeMaxGroups);
     if (cudaMalloc(&h->freq, nfreq * 4) != cudaSuccess || cudaMalloc(&h->qg, pd * 4) != cudaSuccess ||
         cudaMalloc(&h->kg, pd * 4) != cudaSuccess || cudaMalloc(&h->part, part_floats * 4) != cudaSuccess ||
-        cudaMalloc(&h->counters, 2 * c.kv_headn * sizeof(int)) != cudaSuccess)
+        cudaMalloc(&h->gpart, gpart_floats * 4) != cudaSuccess ||
+        cudaMalloc(&h->counters, n_counters * sizeof(int)) != cudaSuccess)
         return bail(fail(LIGGUF_ATTN_ENOMEM, "handle buffers"));
     if (cudaMemcpy(h->freq, freq.data(), nfreq * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemset(h->counters, 0, 2 * c.kv_headn * sizeof(int)) != cudaSuccess)
+        cudaMemset(h->counters, 0, n_counters * sizeof(int)) != cudaSuccess)
         return bail(fail(LIGGUF_ATTN_ECUDA, "handle initialisation copies"));
     if (cudaHostAlloc(&h->h_err, 64, cudaHostAllocMapped) != cudaSuccess ||
         cudaHostGetDevicePointer(reinterpret_cast<void**>(&h->d_err), h->h_err, 0) != cudaSuccess)
@@ -707,7 +712,7 @@ int ligguf_cuda_attn_decode(ligguf_attn* h, int layer, int pos, const float* q, 
     if ((rc = decode_enqueue(h, layer, pos, dq, dk, dv, dout, h->stream, false))) return rc;
     LG_CUDA(cudaMemcpyAsync(out, dout, nq * 4, cudaMemcpyDeviceToHost, h->stream));
     LG_CUDA(cudaStreamSynchronize(h->stream));
-    return check_err_word(h->h_err, h->counters, 2 * h->kv_dim / h->cfg.head_dim);
+    return check_err_word(h->h_err, h->counters, (2 + lg::kDecodeMaxGroups) * h->kv_dim / h->cfg.head_dim);
 }
 
 int ligguf_cuda_attn_prefill_async(ligguf_attn* h, int layer, int pos0, int n, const float* d_q, const float* d_k,
@@ -735,7 +740,7 @@ int ligguf_cuda_attn_prefill(ligguf_attn* h, int layer, int pos0, int n, const f
     if ((rc = prefill_enqueue(h, layer, pos0, n, dq, dk, dv, dout, mode, h->stream))) return rc;
     LG_CUDA(cudaMemcpyAsync(out, dout, nq * 4, cudaMemcpyDeviceToHost, h->stream));
     LG_CUDA(cudaStreamSynchronize(h->stream));
-    return check_err_word(h->h_err, h->counters, 2 * h->kv_dim / h->cfg.head_dim);
+    return check_err_word(h->h_err, h->counters, (2 + lg::kDecodeMaxGroups) * h->kv_dim / h->cfg.head_dim);
 }
 
 int ligguf_cuda_attn_kv_download(ligguf_attn* h, int layer, int pos0, int n, void* host_k, void* host_v) {
@@ -805,7 +810,7 @@ int ligguf_cuda_attn_sync(ligguf_attn* h) {
     DeviceGuard dg(h->cfg.device);
     LG_CUDA(cudaStreamSynchronize(h->stream));
     LG_CUDA(cudaDeviceSynchronize());
-    return check_err_word(h->h_err, h->counters, 2 * h->kv_dim / h->cfg.head_dim);
+    return check_err_word(h->h_err, h->counters, (2 + lg::kDecodeMaxGroups) * h->kv_dim / h->cfg.head_dim);
 }
 
 // ---------------------------------------------------------------------------- SARA gather

@@ -34,6 +34,8 @@ constexpr int kDecodeThreads = kDecodeConsumers + 32;
 constexpr int kDecodeStages = 3;
 constexpr int kDecodeTileBytes = 16384;
 constexpr int kDecodeMaxSplit = 1024;
+constexpr int kDecodeMergeGroup = 48;  // split partials merged per first-level merge
+constexpr int kDecodeMaxGroups = 32;   // >= ceil(kDecodeMaxSplit / kDecodeMergeGroup)
 
 struct DecodeArgs {
     const float* q;     // [q_headn][D] raw q of this layer
@@ -46,7 +48,9 @@ struct DecodeArgs {
     void* vc;
     float* out;         // [q_headn][D]
     float* part;        // [kv_headn][kDecodeMaxSplit][nrep*(D+2)] split partials
-    int* counters;      // [kv_headn] tickets, zero between launches
+    float* gpart;       // [kv_headn][kDecodeMaxGroups][nrep*(D+2)] merged group partials
+    int* counters;      // [kv_headn] head tickets, then [kv_headn] grab counters, then
+                        // [kv_headn][kDecodeMaxGroups] group tickets; zero between launches
     int* err;           // error word (mapped host memory)
     float* const* peer_out;  // multi-GPU gather: [nranks] gather buffers (or null)
     int* const* peer_flag;   // [nranks] flag arrays [nranks*kv_headn]
@@ -60,7 +64,7 @@ struct DecodeArgs {
     int n_tiles;        // tiles covering [0, pos)
     int chunk;          // tiles per grab: CTA `split` starts with tiles [split*chunk, +chunk), then takes
                         // further chunks from chunk_ctr[g] (first dynamic chunk = n_split*chunk)
-    int* chunk_ctr;     // [kv_headn] grab counters, zero between launches (reset with the tickets)
+    int* chunk_ctr;     // = counters + kv_headn
     int n_split;
     int kv_dim;
     int rope_pairs;
@@ -267,6 +271,76 @@ __device__ __forceinline__ void transposed_reduce(float (&x)[V], int lane) {
             x[0] += __shfl_xor_sync(0xffffffffu, x[0], o);
         }
     }
+}
+
+// Merges `count` (o, m, l) partials stored at src[i*PS] (PS = NREP*(D+2): o[NREP][D], m[NREP],
+// l[NREP]) into o_s (unnormalised sum of o*e^(m-M)), m_s (M, the maximum) and l_s (sum of
+// l*e^(m-M)).  All consumer threads take part; `scratch` holds 2*kDecodeMaxSplit*NREP floats.  The
+// loads are issued in batches of 24 partials before any is used (this merge is the kernel's tail).
+template <int NREP, int D>
+__device__ __noinline__ void merge_partials(const float* src, int count, float* scratch, float* o_s, float* m_s,
+                                               float* l_s, int tid, int warp, int lane) {
+    constexpr int PS = NREP * (D + 2);
+    constexpr int CPT = (NREP * D + kDecodeConsumers - 1) / kDecodeConsumers;  // columns per thread
+    constexpr int BATCH = 24;  // partials held in registers at once (no spills at nrep 4, D 128)
+    float* m_all = scratch;                         // [count][NREP] maxima
+    float* w_all = scratch + kDecodeMaxSplit * NREP;  // [count][NREP] sums, then weights
+    float acc[CPT][4];
+#pragma unroll
+    for (int c = 0; c < CPT; ++c)
+#pragma unroll
+        for (int u = 0; u < 4; ++u) acc[c][u] = 0.f;
+    for (int s0 = 0; s0 < count; s0 += BATCH) {
+        float v[CPT][BATCH];
+#pragma unroll
+        for (int c = 0; c < CPT; ++c) {
+            const int idx = tid + c * kDecodeConsumers;
+#pragma unroll
+            for (int u = 0; u < BATCH; ++u)
+                v[c][u] = (idx < NREP * D && s0 + u < count) ? __ldcg(src + (s0 + u) * PS + idx) : 0.f;
+        }
+        if (s0 == 0) {
+            for (int i = tid; i < count * NREP; i += kDecodeConsumers) {
+                const int sp = i / NREP, h = i % NREP;
+                m_all[i] = __ldcg(src + sp * PS + NREP * D + h);
+                w_all[i] = __ldcg(src + sp * PS + NREP * D + NREP + h);
+            }
+            named_bar_sync(1, kDecodeConsumers);
+            if (warp < NREP) {
+                const int h = warp;
+                float M = -INFINITY;
+                for (int sp = lane; sp < count; sp += 32) M = fmaxf(M, m_all[sp * NREP + h]);
+                M = warp_max(M);
+                float L = 0.f;
+                for (int sp = lane; sp < count; sp += 32) {
+                    const float mv = m_all[sp * NREP + h];
+                    const float w = mv == -INFINITY ? 0.f : expf(mv - M);
+                    L = fmaf(w_all[sp * NREP + h], w, L);
+                    w_all[sp * NREP + h] = w;
+                }
+                L = warp_sum(L);
+                if (lane == 0) {
+                    m_s[h] = M;
+                    l_s[h] = L;
+                }
+            }
+            named_bar_sync(1, kDecodeConsumers);
+        }
+#pragma unroll
+        for (int c = 0; c < CPT; ++c) {
+            const int idx = tid + c * kDecodeConsumers;
+            const int h = min(idx, NREP * D - 1) / D;
+#pragma unroll
+            for (int u = 0; u < BATCH; ++u)
+                if (s0 + u < count) acc[c][u & 3] = fmaf(v[c][u], w_all[(s0 + u) * NREP + h], acc[c][u & 3]);
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < CPT; ++c) {
+        const int idx = tid + c * kDecodeConsumers;
+        if (idx < NREP * D) o_s[idx] = (acc[c][0] + acc[c][1]) + (acc[c][2] + acc[c][3]);
+    }
+    named_bar_sync(1, kDecodeConsumers);
 }
 
 template <typename KV, int D, int NREP>
@@ -624,18 +698,11 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
     if (*stop_s) return;
 
     const int head0 = g * NREP;
-    if (a.n_split == 1) {
-        for (int idx = tid; idx < NREP * D; idx += kDecodeConsumers) {
-            const int h = idx / D;
-            const float val = o_s[idx] / l_s[h];
-            a.out[static_cast<size_t>(head0) * D + idx] = val;
-            if (a.peer_out) {
-                for (int rr = 0; rr < a.nranks; ++rr)
-                    a.peer_out[rr][a.q_off + head0 * D + idx] = val;
-            }
-        }
-    } else {
+    if (a.n_split > 1) {
+        // Two-level merge: the last CTA of each group of kDecodeMergeGroup splits merges the group,
+        // then (with more than one group) the last group merger merges the group results.
         constexpr int PS = NREP * (D + 2);
+        const int kvh = a.kv_dim / D;
         float* pp = a.part + (static_cast<size_t>(g) * kDecodeMaxSplit + split) * PS;
         for (int idx = tid; idx < NREP * D; idx += kDecodeConsumers) pp[idx] = o_s[idx];
         if (tid < NREP) {
@@ -644,81 +711,43 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
         }
         __threadfence();
         named_bar_sync(1, kDecodeConsumers);
-        if (tid == 0) *last_s = (atomicAdd(&a.counters[g], 1) == a.n_split - 1) ? 1 : 0;
+        const int grp = split / kDecodeMergeGroup;
+        const int n_groups = (a.n_split + kDecodeMergeGroup - 1) / kDecodeMergeGroup;
+        const int gsize = min(kDecodeMergeGroup, a.n_split - grp * kDecodeMergeGroup);
+        int* grp_ctr = a.counters + 2 * kvh + g * kDecodeMaxGroups + grp;
+        if (tid == 0) *last_s = (atomicAdd(grp_ctr, 1) == gsize - 1) ? 1 : 0;
         named_bar_sync(1, kDecodeConsumers);
         if (!*last_s) return;
         __threadfence();
-        // The last CTA of this KV head merges all splits (the tiles are free: alias them).  This
-        // merge is the kernel's tail, so its loads are issued in batches before any is used: the o
-        // columns of up to 24 splits per thread together with the maxima and sums (two round trips
-        // to L2 for the 37 splits of a 148-SM wave).
-        float* m_all = reinterpret_cast<float*>(tiles);  // [n_split][NREP] split maxima
-        float* w_all = m_all + kDecodeMaxSplit * NREP;   // [n_split][NREP] split sums, then weights
-        const float* pg = a.part + static_cast<size_t>(g) * kDecodeMaxSplit * PS;
-        constexpr int CPT = (NREP * D + kDecodeConsumers - 1) / kDecodeConsumers;  // columns per thread
-        constexpr int BATCH = 24;  // splits held in registers at once (no spills at nrep 4, D 128)
-        float acc[CPT][4];
-#pragma unroll
-        for (int c = 0; c < CPT; ++c)
-#pragma unroll
-            for (int u = 0; u < 4; ++u) acc[c][u] = 0.f;
-        for (int s0 = 0; s0 < a.n_split; s0 += BATCH) {
-            float v[CPT][BATCH];
-#pragma unroll
-            for (int c = 0; c < CPT; ++c) {
-                const int idx = tid + c * kDecodeConsumers;
-#pragma unroll
-                for (int u = 0; u < BATCH; ++u)
-                    v[c][u] = (idx < NREP * D && s0 + u < a.n_split) ? __ldcg(pg + (s0 + u) * PS + idx) : 0.f;
+        float* scratch = reinterpret_cast<float*>(tiles);  // the tiles are free: alias them
+        merge_partials<NREP, D>(a.part + (static_cast<size_t>(g) * kDecodeMaxSplit + grp * kDecodeMergeGroup) * PS,
+                                gsize, scratch, o_s, m_s, l_s, tid, warp, lane);
+        if (tid == 0) *grp_ctr = 0;
+        if (n_groups > 1) {
+            float* gp = a.gpart + (static_cast<size_t>(g) * kDecodeMaxGroups + grp) * PS;
+            for (int idx = tid; idx < NREP * D; idx += kDecodeConsumers) gp[idx] = o_s[idx];
+            if (tid < NREP) {
+                gp[NREP * D + tid] = m_s[tid];
+                gp[NREP * D + NREP + tid] = l_s[tid];
             }
-            if (s0 == 0) {
-                for (int i = tid; i < a.n_split * NREP; i += kDecodeConsumers) {
-                    const int sp = i / NREP, h = i % NREP;
-                    m_all[i] = __ldcg(pg + sp * PS + NREP * D + h);
-                    w_all[i] = __ldcg(pg + sp * PS + NREP * D + NREP + h);
-                }
-                named_bar_sync(1, kDecodeConsumers);
-                if (warp < NREP) {
-                    const int h = warp;
-                    float M = -INFINITY;
-                    for (int sp = lane; sp < a.n_split; sp += 32) M = fmaxf(M, m_all[sp * NREP + h]);
-                    M = warp_max(M);
-                    float L = 0.f;
-                    for (int sp = lane; sp < a.n_split; sp += 32) {
-                        const float w = expf(m_all[sp * NREP + h] - M);
-                        L = fmaf(w_all[sp * NREP + h], w, L);
-                        w_all[sp * NREP + h] = w;
-                    }
-                    L = warp_sum(L);
-                    if (lane == 0) l_s[h] = L;
-                }
-                named_bar_sync(1, kDecodeConsumers);
-            }
-#pragma unroll
-            for (int c = 0; c < CPT; ++c) {
-                const int idx = tid + c * kDecodeConsumers;
-                const int h = min(idx, NREP * D - 1) / D;
-#pragma unroll
-                for (int u = 0; u < BATCH; ++u)
-                    if (s0 + u < a.n_split) acc[c][u & 3] = fmaf(v[c][u], w_all[(s0 + u) * NREP + h], acc[c][u & 3]);
-            }
+            __threadfence();
+            named_bar_sync(1, kDecodeConsumers);
+            if (tid == 0) *last_s = (atomicAdd(&a.counters[g], 1) == n_groups - 1) ? 1 : 0;
+            named_bar_sync(1, kDecodeConsumers);
+            if (!*last_s) return;
+            __threadfence();
+            merge_partials<NREP, D>(a.gpart + static_cast<size_t>(g) * kDecodeMaxGroups * PS, n_groups, scratch,
+                                    o_s, m_s, l_s, tid, warp, lane);
+            if (tid == 0) a.counters[g] = 0;
         }
-#pragma unroll
-        for (int c = 0; c < CPT; ++c) {
-            const int idx = tid + c * kDecodeConsumers;
-            if (idx < NREP * D) {
-                const int h = idx / D;
-                const float val = ((acc[c][0] + acc[c][1]) + (acc[c][2] + acc[c][3])) / l_s[h];
-                a.out[static_cast<size_t>(head0) * D + idx] = val;
-                if (a.peer_out) {
-                    for (int rr = 0; rr < a.nranks; ++rr)
-                        a.peer_out[rr][a.q_off + head0 * D + idx] = val;
-                }
-            }
-        }
-        if (tid == 0) {  // every CTA of this head took its ticket after its last grab: reset both
-            a.counters[g] = 0;
-            a.chunk_ctr[g] = 0;
+        // Every CTA of this head took its group ticket after its last grab: the counter is free.
+        if (tid == 0) a.chunk_ctr[g] = 0;
+    }
+    for (int idx = tid; idx < NREP * D; idx += kDecodeConsumers) {
+        const float val = o_s[idx] / l_s[idx / D];
+        a.out[static_cast<size_t>(head0) * D + idx] = val;
+        if (a.peer_out) {
+            for (int rr = 0; rr < a.nranks; ++rr) a.peer_out[rr][a.q_off + head0 * D + idx] = val;
         }
     }
     if (a.peer_out) {
