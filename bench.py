@@ -38,7 +38,7 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extra", action="store_true", help="skip the other configurations at N=1")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    ap.add_argument("--gather", choices=["p2p", "nccl"], default="p2p",
+    ap.add_argument("--gather", choices=["p2p", "nccl"], default="nccl",
                     help="N>1: all-gather of head outputs by the decode kernel's peer stores (p2p) or NCCL")
     ap.add_argument("--case", choices=["decode-layer", "prefill-layer", "bert-layer"], default=None,
                     help="run one small case a few times and exit (the command the ncu summaries use)")
