@@ -360,12 +360,12 @@ int grow(T** p, size_t* cap, size_t need) {
 }
 
 // ---------------------------------------------------------------------------- tensor-core launch
-int make_bf16_tmap(CUtensorMap* m, const void* base, int D, int heads, int rows) {
+int make_bf16_tmap(CUtensorMap* m, const void* base, int D, int heads, int rows, int box_rows) {
     auto enc = tensor_map_encoder();
     if (!enc) return fail(LIGGUF_ATTN_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
     cuuint64_t dims[3] = {cuuint64_t(D), cuuint64_t(heads), cuuint64_t(rows)};
     cuuint64_t strides[2] = {cuuint64_t(D) * 2, cuuint64_t(heads) * D * 2};
-    cuuint32_t box[3] = {64u, 1u, cuuint32_t(lg::kTcRows)};
+    cuuint32_t box[3] = {64u, 1u, cuuint32_t(box_rows)};
     cuuint32_t estr[3] = {1u, 1u, 1u};
     const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -378,9 +378,9 @@ template <int D>
 int launch_flash_tc_t(const lg::TcArgs& t, cudaStream_t st, int device) {
     alignas(64) CUtensorMap tq, tk, tv;
     int rc;
-    if ((rc = make_bf16_tmap(&tq, t.q, D, t.q_heads, t.q_rows))) return rc;
-    if ((rc = make_bf16_tmap(&tk, t.k, D, t.kv_heads, t.kv_rows))) return rc;
-    if ((rc = make_bf16_tmap(&tv, t.v, D, t.kv_heads, t.kv_rows))) return rc;
+    if ((rc = make_bf16_tmap(&tq, t.q, D, t.q_heads, t.q_rows, lg::kTcRows))) return rc;
+    if ((rc = make_bf16_tmap(&tk, t.k, D, t.kv_heads, t.kv_rows, lg::kTcKeys))) return rc;
+    if ((rc = make_bf16_tmap(&tv, t.v, D, t.kv_heads, t.kv_rows, lg::kTcKeys))) return rc;
     auto kern = lg::flash_tc_kernel<D>;
     static bool attr_done[64] = {};
     LG_CUDA(ensure_smem_attr(kern, device, lg::TcSmem<D>::kTotal, attr_done));

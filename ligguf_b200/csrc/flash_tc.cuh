@@ -4,17 +4,20 @@
 // fast/ligguf_fast_qk.cpp:340-356; BERT = fast/vdb.cpp:189-212 per sequence), with q, k, v rounded
 // to bf16 and every product accumulated in fp32 by the tensor cores.
 //
-// CTA = 128 query rows of one q head (of one batch entry), 192 threads:
-//   warp 0      TMA producer: Q tile once, then K and V tiles (128 keys each) into a ring
-//   warp 1      allocates 512 TMEM columns; lane 0 issues every tcgen05.mma and commit
+// CTA = 128 query rows of one q head (of one batch entry), 192 threads, two CTAs per SM (96 KB of
+// shared memory and 256 TMEM columns each) so that one CTA's MMAs run while the other's softmax
+// warps work:
+//   warp 0      TMA producer: Q tile once, then K and V tiles (64 keys each) into 2-stage rings
+//   warp 1      allocates 256 TMEM columns; lane 0 issues every tcgen05.mma and commit
 //   warps 2..5  softmax: thread = query row = TMEM lane; reads S from TMEM, online softmax with
-//               exp2, writes P (bf16) into shared memory in the 128B-swizzled K-major layout,
-//               rescales O in TMEM when the running max moves; final O / l to global memory.
-// TMEM: S double buffer at columns [0,128) and [128,256), O at [256, 256+D).
-// MMA order S0, S1, PV0, S2, PV1, ... so that S(j+1) runs on the tensor cores while the softmax
-// warps work on S(j).  Operands: Q, K K-major (SWIZZLE_128B), V MN-major (SWIZZLE_128B), P K-major.
-// Every wait is bounded; on a timeout the kernel records an error, drains its own copies and MMAs,
-// frees TMEM and returns.
+//               exp2, writes P as bf16 pairs back into the same TMEM columns, rescales O in TMEM
+//               when the running max moves; final O / l to global memory.
+// TMEM: S double buffer at columns [0,64) and [64,128) (P of a tile overwrites the first 32 columns
+// of its S buffer), O at [128, 128+D).  MMA order S0, S1, PV0, S2, PV1, ...: S = Q.K^T with both
+// operands in shared memory (K-major, SWIZZLE_128B); O += P.V with P read from TMEM and V from
+// shared memory (MN-major, SWIZZLE_128B).  MMAs of one CTA execute in issue order, so PV(j) has read
+// P(j) before S(j+2) overwrites that buffer.  Every wait is bounded; on a timeout the kernel records
+// an error, drains its own copies and MMAs, frees TMEM and returns.
 #pragma once
 
 #include "common.cuh"
@@ -40,21 +43,25 @@ __global__ void to_bf16_kernel(const float* __restrict__ src, __nv_bfloat16* __r
 }
 
 constexpr int kTcRows = 128;  // query rows per tile (UMMA M)
-constexpr int kTcKeys = 128;  // keys per tile (UMMA N of S, K of P.V)
+constexpr int kTcKeys = 64;   // keys per tile (UMMA N of S, K of P.V)
 constexpr int kTcThreads = 192;
-constexpr uint32_t kTcTmemCols = 512;
+constexpr uint32_t kTcTmemCols = 256;
+constexpr uint32_t kTcTmemO = 128;  // first TMEM column of O
 
 template <int D>
 struct TcSmem {
-    static constexpr int kChunks = D / 64;                // 128-byte column chunks of a row
-    static constexpr int kTileBytes = kTcRows * D * 2;    // 128 rows of bf16
-    static constexpr int kChunkBytes = kTcRows * 128;     // one 128-byte-wide chunk of 128 rows
-    static constexpr int kStages = D == 128 ? 2 : 3;
+    static constexpr int kChunks = D / 64;               // 128-byte column chunks of a row
+    static constexpr int kQBytes = kTcRows * D * 2;      // the Q tile: 128 rows of bf16
+    static constexpr int kQChunkBytes = kTcRows * 128;   // one 128-byte-wide chunk of Q
+    static constexpr int kKvBytes = kTcKeys * D * 2;     // a K or V tile: 64 rows of bf16
+    static constexpr int kKvChunkBytes = kTcKeys * 128;  // one 128-byte-wide chunk of a K/V tile
+    // D = 64 takes 4 stages: besides the deeper ring, 80 KB keeps a third CTA (whose TMEM allocation
+    // would have to wait for one of the two resident CTAs to finish) off the SM.
+    static constexpr int kStages = D == 128 ? 2 : 4;
     static constexpr size_t kQ = 0;
-    static constexpr size_t kK = kQ + kTileBytes;
-    static constexpr size_t kV = kK + size_t(kStages) * kTileBytes;
-    static constexpr size_t kP = kV + size_t(kStages) * kTileBytes;
-    static constexpr size_t kBar = kP + size_t(kTcRows) * kTcKeys * 2;
+    static constexpr size_t kK = kQ + kQBytes;
+    static constexpr size_t kV = kK + size_t(kStages) * kKvBytes;
+    static constexpr size_t kBar = kV + size_t(kStages) * kKvBytes;
     // q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], s_free[2], p_full, o_done, drain
     static constexpr int kNumBars = 1 + 4 * kStages + 2 + 2 + 1 + 1 + 1;
     static constexpr size_t kMisc = kBar + size_t(kNumBars) * 8;  // tmem base, abort flag
@@ -82,6 +89,16 @@ __device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t adesc, uint64_
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// D[tmem] (+)= A[tmem] * B[smem desc]: A (M x 16, bf16 pairs packed in 32-bit columns) from TMEM.
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 // Arrives once on `bar` when every tcgen05 operation this thread issued so far has completed.
@@ -167,7 +184,7 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, uint64_t
 }
 
 template <int D>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(kTcThreads, 2)
     flash_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const TcArgs a) {
     using Sm = TcSmem<D>;
@@ -238,30 +255,30 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t tmem_s0 = tmem, tmem_o = tmem + 256;
+    const uint32_t tmem_s0 = tmem, tmem_o = tmem + kTcTmemO;
 
     if (warp == 0) {
         // ------------------------------------------------------------------ TMA producer
         if (lane == 0) {
             int issued = 0;
-            mbar_arrive_expect_tx(q_full, Sm::kTileBytes);
+            mbar_arrive_expect_tx(q_full, Sm::kQBytes);
             for (int c = 0; c < NCH; ++c)
-                tma_load_3d(sm + Sm::kQ + c * Sm::kChunkBytes, &tm_q, q_full, 64 * c, h, q_row0);
+                tma_load_3d(sm + Sm::kQ + c * Sm::kQChunkBytes, &tm_q, q_full, 64 * c, h, q_row0);
             for (int j = 0; j < n_kv; ++j) {
                 const int s = j % S;
                 const uint32_t par = ((j / S) - 1) & 1;
                 if (j >= S && !tc_wait(&k_empty[s], par, deadline, abort, a.err, KERR_TIMEOUT_EMPTY)) break;
-                mbar_arrive_expect_tx(&k_full[s], Sm::kTileBytes);
+                mbar_arrive_expect_tx(&k_full[s], Sm::kKvBytes);
                 for (int c = 0; c < NCH; ++c)
-                    tma_load_3d(sm + Sm::kK + s * Sm::kTileBytes + c * Sm::kChunkBytes, &tm_k, &k_full[s], 64 * c,
+                    tma_load_3d(sm + Sm::kK + s * Sm::kKvBytes + c * Sm::kKvChunkBytes, &tm_k, &k_full[s], 64 * c,
                                 g, kv_row0 + j * kTcKeys);
                 if (j >= S && !tc_wait(&v_empty[s], par, deadline, abort, a.err, KERR_TIMEOUT_EMPTY)) {
                     ++issued;  // the K half of this stage is in flight
                     break;
                 }
-                mbar_arrive_expect_tx(&v_full[s], Sm::kTileBytes);
+                mbar_arrive_expect_tx(&v_full[s], Sm::kKvBytes);
                 for (int c = 0; c < NCH; ++c)
-                    tma_load_3d(sm + Sm::kV + s * Sm::kTileBytes + c * Sm::kChunkBytes, &tm_v, &v_full[s], 64 * c,
+                    tma_load_3d(sm + Sm::kV + s * Sm::kKvBytes + c * Sm::kKvChunkBytes, &tm_v, &v_full[s], 64 * c,
                                 g, kv_row0 + j * kTcKeys);
                 ++issued;
             }
@@ -286,18 +303,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const uint32_t q_base = smem_u32(sm + Sm::kQ);
             const uint32_t k_base = smem_u32(sm + Sm::kK);
             const uint32_t v_base = smem_u32(sm + Sm::kV);
-            const uint32_t p_base = smem_u32(sm + Sm::kP);
             bool ok = tc_wait(q_full, 0, deadline, abort, a.err, KERR_TIMEOUT_FULL);
             auto issue_pv = [&](int i) -> bool {
                 const int s = i % S;
                 if (!tc_wait(p_full, i & 1, deadline, abort, a.err, KERR_TIMEOUT_MMA)) return false;
                 if (!tc_wait(&v_full[s], (i / S) & 1, deadline, abort, a.err, KERR_TIMEOUT_FULL)) return false;
                 tc_fence_after();
+                const uint32_t p_tmem = tmem_s0 + (i & 1) * kTcKeys;  // P(i) packed in its S buffer
 #pragma unroll
                 for (int kk = 0; kk < kTcKeys / 16; ++kk) {
-                    const uint64_t ad = smem_desc_sw128(p_base + (kk >> 2) * (kTcRows * 128) + (kk & 3) * 32, 16, 1024);
-                    const uint64_t bd = smem_desc_sw128(v_base + s * Sm::kTileBytes + kk * 2048, Sm::kChunkBytes, 1024);
-                    umma_ss(tmem_o, ad, bd, kIdO, (i > 0 || kk > 0) ? 1u : 0u);
+                    const uint64_t bd = smem_desc_sw128(v_base + s * Sm::kKvBytes + kk * 2048, Sm::kKvChunkBytes, 1024);
+                    umma_ts(tmem_o, p_tmem + kk * 8, bd, kIdO, (i > 0 || kk > 0) ? 1u : 0u);
                 }
                 umma_commit(o_done);
                 umma_commit(&v_empty[s]);
@@ -311,9 +327,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 tc_fence_after();
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint32_t off = (kk >> 2) * Sm::kChunkBytes + (kk & 3) * 32;
-                    umma_ss(tmem_s0 + bf * kTcKeys, smem_desc_sw128(q_base + off, 16, 1024),
-                            smem_desc_sw128(k_base + s * Sm::kTileBytes + off, 16, 1024), kIdS, kk > 0 ? 1u : 0u);
+                    const uint32_t qoff = (kk >> 2) * Sm::kQChunkBytes + (kk & 3) * 32;
+                    const uint32_t koff = s * Sm::kKvBytes + (kk >> 2) * Sm::kKvChunkBytes + (kk & 3) * 32;
+                    umma_ss(tmem_s0 + bf * kTcKeys, smem_desc_sw128(q_base + qoff, 16, 1024),
+                            smem_desc_sw128(k_base + koff, 16, 1024), kIdS, kk > 0 ? 1u : 0u);
                 }
                 umma_commit(&s_full[bf]);
                 umma_commit(&k_empty[s]);
@@ -336,7 +353,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int qr = r0 + row;                       // query row within the sequence
         const bool row_valid = qr < nq_valid;
         const uint32_t lane_off = uint32_t(quarter * 32) << 16;
-        const uint32_t p_row = smem_u32(sm + Sm::kP) + row * 128;
         const float c2 = a.scale_log2;
         float m = -INFINITY, l = 0.f;
         bool ok = true;
@@ -367,7 +383,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
                 for (int c = 0; c < kTcKeys; ++c) sv[c] = (c < lim_c && c <= lim_r) ? sv[c] : -INFINITY;
             }
-            // Row max and sum with 8 independent chains (a single chain serialises 128 dependent ops).
+            // Row max and sum with 8 independent chains (a single chain serialises 64 dependent ops).
             float mx8[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u) mx8[u] = sv[u];
@@ -410,17 +426,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     tmem_wait_st();
                 }
             }
-            // P row -> shared memory, K-major SWIZZLE_128B: 16-byte unit u of chunk ch at
-            // chunk + row*128 + ((u ^ (row & 7)) * 16).
+            // P row -> TMEM over the S buffer just read: column c holds keys (2c, 2c+1) as bf16, the
+            // lower key in the low half (the A-operand layout of a TMEM-sourced kind::f16 MMA).
 #pragma unroll
-            for (int ch = 0; ch < 2; ++ch)
-#pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    const float* pv = sv + ch * 64 + u * 8;
-                    sts128(p_row + ch * (kTcRows * 128) + ((u ^ (row & 7)) << 4), pack_bf16(pv[0], pv[1]),
-                           pack_bf16(pv[2], pv[3]), pack_bf16(pv[4], pv[5]), pack_bf16(pv[6], pv[7]));
-                }
-            fence_proxy_async_smem();
+            for (int c = 0; c < kTcKeys / 2; ++c) x[c] = pack_bf16(sv[2 * c], sv[2 * c + 1]);
+            tmem_st32(tmem_s0 + bf * kTcKeys + lane_off, x);
+            tmem_wait_st();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(p_full);
