@@ -113,6 +113,9 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
     return uint64_t((saddr >> 4) & 0x3FFFu) | (uint64_t((lbo >> 4) & 0x3FFFu) << 16) |
            (uint64_t((sbo >> 4) & 0x3FFFu) << 32) | (uint64_t(1) << 46) | (uint64_t(2) << 61);
 }
+// The same descriptor `bytes` further on: the start address is the low 14-bit field (address >> 4),
+// and shared-memory addresses stay below 2^18, so the add never carries out of the field.
+__device__ __forceinline__ uint64_t desc_advance(uint64_t desc, uint32_t bytes) { return desc + (bytes >> 4); }
 // Instruction descriptor, kind::f16: bf16 A and B, fp32 accumulator, M x N, majors (0 K, 1 MN).
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, int a_mn, int b_mn) {
     return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(a_mn) << 15) | (uint32_t(b_mn) << 16) |
@@ -300,9 +303,11 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         if (lane == 0) {
             constexpr uint32_t kIdS = idesc_bf16(kTcRows, kTcKeys, 0, 0);
             constexpr uint32_t kIdO = idesc_bf16(kTcRows, D, 0, 1);
-            const uint32_t q_base = smem_u32(sm + Sm::kQ);
-            const uint32_t k_base = smem_u32(sm + Sm::kK);
-            const uint32_t v_base = smem_u32(sm + Sm::kV);
+            // Descriptors are built once and advanced by constant offsets: a single issuing thread
+            // pays the latency of every instruction between two MMAs.
+            const uint64_t q_desc = smem_desc_sw128(smem_u32(sm + Sm::kQ), 16, 1024);
+            const uint64_t k_desc = smem_desc_sw128(smem_u32(sm + Sm::kK), 16, 1024);
+            const uint64_t v_desc = smem_desc_sw128(smem_u32(sm + Sm::kV), Sm::kKvChunkBytes, 1024);
             bool ok = tc_wait(q_full, 0, deadline, abort, a.err, KERR_TIMEOUT_FULL);
             auto issue_pv = [&](int i) -> bool {
                 const int s = i % S;
@@ -310,11 +315,11 @@ __global__ void __launch_bounds__(kTcThreads, 2)
                 if (!tc_wait(&v_full[s], (i / S) & 1, deadline, abort, a.err, KERR_TIMEOUT_FULL)) return false;
                 tc_fence_after();
                 const uint32_t p_tmem = tmem_s0 + (i & 1) * kTcKeys;  // P(i) packed in its S buffer
+                const uint64_t vd = desc_advance(v_desc, s * Sm::kKvBytes);
+                umma_ts(tmem_o, p_tmem, vd, kIdO, i > 0 ? 1u : 0u);
 #pragma unroll
-                for (int kk = 0; kk < kTcKeys / 16; ++kk) {
-                    const uint64_t bd = smem_desc_sw128(v_base + s * Sm::kKvBytes + kk * 2048, Sm::kKvChunkBytes, 1024);
-                    umma_ts(tmem_o, p_tmem + kk * 8, bd, kIdO, (i > 0 || kk > 0) ? 1u : 0u);
-                }
+                for (int kk = 1; kk < kTcKeys / 16; ++kk)
+                    umma_ts(tmem_o, p_tmem + kk * 8, desc_advance(vd, kk * 2048), kIdO, 1u);
                 umma_commit(o_done);
                 umma_commit(&v_empty[s]);
                 return true;
@@ -325,12 +330,13 @@ __global__ void __launch_bounds__(kTcThreads, 2)
                 if (j >= 2 && !tc_wait(&s_free[bf], ((j >> 1) - 1) & 1, deadline, abort, a.err, KERR_TIMEOUT_MMA))
                     break;
                 tc_fence_after();
+                const uint64_t kd = desc_advance(k_desc, s * Sm::kKvBytes);
+                const uint32_t d_tmem = tmem_s0 + bf * kTcKeys;
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
                     const uint32_t qoff = (kk >> 2) * Sm::kQChunkBytes + (kk & 3) * 32;
-                    const uint32_t koff = s * Sm::kKvBytes + (kk >> 2) * Sm::kKvChunkBytes + (kk & 3) * 32;
-                    umma_ss(tmem_s0 + bf * kTcKeys, smem_desc_sw128(q_base + qoff, 16, 1024),
-                            smem_desc_sw128(k_base + koff, 16, 1024), kIdS, kk > 0 ? 1u : 0u);
+                    const uint32_t koff = (kk >> 2) * Sm::kKvChunkBytes + (kk & 3) * 32;
+                    umma_ss(d_tmem, desc_advance(q_desc, qoff), desc_advance(kd, koff), kIdS, kk > 0 ? 1u : 0u);
                 }
                 umma_commit(&s_full[bf]);
                 umma_commit(&k_empty[s]);
