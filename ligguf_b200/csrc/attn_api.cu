@@ -335,7 +335,8 @@ int launch_flash_simt(const lg::FlashArgs& f, int D, dim3 grid, cudaStream_t st,
 
 template <typename KV, int D>
 int launch_prep_t(const lg::PrepArgs& p, cudaStream_t st) {
-    lg::prefill_prep_kernel<KV, D><<<p.n, 256, 0, st>>>(p);
+    const dim3 grid(p.n, ceil_div(p.q_headn + 2 * p.kv_headn, lg::kPrepWarps));
+    lg::prefill_prep_kernel<KV, D><<<grid, lg::kPrepWarps * 32, 0, st>>>(p);
     LG_CUDA(cudaGetLastError());
     return LIGGUF_ATTN_OK;
 }
@@ -939,6 +940,16 @@ int ligguf_cuda_bert_init(int n_heads, int head_dim, int max_batch, int max_len,
     return LIGGUF_ATTN_OK;
 }
 
+// q, k, v (fp32, [batch][max_len][E]) to the bf16 operands of the tensor-core path, valid rows only
+// (one pass; padded v rows zeroed).  E is n_heads * head_dim, a multiple of 64.
+static cudaError_t bert_convert(const float* q, const float* k, const float* v, const int* lens, int batch,
+                               int max_len, int E, __nv_bfloat16* bq, __nv_bfloat16* bk, __nv_bfloat16* bv,
+                               cudaStream_t st) {
+    const dim3 grid(ceil_div(max_len, lg::kBertConvRows), batch);
+    lg::bert_to_bf16_kernel<<<grid, 256, 0, st>>>(q, k, v, lens, max_len, E, bq, bk, bv);
+    return cudaGetLastError();
+}
+
 int ligguf_cuda_bert_attn_async(ligguf_bert_attn* b, int batch, int max_len, const int* d_lens, const float* d_q,
                                 const float* d_k, const float* d_v, float* d_out, int mode, void* stream) {
     if (!b || !d_lens || !d_q || !d_k || !d_v || !d_out) return fail(LIGGUF_ATTN_EINVAL, "null argument");
@@ -982,12 +993,7 @@ int ligguf_cuda_bert_attn_async(ligguf_bert_attn* b, int batch, int max_len, con
     t.q = b->bf;
     t.k = b->bf + elems;
     t.v = b->bf + 2 * elems;
-    int threads = 256;
-    const int blocks = std::min(1184, std::max(1, ceil_div(elems, threads)));
-    lg::to_bf16_kernel<<<blocks, threads, 0, st>>>(d_q, b->bf, elems);
-    lg::to_bf16_kernel<<<blocks, threads, 0, st>>>(d_k, b->bf + elems, elems);
-    lg::to_bf16_kernel<<<blocks, threads, 0, st>>>(d_v, b->bf + 2 * elems, elems);
-    LG_CUDA(cudaGetLastError());
+    LG_CUDA(bert_convert(d_q, d_k, d_v, d_lens, batch, max_len, E, b->bf, b->bf + elems, b->bf + 2 * elems, st));
     t.out = d_out;
     t.q_rows = batch * max_len;
     t.q_heads = b->n_heads;
@@ -1059,11 +1065,7 @@ int ligguf_cuda_bert_attn_tc_noalloc(int n_heads, int head_dim, int batch, int m
     int* err = reinterpret_cast<int*>(base + 3 * kNoallocOperandBytes);
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     LG_CUDA(cudaMemsetAsync(err, 0, sizeof(int), st));  // the previous call's error word must not leak
-    const int blocks = std::min(1184, std::max(1, ceil_div(elems, 256)));
-    lg::to_bf16_kernel<<<blocks, 256, 0, st>>>(d_q, bq, elems);
-    lg::to_bf16_kernel<<<blocks, 256, 0, st>>>(d_k, bk, elems);
-    lg::to_bf16_kernel<<<blocks, 256, 0, st>>>(d_v, bv, elems);
-    LG_CUDA(cudaGetLastError());
+    LG_CUDA(bert_convert(d_q, d_k, d_v, d_lens, batch, max_len, n_heads * head_dim, bq, bk, bv, st));
     lg::TcArgs t = {};
     t.q = bq;
     t.k = bk;

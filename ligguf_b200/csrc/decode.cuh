@@ -150,14 +150,10 @@ __device__ __forceinline__ void norm_rope_head(const float* __restrict__ src,
 // Same as norm_rope_head with the rotation taken from per-position tables cs/sn[rope_pairs]
 // (shared by every head of one token).
 template <int D>
-__device__ __forceinline__ void norm_rope_head_tab(const float* __restrict__ src,
-                                                   const float* __restrict__ gamma, int norm, float eps,
-                                                   const float* cs, const float* sn, int rope_pairs,
-                                                   float* dst, int lane) {
+__device__ __forceinline__ void norm_rope_regs(float2 (&x)[D / 64], const float* __restrict__ gamma, int norm,
+                                               float eps, const float* cs, const float* sn, int rope_pairs,
+                                               int lane) {
     constexpr int kPairs = D / 64;
-    float2 x[kPairs];
-#pragma unroll
-    for (int u = 0; u < kPairs; ++u) x[u] = reinterpret_cast<const float2*>(src)[lane + 32 * u];
     if (norm) {
         float ss = 0.f;
 #pragma unroll
@@ -184,6 +180,19 @@ __device__ __forceinline__ void norm_rope_head_tab(const float* __restrict__ src
             x[u].y = x0 * sn_ + x1 * c;
         }
     }
+}
+// One head (D floats at src): optional RMS norm with gamma, then RoPE from a cos/sin table; lane
+// holds pairs m = lane + 32 u (elements 2m, 2m+1).  Result to dst.
+template <int D>
+__device__ __forceinline__ void norm_rope_head_tab(const float* __restrict__ src,
+                                                   const float* __restrict__ gamma, int norm, float eps,
+                                                   const float* cs, const float* sn, int rope_pairs,
+                                                   float* dst, int lane) {
+    constexpr int kPairs = D / 64;
+    float2 x[kPairs];
+#pragma unroll
+    for (int u = 0; u < kPairs; ++u) x[u] = reinterpret_cast<const float2*>(src)[lane + 32 * u];
+    norm_rope_regs<D>(x, gamma, norm, eps, cs, sn, rope_pairs, lane);
 #pragma unroll
     for (int u = 0; u < kPairs; ++u) reinterpret_cast<float2*>(dst)[lane + 32 * u] = x[u];
 }

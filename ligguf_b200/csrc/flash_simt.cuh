@@ -243,9 +243,31 @@ struct PrepArgs {
     float eps;
 };
 
+// Two consecutive elements to a cache row of type KV (one 8- or 4-byte store).
+template <typename KV>
+__device__ __forceinline__ void store_pair(KV* p, float x, float y) {
+    if constexpr (sizeof(KV) == 4) {
+        *reinterpret_cast<float2*>(p) = make_float2(x, y);
+    } else {
+        const KV lo = KvTraits<KV>::from_float(x), hi = KvTraits<KV>::from_float(y);
+        const uint32_t w = uint32_t(*reinterpret_cast<const uint16_t*>(&lo)) |
+                           (uint32_t(*reinterpret_cast<const uint16_t*>(&hi)) << 16);
+        *reinterpret_cast<uint32_t*>(p) = w;
+    }
+}
+__device__ __forceinline__ void store_pair_bf16(__nv_bfloat16* p, float x, float y) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(x, y);
+    *reinterpret_cast<__nv_bfloat162*>(p) = v;
+}
+
+// Prompt rows before attention: per token, the q heads (norm + RoPE; fp32 and/or bf16 out), the k
+// heads (norm + RoPE) and the v heads into this layer's cache rows (and their bf16 shadow).  One warp
+// per head: block (token, group of kPrepWarps heads), the token's cos/sin table in shared memory; each
+// lane holds element pairs (2m, 2m+1), m = lane + 32 u, loaded and stored 8 bytes at a time.
+constexpr int kPrepWarps = 16;
 template <typename KV, int D>
-__global__ void __launch_bounds__(256) prefill_prep_kernel(const PrepArgs a) {
-    __shared__ float rowbuf[8][D];
+__global__ void __launch_bounds__(kPrepWarps * 32) prefill_prep_kernel(const PrepArgs a) {
+    constexpr int kPairs = D / 64;
     __shared__ float cs[D / 2], sn[D / 2];  // RoPE rotation of this token, shared by all heads
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int i = blockIdx.x;
@@ -253,37 +275,36 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const PrepArgs a) {
     for (int m = threadIdx.x; m < a.rope_pairs; m += blockDim.x)
         sincosf(static_cast<float>(pos) * a.freq[m], &sn[m], &cs[m]);
     __syncthreads();
-    const int jobs = a.q_headn + 2 * a.kv_headn;
-    float* buf = rowbuf[warp];
-    for (int job = warp; job < jobs; job += 8) {
-        if (job < a.q_headn) {
-            norm_rope_head_tab<D>(a.q + (static_cast<size_t>(i) * a.q_headn + job) * D, a.qg, a.qk_norm,
-                                  a.eps, cs, sn, a.rope_pairs, buf, lane);
-            __syncwarp();
-            const size_t o = (static_cast<size_t>(i) * a.q_headn + job) * D;
-            for (int d = lane; d < D; d += 32) {
-                if (a.qf) a.qf[o + d] = buf[d];
-                if (a.qb) a.qb[o + d] = __float2bfloat16_rn(buf[d]);
-            }
-        } else {
-            const bool is_k = job < a.q_headn + a.kv_headn;
-            const int gi = is_k ? job - a.q_headn : job - a.q_headn - a.kv_headn;
-            const float* src = (is_k ? a.k : a.v) + (static_cast<size_t>(i) * a.kv_headn + gi) * D;
-            if (is_k) {
-                norm_rope_head_tab<D>(src, a.kg, a.qk_norm, a.eps, cs, sn, a.rope_pairs, buf, lane);
-            } else {
-                for (int d = lane; d < D; d += 32) buf[d] = src[d];
-            }
-            __syncwarp();
-            const size_t o = static_cast<size_t>(pos) * a.kv_dim + static_cast<size_t>(gi) * D;
-            KV* cache = reinterpret_cast<KV*>(is_k ? a.kc : a.vc);
-            __nv_bfloat16* shadow = is_k ? a.kb : a.vb;
-            for (int d = lane; d < D; d += 32) {
-                cache[o + d] = KvTraits<KV>::from_float(buf[d]);
-                if (shadow) shadow[o + d] = __float2bfloat16_rn(buf[d]);
-            }
+    const int job = blockIdx.y * kPrepWarps + warp;
+    if (job >= a.q_headn + 2 * a.kv_headn) return;
+    float2 x[kPairs];
+    if (job < a.q_headn) {
+        const size_t o = (static_cast<size_t>(i) * a.q_headn + job) * D;
+#pragma unroll
+        for (int u = 0; u < kPairs; ++u) x[u] = reinterpret_cast<const float2*>(a.q + o)[lane + 32 * u];
+        norm_rope_regs<D>(x, a.qg, a.qk_norm, a.eps, cs, sn, a.rope_pairs, lane);
+#pragma unroll
+        for (int u = 0; u < kPairs; ++u) {
+            const int e = 2 * (lane + 32 * u);
+            if (a.qf) *reinterpret_cast<float2*>(a.qf + o + e) = x[u];
+            if (a.qb) store_pair_bf16(a.qb + o + e, x[u].x, x[u].y);
         }
-        __syncwarp();
+        return;
+    }
+    const bool is_k = job < a.q_headn + a.kv_headn;
+    const int gi = is_k ? job - a.q_headn : job - a.q_headn - a.kv_headn;
+    const float* src = (is_k ? a.k : a.v) + (static_cast<size_t>(i) * a.kv_headn + gi) * D;
+#pragma unroll
+    for (int u = 0; u < kPairs; ++u) x[u] = reinterpret_cast<const float2*>(src)[lane + 32 * u];
+    if (is_k) norm_rope_regs<D>(x, a.kg, a.qk_norm, a.eps, cs, sn, a.rope_pairs, lane);
+    const size_t o = static_cast<size_t>(pos) * a.kv_dim + static_cast<size_t>(gi) * D;
+    KV* cache = reinterpret_cast<KV*>(is_k ? a.kc : a.vc);
+    __nv_bfloat16* shadow = is_k ? a.kb : a.vb;
+#pragma unroll
+    for (int u = 0; u < kPairs; ++u) {
+        const int e = 2 * (lane + 32 * u);
+        store_pair<KV>(cache + o + e, x[u].x, x[u].y);
+        if (shadow) store_pair_bf16(shadow + o + e, x[u].x, x[u].y);
     }
 }
 

@@ -42,6 +42,43 @@ __global__ void to_bf16_kernel(const float* __restrict__ src, __nv_bfloat16* __r
         dst[i] = __float2bfloat16_rn(src[i]);
 }
 
+// BERT operands to bf16 in one pass, valid rows only: rows r < lens[b] of q, k and v are converted;
+// padded rows of v are written as zeros (P.V multiplies them by P = 0, so they must be finite), while
+// padded rows of q and k are left as they are (their scores are masked or their outputs discarded).
+// Block = kBertConvRows rows of one batch entry; 8 values per thread step (two 16-byte loads, one
+// 16-byte store).  Needs E % 8 == 0 and 16-byte aligned bases.
+constexpr int kBertConvRows = 8;
+__global__ void __launch_bounds__(256) bert_to_bf16_kernel(const float* __restrict__ q, const float* __restrict__ k,
+                                                           const float* __restrict__ v, const int* __restrict__ lens,
+                                                           int max_len, int E, __nv_bfloat16* __restrict__ bq,
+                                                           __nv_bfloat16* __restrict__ bk, __nv_bfloat16* __restrict__ bv) {
+    const int b = blockIdx.y;
+    const int r0 = blockIdx.x * kBertConvRows;
+    const int len = min(lens[b], max_len);
+    const int units = E / 8;  // 16-byte output units per row
+    const int per_tensor = kBertConvRows * units;
+    for (int u = threadIdx.x; u < 3 * per_tensor; u += blockDim.x) {
+        const int t = u / per_tensor;
+        const int rem = u - t * per_tensor;
+        const int r = r0 + rem / units;
+        if (r >= max_len) continue;
+        const size_t off = (static_cast<size_t>(b) * max_len + r) * E + size_t(rem % units) * 8;
+        __nv_bfloat16* dst = t == 0 ? bq : (t == 1 ? bk : bv);
+        if (r >= len) {
+            if (t == 2) *reinterpret_cast<uint4*>(dst + off) = make_uint4(0u, 0u, 0u, 0u);
+            continue;
+        }
+        const float* src = t == 0 ? q : (t == 1 ? k : v);
+        const float4 x0 = __ldcs(reinterpret_cast<const float4*>(src + off));
+        const float4 x1 = __ldcs(reinterpret_cast<const float4*>(src + off) + 1);
+        const __nv_bfloat162 p0 = __floats2bfloat162_rn(x0.x, x0.y), p1 = __floats2bfloat162_rn(x0.z, x0.w);
+        const __nv_bfloat162 p2 = __floats2bfloat162_rn(x1.x, x1.y), p3 = __floats2bfloat162_rn(x1.z, x1.w);
+        *reinterpret_cast<uint4*>(dst + off) =
+            make_uint4(*reinterpret_cast<const uint32_t*>(&p0), *reinterpret_cast<const uint32_t*>(&p1),
+                       *reinterpret_cast<const uint32_t*>(&p2), *reinterpret_cast<const uint32_t*>(&p3));
+    }
+}
+
 constexpr int kTcRows = 128;  // query rows per tile (UMMA M)
 constexpr int kTcKeys = 64;   // keys per tile (UMMA N of S, K of P.V)
 constexpr int kTcThreads = 192;
