@@ -228,6 +228,13 @@ int launch_decode_t(ligguf_attn* h, const lg::DecodeArgs& a, cudaStream_t st) {
     lc.blockDim = dim3(lg::kDecodeThreads, 1, 1);
     lc.dynamicSmemBytes = Sm::kTotal;
     lc.stream = st;
+    // Programmatic dependent launch: the kernel may start while the previous kernel of the stream
+    // finishes; it waits for that grid (griddepcontrol.wait) before its first global read.
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
     LG_CUDA(cudaLaunchKernelEx(&lc, kern, h->tm_k, h->tm_v, a));
     return LIGGUF_ATTN_OK;
 }
@@ -287,6 +294,8 @@ int decode_enqueue(ligguf_attn* h, int layer, int pos, const float* dq, const fl
     // CTA (finish times then differ by about one tile), larger chunks beyond.
     const int want = std::max(1, decode_blocks_per_sm(c.kv_type, h->nrep) * h->num_sms / kvh);
     a.n_split = std::max(1, std::min(want, a.n_tiles));
+    // the two-level merge handles up to kDecodeMaxGroups groups of decode_merge_group partials
+    a.n_split = std::min(a.n_split, std::min(lg::kDecodeMaxSplit, lg::kDecodeMaxGroups * lg::decode_merge_group(h->nrep, D)));
     a.chunk = std::max(1, a.n_tiles / (a.n_split * 48));
     a.chunk_ctr = h->counters + kvh;
     a.kv_dim = h->kv_dim;
@@ -655,8 +664,8 @@ int ligguf_cuda_attn_init(const ligguf_attn_cfg* cfg, ligguf_attn** out) {
         freq[i] = cfg->rope_freq ? cfg->rope_freq[i]
                                  : powf(c.rope_base, -2.0f * static_cast<float>(i) / static_cast<float>(c.rope_dim));
     const size_t pd = size_t(c.n_layers) * c.head_dim;
-    const size_t part_floats = size_t(c.kv_headn) * lg::kDecodeMaxSplit * nrep * (c.head_dim + 2);
-    const size_t gpart_floats = size_t(c.kv_headn) * lg::kDecodeMaxGroups * nrep * (c.head_dim + 2);
+    const size_t part_floats = size_t(c.kv_headn) * lg::kDecodeMaxSplit * lg::decode_part_stride(nrep, c.head_dim);
+    const size_t gpart_floats = size_t(c.kv_headn) * lg::kDecodeMaxGroups * lg::decode_part_stride(nrep, c.head_dim);
     const size_t n_counters = size_t(c.kv_headn) * (2 + lg::kDecodeMaxGroups);
     if (cudaMalloc(&h->freq, nfreq * 4) != cudaSuccess || cudaMalloc(&h->qg, pd * 4) != cudaSuccess ||
         cudaMalloc(&h->kg, pd * 4) != cudaSuccess || cudaMalloc(&h->part, part_floats * 4) != cudaSuccess ||

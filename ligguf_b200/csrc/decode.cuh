@@ -34,8 +34,18 @@ constexpr int kDecodeThreads = kDecodeConsumers + 32;
 constexpr int kDecodeStages = 3;
 constexpr int kDecodeTileBytes = 16384;
 constexpr int kDecodeMaxSplit = 1024;
-constexpr int kDecodeMergeGroup = 48;  // split partials merged per first-level merge
-constexpr int kDecodeMaxGroups = 32;   // >= ceil(kDecodeMaxSplit / kDecodeMergeGroup)
+constexpr int kDecodeMaxGroups = 32;   // first-level merge groups per KV head (the host bounds n_split)
+
+// One partial (o[NREP][D], m[NREP], l[NREP]) in floats, padded to 16 bytes so that a run of
+// partials can be fetched with one bulk copy.
+__host__ __device__ constexpr int decode_part_stride(int nrep, int d) { return (nrep * (d + 2) + 3) & ~3; }
+// Split partials merged by one CTA: as many as fit the tile ring (the merge copies them there), at
+// most 48.
+__host__ __device__ constexpr int decode_merge_group(int nrep, int d) {
+    return (kDecodeStages * 2 * kDecodeTileBytes) / (decode_part_stride(nrep, d) * 4) < 48
+               ? (kDecodeStages * 2 * kDecodeTileBytes) / (decode_part_stride(nrep, d) * 4)
+               : 48;
+}
 
 struct DecodeArgs {
     const float* q;     // [q_headn][D] raw q of this layer
@@ -47,8 +57,8 @@ struct DecodeArgs {
     void* kc;           // this layer's K cache block [n_context][kv_dim]
     void* vc;
     float* out;         // [q_headn][D]
-    float* part;        // [kv_headn][kDecodeMaxSplit][nrep*(D+2)] split partials
-    float* gpart;       // [kv_headn][kDecodeMaxGroups][nrep*(D+2)] merged group partials
+    float* part;        // [kv_headn][kDecodeMaxSplit][decode_part_stride] split partials
+    float* gpart;       // [kv_headn][kDecodeMaxGroups][decode_part_stride] merged group partials
     int* counters;      // [kv_headn] head tickets, then [kv_headn] grab counters, then
                         // [kv_headn][kDecodeMaxGroups] group tickets; zero between launches
     int* err;           // error word (mapped host memory)
@@ -100,9 +110,11 @@ struct DecodeSmem {
     static constexpr size_t kVnOff = kKnOff + D * 4;
     static constexpr size_t kMiscOff = kVnOff + D * 4;  // corr, m, l [NREP] + 4 ints + stage tile ids
     static constexpr size_t kBarOff = (kMiscOff + 3 * NREP * 4 + 16 + 4 * kDecodeStages + 7) & ~size_t(7);
-    static constexpr size_t kTotal = kBarOff + 3 * kDecodeStages * 8;
+    static constexpr size_t kTotal = kBarOff + (3 * kDecodeStages + 1) * 8;  // + the merge barrier
+    static constexpr int kMergeGroup = decode_merge_group(NREP, D);
     static_assert(kDecodeConsumerWarps * NREP * D * 4 <= kTilesBytes, "reduction buffer alias");
-    static_assert(2 * kDecodeMaxSplit * NREP * 4 <= kTilesBytes, "combine maxima/weights alias");
+    static_assert(size_t(kMergeGroup) * decode_part_stride(NREP, D) * 4 <= kTilesBytes, "merge copy fits the ring");
+    static_assert(kMergeGroup * NREP <= 2 * NREP * Sh::kTileRows, "merge weights fit the score buffer");
 };
 
 // One warp: optional RMSNorm then RoPE of one head (D floats) from global `src` into `dst`.
@@ -282,74 +294,79 @@ __device__ __forceinline__ void transposed_reduce(float (&x)[V], int lane) {
     }
 }
 
-// Merges `count` (o, m, l) partials stored at src[i*PS] (PS = NREP*(D+2): o[NREP][D], m[NREP],
-// l[NREP]) into o_s (unnormalised sum of o*e^(m-M)), m_s (M, the maximum) and l_s (sum of
-// l*e^(m-M)).  All consumer threads take part; `scratch` holds 2*kDecodeMaxSplit*NREP floats.  The
-// loads are issued in batches of 24 partials before any is used (this merge is the kernel's tail).
+// Merges `count` (o, m, l) partials stored at src[i*PS] (PS = decode_part_stride: o[NREP][D],
+// m[NREP], l[NREP]) into o_s (unnormalised sum of o*e^(m-M)), m_s (M, the maximum) and l_s (sum of
+// l*e^(m-M)).  The partials were just written by other CTAs: one bulk copy brings them all into
+// `buf` (the free tile ring) in a single round trip, and the merge then runs from shared memory;
+// `w_s` holds count*NREP weights.  All consumer threads take part.  Returns false (error recorded)
+// if the copy did not land in time; the copy is drained before returning either way.
 template <int NREP, int D>
-__device__ __noinline__ void merge_partials(const float* src, int count, float* scratch, float* o_s, float* m_s,
-                                               float* l_s, int tid, int warp, int lane) {
-    constexpr int PS = NREP * (D + 2);
-    constexpr int CPT = (NREP * D + kDecodeConsumers - 1) / kDecodeConsumers;  // columns per thread
-    constexpr int BATCH = 24;  // partials held in registers at once (no spills at nrep 4, D 128)
-    float* m_all = scratch;                         // [count][NREP] maxima
-    float* w_all = scratch + kDecodeMaxSplit * NREP;  // [count][NREP] sums, then weights
-    float acc[CPT][4];
-#pragma unroll
-    for (int c = 0; c < CPT; ++c)
-#pragma unroll
-        for (int u = 0; u < 4; ++u) acc[c][u] = 0.f;
-    for (int s0 = 0; s0 < count; s0 += BATCH) {
-        float v[CPT][BATCH];
-#pragma unroll
-        for (int c = 0; c < CPT; ++c) {
-            const int idx = tid + c * kDecodeConsumers;
-#pragma unroll
-            for (int u = 0; u < BATCH; ++u)
-                v[c][u] = (idx < NREP * D && s0 + u < count) ? __ldcg(src + (s0 + u) * PS + idx) : 0.f;
-        }
-        if (s0 == 0) {
-            for (int i = tid; i < count * NREP; i += kDecodeConsumers) {
-                const int sp = i / NREP, h = i % NREP;
-                m_all[i] = __ldcg(src + sp * PS + NREP * D + h);
-                w_all[i] = __ldcg(src + sp * PS + NREP * D + NREP + h);
-            }
-            named_bar_sync(1, kDecodeConsumers);
-            if (warp < NREP) {
-                const int h = warp;
-                float M = -INFINITY;
-                for (int sp = lane; sp < count; sp += 32) M = fmaxf(M, m_all[sp * NREP + h]);
-                M = warp_max(M);
-                float L = 0.f;
-                for (int sp = lane; sp < count; sp += 32) {
-                    const float mv = m_all[sp * NREP + h];
-                    const float w = mv == -INFINITY ? 0.f : expf(mv - M);
-                    L = fmaf(w_all[sp * NREP + h], w, L);
-                    w_all[sp * NREP + h] = w;
-                }
-                L = warp_sum(L);
-                if (lane == 0) {
-                    m_s[h] = M;
-                    l_s[h] = L;
-                }
-            }
-            named_bar_sync(1, kDecodeConsumers);
-        }
-#pragma unroll
-        for (int c = 0; c < CPT; ++c) {
-            const int idx = tid + c * kDecodeConsumers;
-            const int h = min(idx, NREP * D - 1) / D;
-#pragma unroll
-            for (int u = 0; u < BATCH; ++u)
-                if (s0 + u < count) acc[c][u & 3] = fmaf(v[c][u], w_all[(s0 + u) * NREP + h], acc[c][u & 3]);
+__device__ __noinline__ bool merge_partials(const float* src, int count, uint8_t* buf, float* w_s, uint64_t* bar,
+                                            uint32_t phase, float* o_s, float* m_s, float* l_s, int tid, int warp,
+                                            int lane, uint64_t deadline, volatile int* abort, int* err) {
+    constexpr int PS = decode_part_stride(NREP, D);
+    const float* pb = reinterpret_cast<const float*>(buf);
+    // The ring was last written through the generic proxy (the CTA reduction); order those accesses
+    // before the copy engine's writes.
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    named_bar_sync(1, kDecodeConsumers);
+    if (tid == 0) {
+        const uint32_t bytes = uint32_t(count) * PS * 4;
+        // The other CTAs' stores were made visible (fence + ticket); order them before the async
+        // proxy's reads.
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        mbar_arrive_expect_tx(bar, bytes);
+        constexpr uint32_t kChunk = 16384;
+        for (uint32_t off = 0; off < bytes; off += kChunk) {
+            const uint32_t n = bytes - off < kChunk ? bytes - off : kChunk;
+            asm volatile(
+                "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                    smem_u32(buf + off)),
+                "l"(reinterpret_cast<const uint8_t*>(src) + off), "r"(n), "r"(smem_u32(bar))
+                : "memory");
         }
     }
-#pragma unroll
-    for (int c = 0; c < CPT; ++c) {
-        const int idx = tid + c * kDecodeConsumers;
-        if (idx < NREP * D) o_s[idx] = (acc[c][0] + acc[c][1]) + (acc[c][2] + acc[c][3]);
+    bool ok = mbar_wait_bounded(bar, phase, deadline, abort);
+    if (!ok) {
+        *abort = 1;
+        *reinterpret_cast<volatile int*>(err) = KERR_TIMEOUT_FULL;
+        const uint64_t dd = deadline + kWaitLimitNs / 2;  // the copy writes this CTA's memory: drain it
+        while (!mbar_try_wait(bar, phase) && globaltimer_ns() < dd) {
+        }
     }
     named_bar_sync(1, kDecodeConsumers);
+    if (*abort) return false;  // raised by any consumer whose wait failed
+    if (warp < NREP) {
+        const int h = warp;
+        float M = -INFINITY;
+        for (int sp = lane; sp < count; sp += 32) M = fmaxf(M, pb[sp * PS + NREP * D + h]);
+        M = warp_max(M);
+        float L = 0.f;
+        for (int sp = lane; sp < count; sp += 32) {
+            const float mv = pb[sp * PS + NREP * D + h];
+            const float w = mv == -INFINITY ? 0.f : expf(mv - M);
+            L = fmaf(pb[sp * PS + NREP * D + NREP + h], w, L);
+            w_s[sp * NREP + h] = w;
+        }
+        L = warp_sum(L);
+        if (lane == 0) {
+            m_s[h] = M;
+            l_s[h] = L;
+        }
+    }
+    named_bar_sync(1, kDecodeConsumers);
+    for (int idx = tid; idx < NREP * D; idx += kDecodeConsumers) {
+        const int h = idx / D;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        int sp = 0;
+        for (; sp + 4 <= count; sp += 4)
+#pragma unroll
+            for (int u = 0; u < 4; ++u) acc[u] = fmaf(pb[(sp + u) * PS + idx], w_s[(sp + u) * NREP + h], acc[u]);
+        for (; sp < count; ++sp) acc[sp & 3] = fmaf(pb[sp * PS + idx], w_s[sp * NREP + h], acc[sp & 3]);
+        o_s[idx] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+    }
+    named_bar_sync(1, kDecodeConsumers);
+    return true;
 }
 
 template <typename KV, int D, int NREP>
@@ -385,12 +402,33 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
     uint64_t* full_k = reinterpret_cast<uint64_t*>(smem + Sm::kBarOff);
     uint64_t* full_v = full_k + kDecodeStages;
     uint64_t* empty = full_v + kDecodeStages;
+    uint64_t* merge_bar = empty + kDecodeStages;  // bulk copy of the partials into the ring
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int split = blockIdx.x, g = blockIdx.y;
     const uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
     const int t_end = a.pos;  // cached positions are [0, pos); the current token is folded in last
     const bool owner = split == a.n_split - 1;
+
+    if (tid == 0) {
+#pragma unroll
+        for (int s = 0; s < kDecodeStages; ++s) {
+            mbar_init(&full_k[s], 1);
+            mbar_init(&full_v[s], 1);
+            mbar_init(&empty[s], kDecodeConsumerWarps);
+        }
+        mbar_init(merge_bar, 1);
+        *abort_s = 0;
+        *last_s = 0;
+        *stop_s = 0;
+        fence_mbar_init();
+    }
+    // Launched as a programmatic dependent of the previous kernel in the stream: everything above
+    // touches only this CTA's shared memory; every global read (inputs, cache rows, the partials
+    // and counters this kernel shares with other launches) comes after the previous grid has
+    // completed.  The next kernel may then launch: its CTAs take SM slots as this grid's retire.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     // Consumer warps start loading their first prologue job (q head, and k / v of the current token
     // on the owner CTA) right away; the norm and rotation happen after the set-up barrier.
@@ -405,19 +443,6 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
                              a.pos, lane);
         else
             head_prefetch<D>(pin, a.v + static_cast<size_t>(g) * D, nullptr, 0, a.freq, 0, a.pos, lane);
-    }
-
-    if (tid == 0) {
-#pragma unroll
-        for (int s = 0; s < kDecodeStages; ++s) {
-            mbar_init(&full_k[s], 1);
-            mbar_init(&full_v[s], 1);
-            mbar_init(&empty[s], kDecodeConsumerWarps);
-        }
-        *abort_s = 0;
-        *last_s = 0;
-        *stop_s = 0;
-        fence_mbar_init();
     }
     __syncthreads();
 
@@ -708,9 +733,10 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
 
     const int head0 = g * NREP;
     if (a.n_split > 1) {
-        // Two-level merge: the last CTA of each group of kDecodeMergeGroup splits merges the group,
+        // Two-level merge: the last CTA of each group of Sm::kMergeGroup splits merges the group,
         // then (with more than one group) the last group merger merges the group results.
-        constexpr int PS = NREP * (D + 2);
+        constexpr int PS = decode_part_stride(NREP, D);
+        constexpr int GRP = Sm::kMergeGroup;
         const int kvh = a.kv_dim / D;
         float* pp = a.part + (static_cast<size_t>(g) * kDecodeMaxSplit + split) * PS;
         for (int idx = tid; idx < NREP * D; idx += kDecodeConsumers) pp[idx] = o_s[idx];
@@ -720,17 +746,19 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
         }
         __threadfence();
         named_bar_sync(1, kDecodeConsumers);
-        const int grp = split / kDecodeMergeGroup;
-        const int n_groups = (a.n_split + kDecodeMergeGroup - 1) / kDecodeMergeGroup;
-        const int gsize = min(kDecodeMergeGroup, a.n_split - grp * kDecodeMergeGroup);
+        const int grp = split / GRP;
+        const int n_groups = (a.n_split + GRP - 1) / GRP;
+        const int gsize = min(GRP, a.n_split - grp * GRP);
         int* grp_ctr = a.counters + 2 * kvh + g * kDecodeMaxGroups + grp;
         if (tid == 0) *last_s = (atomicAdd(grp_ctr, 1) == gsize - 1) ? 1 : 0;
         named_bar_sync(1, kDecodeConsumers);
         if (!*last_s) return;
         __threadfence();
-        float* scratch = reinterpret_cast<float*>(tiles);  // the tiles are free: alias them
-        merge_partials<NREP, D>(a.part + (static_cast<size_t>(g) * kDecodeMaxSplit + grp * kDecodeMergeGroup) * PS,
-                                gsize, scratch, o_s, m_s, l_s, tid, warp, lane);
+        // The tiles are free: the merge copies the partials there; its weights go to the score buffer.
+        if (!merge_partials<NREP, D>(a.part + (static_cast<size_t>(g) * kDecodeMaxSplit + grp * GRP) * PS, gsize,
+                                     tiles, sc, merge_bar, 0, o_s, m_s, l_s, tid, warp, lane, deadline, abort_s,
+                                     a.err))
+            return;
         if (tid == 0) *grp_ctr = 0;
         if (n_groups > 1) {
             float* gp = a.gpart + (static_cast<size_t>(g) * kDecodeMaxGroups + grp) * PS;
@@ -745,8 +773,9 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
             named_bar_sync(1, kDecodeConsumers);
             if (!*last_s) return;
             __threadfence();
-            merge_partials<NREP, D>(a.gpart + static_cast<size_t>(g) * kDecodeMaxGroups * PS, n_groups, scratch,
-                                    o_s, m_s, l_s, tid, warp, lane);
+            if (!merge_partials<NREP, D>(a.gpart + static_cast<size_t>(g) * kDecodeMaxGroups * PS, n_groups, tiles,
+                                         sc, merge_bar, 1, o_s, m_s, l_s, tid, warp, lane, deadline, abort_s, a.err))
+                return;
             if (tid == 0) a.counters[g] = 0;
         }
         // Every CTA of this head took its group ticket after its last grab: the counter is free.
