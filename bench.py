@@ -7,8 +7,9 @@ Workload (every N): qwen3_8b_decode_32k - Qwen3-8B-shaped single-stream decode a
 36 per-layer launches of the decode kernel (the real forward's order: layer l+1 starts after layer
 l), each streaming that layer's K and V rows [0, 32768] (268 MB) from HBM.  With N > 1 the KV heads
 are split over the ranks as SARA does (cpp/ligguf_distrib.cpp:665-679) and every layer's head
-outputs are all-gathered over NVLink (NCCL) - strong scaling of one stream.  Inputs are larger than
-L2 (9.66 GB of KV per step), so no L2 flush is needed between steps.
+outputs are all-gathered over NVLink by the decode kernel's own peer stores (NCCL all-gather is
+timed alongside) - strong scaling of one stream.  Inputs are larger than L2 (9.66 GB of KV per
+step), so no L2 flush is needed between steps.
 
 At N == 1 the line also carries the other configurations as `extra`: the 4K-context decode, the
 causal 2048-token prefill (fp32 SIMT and bf16 tensor cores) and the BERT attention.
@@ -38,8 +39,8 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extra", action="store_true", help="skip the other configurations at N=1")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    ap.add_argument("--gather", choices=["p2p", "nccl"], default="nccl",
-                    help="N>1: all-gather of head outputs by the decode kernel's peer stores (p2p) or NCCL")
+    ap.add_argument("--gather", choices=["p2p", "nccl"], default="p2p",
+                    help="N>1: all-gather of head outputs by the decode kernel's peer stores (p2p, default) or NCCL")
     ap.add_argument("--case", choices=["decode-layer", "prefill-layer", "bert-layer"], default=None,
                     help="run one small case a few times and exit (the command the ncu summaries use)")
     return ap.parse_args()

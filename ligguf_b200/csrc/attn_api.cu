@@ -111,31 +111,28 @@ __global__ void kv_synth_kernel(T* layer_base, int kv_dim, int kv_dim_full, int 
 float synth_mul(float scale) { return static_cast<float>(static_cast<double>(scale) / lg::kSynthSd); }
 
 // ---------------------------------------------------------------------------- gather wait
-// Waits (bounded) until every KV head's flag in `flags` shows `epoch`, then copies the gathered
-// vector to `out`.  One CTA.
-__global__ void gather_wait_kernel(const float* gathered, const int* flags, int n_flags, int epoch, float* out,
-                                   int n, int* err) {
-    __shared__ int ok_s;
-    if (threadIdx.x == 0) {
-        const uint64_t deadline = lg::globaltimer_ns() + lg::kWaitLimitNs;
-        int ok = 1;
-        for (int i = 0; i < n_flags && ok; ++i) {
-            int v;
-            while (true) {
-                asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(flags + i) : "memory");
-                if (v == epoch) break;
-                if (lg::globaltimer_ns() > deadline) {
-                    ok = 0;
-                    break;
-                }
-            }
+// Gather wait: one thread per element polls its 64-bit word in this rank's gather slot until the
+// word carries `epoch` (bounded), then writes the fp32 value to `out`.  Launched as a programmatic
+// dependent of the decode kernel, it starts while the decode still runs; it reads nothing the decode
+// writes other than these self-validating words, so it never waits for the decode grid itself.
+__global__ void __launch_bounds__(256) gather_wait_kernel(const unsigned long long* words, int epoch, float* out,
+                                                          int n, int* err) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const uint64_t deadline = lg::globaltimer_ns() + lg::kWaitLimitNs;
+    const uint32_t want = static_cast<uint32_t>(epoch);
+    unsigned long long w;
+    uint32_t spins = 0;
+    while (true) {
+        asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(words + i) : "memory");
+        if (static_cast<uint32_t>(w >> 32) == want) break;
+        if ((++spins & 63u) == 0u && lg::globaltimer_ns() > deadline) {
+            *reinterpret_cast<volatile int*>(err) = lg::KERR_TIMEOUT_PEER;
+            return;
         }
-        if (!ok) *reinterpret_cast<volatile int*>(err) = lg::KERR_TIMEOUT_PEER;
-        ok_s = ok;
     }
-    __syncthreads();
-    if (!ok_s) return;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = __ldcv(gathered + i);
+    out[i] = __uint_as_float(static_cast<uint32_t>(w));
 }
 
 }  // namespace
@@ -168,12 +165,11 @@ struct ligguf_attn {
     alignas(64) CUtensorMap tm_k;
     alignas(64) CUtensorMap tm_v;
     // SARA gather over CUDA IPC
-    float* gbuf = nullptr;  // [2][n_heads*D] floats then [2][n_kv_heads] ints
+    unsigned long long* gbuf = nullptr;  // [2][n_heads*D] gather words: (epoch << 32) | fp32 bits
     size_t gbuf_bytes = 0;
     int g_nranks = 0, g_rank = -1, g_epoch = 0;
     std::vector<void*> g_opened;
-    float** d_peer_out = nullptr;  // [2][nranks]
-    int** d_peer_flag = nullptr;   // [2][nranks]
+    unsigned long long** d_peer_ll = nullptr;  // [2][nranks]: slot s of every rank's gather buffer
 };
 
 struct ligguf_bert_attn {
@@ -307,15 +303,11 @@ int decode_enqueue(ligguf_attn* h, int layer, int pos, const float* dq, const fl
     a.kv_head0 = c.kv_head0;
     if (gather) {
         const int slot = h->g_epoch & 1;
-        a.peer_out = h->d_peer_out + slot * h->g_nranks;
-        a.peer_flag = h->d_peer_flag + slot * h->g_nranks;
+        a.peer_ll = h->d_peer_ll + slot * h->g_nranks;
         a.nranks = h->g_nranks;
         a.rank = h->g_rank;
         a.q_off = c.kv_head0 * h->nrep * D;
         a.flag_value = h->g_epoch;
-        // the local copy of this shard's slice lands in this rank's own gather buffer
-        a.out = reinterpret_cast<float*>(reinterpret_cast<char*>(h->gbuf) + size_t(slot) * c.n_heads * D * 4) +
-                a.q_off;
     }
     switch (c.kv_type) {
         case LIGGUF_KV_F32: return launch_decode_k<float>(h, a, st);
@@ -590,7 +582,7 @@ int ligguf_cuda_attn_free(ligguf_attn* h) {
     for (void* p : h->g_opened)
         if (p) cudaIpcCloseMemHandle(p);
     void* dev_ptrs[] = {h->kc, h->vc, h->freq, h->qg, h->kg, h->part, h->gpart, h->counters, h->d_stage, h->qf, h->qb,
-                        h->kb, h->vb, h->gbuf, h->d_peer_out, h->d_peer_flag};
+                        h->kb, h->vb, h->gbuf, h->d_peer_ll};
     for (void* p : dev_ptrs)
         if (p) cudaFree(p);
     if (h->h_err) cudaFreeHost(h->h_err);
@@ -830,7 +822,7 @@ int ligguf_cuda_attn_gather_ipc_handle(ligguf_attn* h, void* handle_out, size_t 
         return fail(LIGGUF_ATTN_EINVAL, "handle buffer of %zu bytes (need %zu)", handle_size, sizeof(cudaIpcMemHandle_t));
     DeviceGuard dg(h->cfg.device);
     if (!h->gbuf) {
-        h->gbuf_bytes = 2 * size_t(h->cfg.n_heads) * h->cfg.head_dim * 4 + 2 * size_t(h->cfg.n_kv_heads) * 4;
+        h->gbuf_bytes = 2 * size_t(h->cfg.n_heads) * h->cfg.head_dim * sizeof(unsigned long long);
         if (cudaMalloc(reinterpret_cast<void**>(&h->gbuf), h->gbuf_bytes) != cudaSuccess)
             return fail(LIGGUF_ATTN_ENOMEM, "gather buffer");
         LG_CUDA(cudaMemset(h->gbuf, 0, h->gbuf_bytes));
@@ -849,30 +841,24 @@ int ligguf_cuda_attn_gather_open(ligguf_attn* h, int nranks, int rank, const voi
     if (h->g_nranks) return fail(LIGGUF_ATTN_ESTATE, "gather already open");
     DeviceGuard dg(h->cfg.device);
     const size_t vec = size_t(h->cfg.n_heads) * h->cfg.head_dim;
-    std::vector<float*> outs(2 * nranks);
-    std::vector<int*> flags(2 * nranks);
+    std::vector<unsigned long long*> slots(2 * nranks);
     h->g_opened.assign(nranks, nullptr);
     for (int r = 0; r < nranks; ++r) {
-        char* base;
+        unsigned long long* base;
         if (r == rank) {
-            base = reinterpret_cast<char*>(h->gbuf);
+            base = h->gbuf;
         } else {
             cudaIpcMemHandle_t hd;
             memcpy(&hd, static_cast<const char*>(handles) + size_t(r) * handle_size, sizeof(hd));
             void* p = nullptr;
             LG_CUDA(cudaIpcOpenMemHandle(&p, hd, cudaIpcMemLazyEnablePeerAccess));
             h->g_opened[r] = p;
-            base = static_cast<char*>(p);
+            base = static_cast<unsigned long long*>(p);
         }
-        for (int slot = 0; slot < 2; ++slot) {
-            outs[slot * nranks + r] = reinterpret_cast<float*>(base) + slot * vec;
-            flags[slot * nranks + r] = reinterpret_cast<int*>(base + 2 * vec * 4) + slot * h->cfg.n_kv_heads;
-        }
+        for (int slot = 0; slot < 2; ++slot) slots[slot * nranks + r] = base + slot * vec;
     }
-    LG_CUDA(cudaMalloc(reinterpret_cast<void**>(&h->d_peer_out), outs.size() * sizeof(float*)));
-    LG_CUDA(cudaMalloc(reinterpret_cast<void**>(&h->d_peer_flag), flags.size() * sizeof(int*)));
-    LG_CUDA(cudaMemcpy(h->d_peer_out, outs.data(), outs.size() * sizeof(float*), cudaMemcpyHostToDevice));
-    LG_CUDA(cudaMemcpy(h->d_peer_flag, flags.data(), flags.size() * sizeof(int*), cudaMemcpyHostToDevice));
+    LG_CUDA(cudaMalloc(reinterpret_cast<void**>(&h->d_peer_ll), slots.size() * sizeof(unsigned long long*)));
+    LG_CUDA(cudaMemcpy(h->d_peer_ll, slots.data(), slots.size() * sizeof(unsigned long long*), cudaMemcpyHostToDevice));
     h->g_nranks = nranks;
     h->g_rank = rank;
     h->g_epoch = 0;
@@ -896,12 +882,18 @@ int ligguf_cuda_attn_gather_wait_async(ligguf_attn* h, int layer, float* d_out, 
     if (layer < 0 || layer >= h->cfg.n_layers) return fail(LIGGUF_ATTN_EINVAL, "layer %d out of range", layer);
     DeviceGuard dg(h->cfg.device);
     const int slot = h->g_epoch & 1;
-    const size_t vec = size_t(h->cfg.n_heads) * h->cfg.head_dim;
-    const float* gathered = h->gbuf + slot * vec;
-    const int* flags = reinterpret_cast<const int*>(reinterpret_cast<const char*>(h->gbuf) + 2 * vec * 4) +
-                       slot * h->cfg.n_kv_heads;
-    gather_wait_kernel<<<1, 256, 0, static_cast<cudaStream_t>(stream)>>>(gathered, flags, h->cfg.n_kv_heads,
-                                                                         h->g_epoch, d_out, int(vec), h->d_err);
+    const int vec = h->cfg.n_heads * h->cfg.head_dim;
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(ceil_div(vec, 256), 1, 1);
+    lc.blockDim = dim3(256, 1, 1);
+    lc.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    LG_CUDA(cudaLaunchKernelEx(&lc, gather_wait_kernel, static_cast<const unsigned long long*>(h->gbuf + size_t(slot) * vec),
+                               h->g_epoch, d_out, vec, h->d_err));
     LG_CUDA(cudaGetLastError());
     return LIGGUF_ATTN_OK;
 }

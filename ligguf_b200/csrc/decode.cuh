@@ -62,13 +62,12 @@ struct DecodeArgs {
     int* counters;      // [kv_headn] head tickets, then [kv_headn] grab counters, then
                         // [kv_headn][kDecodeMaxGroups] group tickets; zero between launches
     int* err;           // error word (mapped host memory)
-    float* const* peer_out;  // multi-GPU gather: [nranks] gather buffers (or null)
-    int* const* peer_flag;   // [nranks] flag arrays [nranks*kv_headn]
+    unsigned long long* const* peer_ll;  // multi-GPU gather: [nranks] gather slots of [n_heads*D] words (or null)
     int nranks;
     int rank;
     int q_off;          // element offset of this shard's heads in the gathered vector
     int kv_head0;       // global index of this shard's first KV head (gather flag slot)
-    int flag_value;
+    int flag_value;     // epoch carried in the high half of every gather word
     int row0;           // tensor-map row of (this layer, position 0) = layer * n_context
     int pos;
     int n_tiles;        // tiles covering [0, pos)
@@ -781,22 +780,21 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
         // Every CTA of this head took its group ticket after its last grab: the counter is free.
         if (tid == 0) a.chunk_ctr[g] = 0;
     }
-    for (int idx = tid; idx < NREP * D; idx += kDecodeConsumers) {
-        const float val = o_s[idx] / l_s[idx / D];
-        a.out[static_cast<size_t>(head0) * D + idx] = val;
-        if (a.peer_out) {
-            for (int rr = 0; rr < a.nranks; ++rr) a.peer_out[rr][a.q_off + head0 * D + idx] = val;
+    if (a.peer_ll) {
+        // Multi-GPU gather: every output element goes to every rank's gather slot as one 64-bit word,
+        // (epoch << 32) | fp32 bits, stored with a single relaxed system-scope store.  A reader that
+        // sees the current epoch in a word has that word's value: no fence, no flags.
+        const unsigned long long tag = static_cast<unsigned long long>(static_cast<uint32_t>(a.flag_value)) << 32;
+        for (int idx = tid; idx < NREP * D; idx += kDecodeConsumers) {
+            const unsigned long long w = tag | __float_as_uint(o_s[idx] / l_s[idx / D]);
+            const size_t e = static_cast<size_t>(a.q_off) + static_cast<size_t>(head0) * D + idx;
+            for (int rr = 0; rr < a.nranks; ++rr)
+                asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(a.peer_ll[rr] + e), "l"(w) : "memory");
         }
+        return;
     }
-    if (a.peer_out) {
-        // Publish: every store of this head group is visible system-wide before the flags.
-        __threadfence_system();
-        named_bar_sync(1, kDecodeConsumers);
-        if (tid < a.nranks) {
-            volatile int* f = a.peer_flag[tid] + a.kv_head0 + g;
-            *f = a.flag_value;
-        }
-    }
+    for (int idx = tid; idx < NREP * D; idx += kDecodeConsumers)
+        a.out[static_cast<size_t>(head0) * D + idx] = o_s[idx] / l_s[idx / D];
 }
 
 }  // namespace lg
