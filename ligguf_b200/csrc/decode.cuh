@@ -293,6 +293,15 @@ __device__ __forceinline__ void transposed_reduce(float (&x)[V], int lane) {
     }
 }
 
+// Ticket of a merge level: after a CTA barrier that orders every thread's partial stores, one
+// thread's acquire-release add publishes them at GPU scope (release is cumulative over what the
+// barrier ordered before it) and, for the last arrival, makes every other CTA's partials visible.
+__device__ __forceinline__ int ticket_acq_rel(int* ctr) {
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(ctr) : "memory");
+    return old;
+}
+
 // Merges `count` (o, m, l) partials stored at src[i*PS] (PS = decode_part_stride: o[NREP][D],
 // m[NREP], l[NREP]) into o_s (unnormalised sum of o*e^(m-M)), m_s (M, the maximum) and l_s (sum of
 // l*e^(m-M)).  The partials were just written by other CTAs: one bulk copy brings them all into
@@ -743,16 +752,14 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
             pp[NREP * D + tid] = m_s[tid];
             pp[NREP * D + NREP + tid] = l_s[tid];
         }
-        __threadfence();
         named_bar_sync(1, kDecodeConsumers);
         const int grp = split / GRP;
         const int n_groups = (a.n_split + GRP - 1) / GRP;
         const int gsize = min(GRP, a.n_split - grp * GRP);
         int* grp_ctr = a.counters + 2 * kvh + g * kDecodeMaxGroups + grp;
-        if (tid == 0) *last_s = (atomicAdd(grp_ctr, 1) == gsize - 1) ? 1 : 0;
+        if (tid == 0) *last_s = (ticket_acq_rel(grp_ctr) == gsize - 1) ? 1 : 0;
         named_bar_sync(1, kDecodeConsumers);
         if (!*last_s) return;
-        __threadfence();
         // The tiles are free: the merge copies the partials there; its weights go to the score buffer.
         if (!merge_partials<NREP, D>(a.part + (static_cast<size_t>(g) * kDecodeMaxSplit + grp * GRP) * PS, gsize,
                                      tiles, sc, merge_bar, 0, o_s, m_s, l_s, tid, warp, lane, deadline, abort_s,
@@ -766,12 +773,10 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
                 gp[NREP * D + tid] = m_s[tid];
                 gp[NREP * D + NREP + tid] = l_s[tid];
             }
-            __threadfence();
             named_bar_sync(1, kDecodeConsumers);
-            if (tid == 0) *last_s = (atomicAdd(&a.counters[g], 1) == n_groups - 1) ? 1 : 0;
+            if (tid == 0) *last_s = (ticket_acq_rel(&a.counters[g]) == n_groups - 1) ? 1 : 0;
             named_bar_sync(1, kDecodeConsumers);
             if (!*last_s) return;
-            __threadfence();
             if (!merge_partials<NREP, D>(a.gpart + static_cast<size_t>(g) * kDecodeMaxGroups * PS, n_groups, tiles,
                                          sc, merge_bar, 1, o_s, m_s, l_s, tid, warp, lane, deadline, abort_s, a.err))
                 return;
