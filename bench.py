@@ -245,30 +245,25 @@ def bench_decode(args, w, rank, world, local, pg, peaks):
     out = torch.empty(w.n_layers, s["q_headn"] * D, device=dev)
     full = torch.empty(w.n_layers, w.n_heads * D, device=dev) if world > 1 else out
     L = w.n_layers
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L * args.steps)]
     if world > 1:  # the fused gather: decode epilogues store into every peer's buffer (CUDA IPC)
         mine = h.gather_ipc_handle()
         handles = [None] * world
         pg.all_gather_object(handles, mine)
         h.gather_open(rank, handles)
 
-    def step(i=None, gather=args.gather):
+    def step(gather=args.gather):
         for l in range(L):
-            if i is not None:
-                ev[i * L + l][0].record()
             if world > 1 and gather == "p2p":
                 h.decode_gather_async(l, w.pos, q[l], k[l], v[l])
             else:
                 h.decode_async(l, w.pos, q[l], k[l], v[l], out[l])
-            if i is not None:
-                ev[i * L + l][1].record()
             if world > 1:
                 if gather == "p2p":
                     h.gather_wait_async(l, full[l])
                 else:
                     pg.all_gather_into_tensor(full[l], out[l])
 
-    def timed(n, gather, with_events):
+    def timed(n, gather):
         for _ in range(args.warmup):
             step(gather=gather)
         torch.cuda.synchronize()
@@ -279,8 +274,8 @@ def bench_decode(args, w, rank, world, local, pg, peaks):
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record()
-        for i in range(n):
-            step(i if with_events else None, gather=gather)
+        for _ in range(n):
+            step(gather=gather)
         t1.record()
         torch.cuda.synchronize()
         if world > 1:
@@ -297,17 +292,19 @@ def bench_decode(args, w, rank, world, local, pg, peaks):
     clk = ClockSampler(local)
     clk.start()
     time.sleep(0.3)
-    ms_per_step = timed(args.steps, args.gather, True)
+    ms_per_step = timed(args.steps, args.gather)
     clocks = clk.stop()
     tok_s = 1e3 / ms_per_step
-    kern_ms = [a.elapsed_time(b) for a, b in ev]
-    kern_avg_ms = statistics.mean(kern_ms)
+    # Average decode-kernel launch duration: the CUDA-event time of the timed region over the decode
+    # launches in it (no events between launches: they would serialise the programmatic launches
+    # that let consecutive layers overlap).  Gaps between launches count against the kernel.
+    kern_avg_ms = ms_per_step / L
     bytes_launch = 2 * (w.pos + 1) * s["kv_headn"] * D * 4 + (s["q_headn"] * 2 + s["kv_headn"] * 2) * D * 4
     achieved = bytes_launch / (kern_avg_ms * 1e-3) / 1e9
     other = None
     if world > 1:  # the other gather, for comparison
         alt = "nccl" if args.gather == "p2p" else "p2p"
-        other = {"gather": alt, "tokens_s": 1e3 / timed(max(3, args.steps // 2), alt, False)}
+        other = {"gather": alt, "tokens_s": 1e3 / timed(max(3, args.steps // 2), alt)}
 
     # end to end through the public API (pinned host buffers, copies inside the timed region)
     e2e = bench_decode_e2e(args, w, h, s, q, k, v, world, local, pg)

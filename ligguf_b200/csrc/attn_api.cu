@@ -148,6 +148,10 @@ struct ligguf_attn {
     float* qg = nullptr;  // [n_layers][D]
     float* kg = nullptr;
     std::vector<uint8_t> norm_set;
+    // Cache rows written by the most recent call that writes the cache (possibly still running when
+    // the next decode starts): layers [wr_l0, wr_l1), rows from wr_row0 up.  A decode may load rows
+    // below it before its predecessor grid completes.
+    int wr_l0 = 0, wr_l1 = 0, wr_row0 = 0;
     float* part = nullptr;
     float* gpart = nullptr;
     int* counters = nullptr;
@@ -256,6 +260,12 @@ int launch_decode_k(ligguf_attn* h, const lg::DecodeArgs& a, cudaStream_t st) {
 // Blocks of the decode kernel resident per SM (its __launch_bounds__ minimum).
 int decode_blocks_per_sm(int kv_type, int nrep) { return nrep * (kv_type == LIGGUF_KV_F32 ? 4 : 8) > 32 ? 1 : 2; }
 
+void note_cache_write(ligguf_attn* h, int layer0, int n_layers, int row0) {
+    h->wr_l0 = layer0;
+    h->wr_l1 = layer0 + n_layers;
+    h->wr_row0 = row0;
+}
+
 int decode_enqueue(ligguf_attn* h, int layer, int pos, const float* dq, const float* dk, const float* dv,
                    float* dout, cudaStream_t st, bool gather) {
     const ligguf_attn_cfg& c = h->cfg;
@@ -301,6 +311,8 @@ int decode_enqueue(ligguf_attn* h, int layer, int pos, const float* dq, const fl
     a.scale = a.scale_div ? sqrtf(static_cast<float>(D)) : 1.0f / sqrtf(static_cast<float>(D));
     a.eps = c.rms_epsilon;
     a.kv_head0 = c.kv_head0;
+    a.pre_rows = (layer >= h->wr_l0 && layer < h->wr_l1) ? std::min(pos, h->wr_row0) : pos;
+    note_cache_write(h, layer, 1, pos);
     if (gather) {
         const int slot = h->g_epoch & 1;
         a.peer_ll = h->d_peer_ll + slot * h->g_nranks;
@@ -410,6 +422,7 @@ int prefill_enqueue(ligguf_attn* h, int layer, int pos0, int n, const float* dq,
         return fail(LIGGUF_ATTN_ESTATE, "QK-norm weights of layer %d were not set", layer);
     const int D = c.head_dim;
     const size_t qn = size_t(n) * h->q_headn * D;
+    note_cache_write(h, layer, 1, pos0);
     lg::PrepArgs p = {};
     p.q = dq;
     p.k = dk;
@@ -766,6 +779,7 @@ int ligguf_cuda_attn_kv_upload(ligguf_attn* h, int layer, int pos0, int n, const
     const size_t off = (size_t(layer) * h->layer_elems + size_t(pos0) * h->kv_dim) * h->es;
     const size_t bytes = size_t(n) * h->kv_dim * h->es;
     LG_CUDA(cudaStreamSynchronize(h->stream));
+    note_cache_write(h, layer, 1, pos0);
     LG_CUDA(cudaMemcpy(static_cast<char*>(h->kc) + off, host_k, bytes, cudaMemcpyHostToDevice));
     LG_CUDA(cudaMemcpy(static_cast<char*>(h->vc) + off, host_v, bytes, cudaMemcpyHostToDevice));
     return LIGGUF_ATTN_OK;
@@ -780,6 +794,7 @@ int ligguf_cuda_attn_kv_synth(ligguf_attn* h, int layer0, int n_layers, int pos0
     DeviceGuard dg(h->cfg.device);
     const float mul = synth_mul(scale);
     const int kv_off = h->cfg.kv_head0 * h->cfg.head_dim;
+    note_cache_write(h, layer0, n_layers, pos0);
     const size_t total = size_t(n) * h->kv_dim;
     const int blocks = std::min(8 * h->num_sms, std::max(1, ceil_div(total, 256)));
     for (int l = layer0; l < layer0 + n_layers && n > 0; ++l) {

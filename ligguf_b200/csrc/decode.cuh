@@ -68,6 +68,7 @@ struct DecodeArgs {
     int q_off;          // element offset of this shard's heads in the gathered vector
     int kv_head0;       // global index of this shard's first KV head (gather flag slot)
     int flag_value;     // epoch carried in the high half of every gather word
+    int pre_rows;       // cache rows [0, pre_rows) of this layer are final before the previous grid ends
     int row0;           // tensor-map row of (this layer, position 0) = layer * n_context
     int pos;
     int n_tiles;        // tiles covering [0, pos)
@@ -432,10 +433,12 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
         fence_mbar_init();
     }
     // Launched as a programmatic dependent of the previous kernel in the stream: everything above
-    // touches only this CTA's shared memory; every global read (inputs, cache rows, the partials
-    // and counters this kernel shares with other launches) comes after the previous grid has
-    // completed.  The next kernel may then launch: its CTAs take SM slots as this grid's retire.
-    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // touches only this CTA's shared memory; every global read (inputs, the partials and counters
+    // this kernel shares with other launches, cache rows) comes after the previous grid has
+    // completed - except the producer's first copies of cache rows below a.pre_rows, which no
+    // kernel still in flight can be writing (see the producer).  The next kernel may then launch:
+    // its CTAs take SM slots as this grid's retire.
+    if (warp != kDecodeConsumerWarps) asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     // Consumer warps start loading their first prologue job (q head, and k / v of the current token
@@ -462,10 +465,36 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
             bool fail = false;
             int base = split * a.chunk;  // first chunk: static
             const int first_dyn = a.n_split * a.chunk;
+            auto issue = [&](int t, int s) {
+                tile_id_s[s] = t;
+                const int row = a.row0 + t * TP;
+                uint8_t* kdst = tiles + s * Sm::kStageBytes;
+                mbar_arrive_expect_tx(&full_k[s], kDecodeTileBytes);
+                tma_load_3d(kdst, &tm_k, &full_k[s], 0, g, row);
+                mbar_arrive_expect_tx(&full_v[s], kDecodeTileBytes);
+                tma_load_3d(kdst + kDecodeTileBytes, &tm_v, &full_v[s], 0, g, row);
+                ++issued;
+            };
+            // While the previous grid finishes: the first tiles of the static chunk that lie wholly
+            // below a.pre_rows.  The host sets pre_rows below every row its most recent cache write
+            // touched in this layer, and with programmatic launches only the immediately preceding
+            // kernel can still be running (each of this library's kernels waits for its own
+            // predecessor before it lets its dependent launch).
+            int t0 = base;
+            const int lim0 = min(base + a.chunk, a.n_tiles);
+            for (; t0 < lim0 && it < kDecodeStages && (t0 + 1) * TP <= a.pre_rows; ++t0, ++it) issue(t0, it);
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            bool first = true;
             while (!fail && base < a.n_tiles) {
                 const int lim = min(base + a.chunk, a.n_tiles);
                 int next = lim;
-                for (int t = base; t < lim; ++t, ++it) {
+                int t = base;
+                if (first && t0 > base) {  // part of the first chunk is already on its way
+                    t = t0;
+                    if (a.n_split > 1) next = first_dyn + atomicAdd(&a.chunk_ctr[g], a.chunk);
+                }
+                first = false;
+                for (; t < lim; ++t, ++it) {
                     const int s = it % kDecodeStages;
                     if (it >= kDecodeStages &&
                         !mbar_wait_bounded(&empty[s], ((it / kDecodeStages) - 1) & 1, deadline, abort_s)) {
@@ -474,14 +503,7 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
                         fail = true;
                         break;
                     }
-                    tile_id_s[s] = t;
-                    const int row = a.row0 + t * TP;
-                    uint8_t* kdst = tiles + s * Sm::kStageBytes;
-                    mbar_arrive_expect_tx(&full_k[s], kDecodeTileBytes);
-                    tma_load_3d(kdst, &tm_k, &full_k[s], 0, g, row);
-                    mbar_arrive_expect_tx(&full_v[s], kDecodeTileBytes);
-                    tma_load_3d(kdst + kDecodeTileBytes, &tm_v, &full_v[s], 0, g, row);
-                    ++issued;
+                    issue(t, s);
                     // Fetch the next chunk once this chunk's first copy is on its way: the grab's
                     // latency overlaps the remaining waits and copies instead of delaying them.
                     if (t == base && a.n_split > 1) next = first_dyn + atomicAdd(&a.chunk_ctr[g], a.chunk);

@@ -160,6 +160,40 @@ def test_decode_async_device_tensors(gpu):
     h.close()
 
 
+def test_back_to_back_steps_read_the_rows_they_append(gpu):
+    """Decode steps launched back to back on one stream with no host synchronisation, alternating two
+    layers: every step reads the row its layer's previous step appended.  (A decode may start loading
+    cache rows while the previous kernel finishes, but only rows no kernel still in flight can write.)"""
+    import torch
+    P0, steps, H, Hk, D = 1000, 6, 32, 8, 128
+    cs = [cases.decode_case(H=H, Hk=Hk, D=D, n_ctx=1100, theta=1e6, qk_norm=1, pos=P0, seed=33, layer=l)
+          for l in (0, 1)]
+    h = make_handle(cs[0], n_layers=2)  # both layers get layer 0's norm weights
+    h.kv_synth(0, 2, 0, P0, 33, 1.0)
+    rng = np.random.default_rng(5)
+    ins = [[rng.standard_normal(n).astype(np.float32) for n in (H * D, Hk * D, Hk * D)] for _ in range(2 * steps)]
+    dev = torch.device("cuda", 0)
+    dins = [[torch.from_numpy(x).to(dev) for x in xs] for xs in ins]
+    outs = [torch.empty(H * D, device=dev) for _ in range(2 * steps)]
+    torch.cuda.synchronize()
+    h.sync()
+    for i in range(steps):
+        for l in (0, 1):
+            q, k, v = dins[2 * i + l]
+            h.decode_async(l, P0 + i, q, k, v, outs[2 * i + l])
+    torch.cuda.synchronize()
+    port = orc.Checker("port")
+    cfg = orc.Checker.cfg(H, Hk, D, 1100, D, cs[0]["eps"], 1, 0, 0)
+    caches = [(c["kc"].copy(), c["vc"].copy()) for c in cs]
+    for i in range(steps):
+        for l in (0, 1):
+            kc, vc = caches[l]
+            q, k, v = ins[2 * i + l]
+            ref = port.decode_layer(cfg, kc, vc, cs[0]["freq"], cs[0]["qg"], cs[0]["kg"], P0 + i, q, k, v)
+            assert cases.rel_err(outs[2 * i + l].cpu().numpy(), ref) <= TOL, (i, l)
+    h.close()
+
+
 @pytest.mark.parametrize("nranks", [2, 4, 8])
 def test_sharded_decode_matches_unsharded(gpu, nranks):
     """SARA split by KV head (cpp/ligguf_distrib.cpp:665-679): the shards' outputs, concatenated in
