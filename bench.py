@@ -581,7 +581,7 @@ def main():
         line = {
             "metric": METRIC, "value": res["value"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "higher_is_better": True,
-            "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f32",
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded generator, ~N(0,1)); random-init QK-norm weights",
             "config": {"workload": WORKLOAD, "layers": w.n_layers, "ctx": w.pos + 1, "kv": "fp32",
                        "heads": [w.n_heads, w.n_kv_heads, w.head_dim],
