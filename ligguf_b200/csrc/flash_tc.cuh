@@ -223,6 +223,31 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, uint64_t
     return false;
 }
 
+// Packed fp32 pair arithmetic (sm_100 f32x2 instructions): half the issue slots of two scalar ops.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "add.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
 template <int D>
 __global__ void __launch_bounds__(kTcThreads, 2)
     flash_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -426,14 +451,15 @@ __global__ void __launch_bounds__(kTcThreads, 2)
 #pragma unroll
                 for (int c = 0; c < kTcKeys; ++c) sv[c] = (c < lim_c && c <= lim_r) ? sv[c] : -INFINITY;
             }
-            // Row max and sum with 8 independent chains (a single chain serialises 64 dependent ops).
+            // Row max with 8 independent chains of three-input max.
             float mx8[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u) mx8[u] = sv[u];
 #pragma unroll
-            for (int c = 8; c < kTcKeys; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], sv[c]);
-            const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                                   fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+            for (int c = 8; c < kTcKeys; c += 16)
+#pragma unroll
+                for (int u = 0; u < 8; ++u) mx8[u] = fmax3(mx8[u], sv[c + u], sv[c + 8 + u]);
+            const float mx = fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
             // The running max (log2 units) only moves when the tile max exceeds it by more than 8:
             // p = 2^(s*c2 - m) then stays <= 256 and O/l are rescaled rarely; the normalisation at
             // the end uses the same m, so the result is unchanged.
@@ -441,38 +467,41 @@ __global__ void __launch_bounds__(kTcThreads, 2)
             const float m_new = (m == -INFINITY || mt > m + 8.0f) ? mt : m;
             const float ms = m_new == -INFINITY ? 0.f : m_new;
             const float corr = (m == m_new || m_new == -INFINITY) ? 1.f : fast_exp2(m - m_new);
-            float rs8[8];
+            // p = 2^(s*c2 - ms) for key pairs, P packed as bf16 pairs (lower key in the low half: the
+            // A-operand layout of a TMEM-sourced kind::f16 MMA), row sum over 4 pair accumulators.
+            float2 rs4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+            const float2 cc = make_float2(c2, c2), nm = make_float2(-ms, -ms);
 #pragma unroll
-            for (int u = 0; u < 8; ++u) rs8[u] = 0.f;
-#pragma unroll
-            for (int c = 0; c < kTcKeys; ++c) {
-                sv[c] = fast_exp2(fmaf(sv[c], c2, -ms));
-                rs8[c & 7] += sv[c];
+            for (int c = 0; c < kTcKeys / 2; ++c) {
+                float2 t = ffma2(make_float2(sv[2 * c], sv[2 * c + 1]), cc, nm);
+                t.x = fast_exp2(t.x);
+                t.y = fast_exp2(t.y);
+                x[c] = pack_bf16(t.x, t.y);
+                rs4[c & 3] = fadd2(rs4[c & 3], t);
             }
-            const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
-            l = l * corr + rs;
+            const float2 rs2 = fadd2(fadd2(rs4[0], rs4[1]), fadd2(rs4[2], rs4[3]));
+            l = l * corr + (rs2.x + rs2.y);
             m = m_new;
-            if (j >= 1) {  // O holds PV(0..j-1): wait for it, then rescale if the max moved
+            // O holds PV(0..j-1); it is rescaled only when the max moved by more than 2^8 (rare), once
+            // PV(j-1) has landed.  P(j) itself needs no wait: its S buffer was last read by PV(j-2),
+            // which the S(j) commit already covered.
+            if (j >= 1 && __any_sync(0xffffffffu, corr != 1.f)) {
                 ok = __all_sync(0xffffffffu, ok && tc_wait(o_done, (j - 1) & 1, deadline, abort, a.err,
                                                          KERR_TIMEOUT_MMA));
                 if (!ok) break;
                 tc_fence_after();
-                if (__any_sync(0xffffffffu, corr != 1.f)) {  // rare: the max moved by more than 2^8
+                uint32_t y[32];
 #pragma unroll 1
-                    for (int ch = 0; ch < D / 32; ++ch) {
-                        tmem_ld32(tmem_o + ch * 32 + lane_off, x);
-                        tmem_wait_ld();
+                for (int ch = 0; ch < D / 32; ++ch) {
+                    tmem_ld32(tmem_o + ch * 32 + lane_off, y);
+                    tmem_wait_ld();
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) x[i] = __float_as_uint(__uint_as_float(x[i]) * corr);
-                        tmem_st32(tmem_o + ch * 32 + lane_off, x);
-                    }
-                    tmem_wait_st();
+                    for (int i = 0; i < 32; ++i) y[i] = __float_as_uint(__uint_as_float(y[i]) * corr);
+                    tmem_st32(tmem_o + ch * 32 + lane_off, y);
                 }
+                tmem_wait_st();
             }
-            // P row -> TMEM over the S buffer just read: column c holds keys (2c, 2c+1) as bf16, the
-            // lower key in the low half (the A-operand layout of a TMEM-sourced kind::f16 MMA).
-#pragma unroll
-            for (int c = 0; c < kTcKeys / 2; ++c) x[c] = pack_bf16(sv[2 * c], sv[2 * c + 1]);
+            // P row -> TMEM over the S buffer just read.
             tmem_st32(tmem_s0 + bf * kTcKeys + lane_off, x);
             tmem_wait_st();
             tc_fence_before();
