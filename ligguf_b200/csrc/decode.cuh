@@ -364,15 +364,31 @@ __device__ __noinline__ bool merge_partials(const float* src, int count, uint8_t
         }
     }
     named_bar_sync(1, kDecodeConsumers);
-    for (int idx = tid; idx < NREP * D; idx += kDecodeConsumers) {
-        const int h = idx / D;
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        int sp = 0;
-        for (; sp + 4 <= count; sp += 4)
+    // Weighted sum: all of a thread's columns in one pass over the partials (independent loads and
+    // two accumulators per column keep the shared-memory latency overlapped).
+    constexpr int CPT = (NREP * D + kDecodeConsumers - 1) / kDecodeConsumers;  // columns per thread
+    int hh[CPT];
+    float acc[CPT][2];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) acc[u] = fmaf(pb[(sp + u) * PS + idx], w_s[(sp + u) * NREP + h], acc[u]);
-        for (; sp < count; ++sp) acc[sp & 3] = fmaf(pb[sp * PS + idx], w_s[sp * NREP + h], acc[sp & 3]);
-        o_s[idx] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+    for (int c = 0; c < CPT; ++c) {
+        hh[c] = min(tid + c * kDecodeConsumers, NREP * D - 1) / D;
+        acc[c][0] = acc[c][1] = 0.f;
+    }
+#pragma unroll 4
+    for (int sp = 0; sp < count; ++sp) {
+        const float* row = pb + sp * PS;
+        const float* wr = w_s + sp * NREP;
+#pragma unroll
+        for (int c = 0; c < CPT; ++c) {
+            const int idx = tid + c * kDecodeConsumers;
+            if (CPT * kDecodeConsumers == NREP * D || idx < NREP * D)
+                acc[c][sp & 1] = fmaf(row[idx], wr[hh[c]], acc[c][sp & 1]);
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < CPT; ++c) {
+        const int idx = tid + c * kDecodeConsumers;
+        if (idx < NREP * D) o_s[idx] = acc[c][0] + acc[c][1];
     }
     named_bar_sync(1, kDecodeConsumers);
     return true;
