@@ -224,7 +224,7 @@ int launch_decode_t(ligguf_attn* h, const lg::DecodeArgs& a, cudaStream_t st) {
     static bool attr_done[64] = {};
     LG_CUDA(ensure_smem_attr(kern, h->cfg.device, Sm::kTotal, attr_done));
     cudaLaunchConfig_t lc = {};
-    lc.gridDim = dim3(a.n_split, h->kv_dim / D, 1);
+    lc.gridDim = dim3(h->kv_dim / D, a.n_split, 1);
     lc.blockDim = dim3(lg::kDecodeThreads, 1, 1);
     lc.dynamicSmemBytes = Sm::kTotal;
     lc.stream = st;

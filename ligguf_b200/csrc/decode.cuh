@@ -430,7 +430,9 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
     uint64_t* merge_bar = empty + kDecodeStages;  // bulk copy of the partials into the ring
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int split = blockIdx.x, g = blockIdx.y;
+    // x = KV head, y = split: consecutive CTAs alternate heads, so every head's CTAs spread over all
+    // SMs and the heads (separate tile pools) see the same bandwidth and finish together.
+    const int g = blockIdx.x, split = blockIdx.y;
     const uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
     const int t_end = a.pos;  // cached positions are [0, pos); the current token is folded in last
     const bool owner = split == a.n_split - 1;

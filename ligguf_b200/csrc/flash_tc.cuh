@@ -482,14 +482,17 @@ __global__ void __launch_bounds__(kTcThreads, 2)
             const float2 rs2 = fadd2(fadd2(rs4[0], rs4[1]), fadd2(rs4[2], rs4[3]));
             l = l * corr + (rs2.x + rs2.y);
             m = m_new;
-            // O holds PV(0..j-1); it is rescaled only when the max moved by more than 2^8 (rare), once
-            // PV(j-1) has landed.  P(j) itself needs no wait: its S buffer was last read by PV(j-2),
-            // which the S(j) commit already covered.
-            if (j >= 1 && __any_sync(0xffffffffu, corr != 1.f)) {
+            // O holds PV(0..j-1).  Wait for PV(j-1) on every tile, also when O needs no rescale: a
+            // parity wait is only exact while the waiter never falls two phases behind the barrier
+            // or gets two ahead of it (skipping waits would let the epilogue's wait return before
+            // the last P.V landed).  O is rescaled only when the max moved by more than 2^8 (rare).
+            if (j >= 1) {
                 ok = __all_sync(0xffffffffu, ok && tc_wait(o_done, (j - 1) & 1, deadline, abort, a.err,
                                                          KERR_TIMEOUT_MMA));
                 if (!ok) break;
                 tc_fence_after();
+            }
+            if (j >= 1 && __any_sync(0xffffffffu, corr != 1.f)) {
                 uint32_t y[32];
 #pragma unroll 1
                 for (int ch = 0; ch < D / 32; ++ch) {
