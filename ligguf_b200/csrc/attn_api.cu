@@ -300,8 +300,11 @@ int decode_enqueue(ligguf_attn* h, int layer, int pos, const float* dq, const fl
     // CTA (finish times then differ by about one tile), larger chunks beyond.
     const int want = std::max(1, decode_blocks_per_sm(c.kv_type, h->nrep) * h->num_sms / kvh);
     a.n_split = std::max(1, std::min(want, a.n_tiles));
-    // the two-level merge handles up to kDecodeMaxGroups groups of decode_merge_group partials
-    a.n_split = std::min(a.n_split, std::min(lg::kDecodeMaxSplit, lg::kDecodeMaxGroups * lg::decode_merge_group(h->nrep, D)));
+    // The two-level merge takes groups of decode_merge_group partials (what one copy into the tile
+    // ring holds), then the group results in one more copy: at most that many groups, and at most
+    // kDecodeMaxGroups counters per head.
+    const int mg = lg::decode_merge_group(h->nrep, D);
+    a.n_split = std::min(a.n_split, std::min(lg::kDecodeMaxSplit, mg * std::min(lg::kDecodeMaxGroups, mg)));
     a.chunk = std::max(1, a.n_tiles / (a.n_split * 48));
     a.chunk_ctr = h->counters + kvh;
     a.kv_dim = h->kv_dim;

@@ -194,6 +194,20 @@ def test_back_to_back_steps_read_the_rows_they_append(gpu):
     h.close()
 
 
+@pytest.mark.parametrize("kv_head0", [0, 5])
+def test_decode_one_kv_head_two_level_merge(gpu, kv_head0):
+    """A one-KV-head shard at 4100 positions splits each head over more CTAs than two ring loads of
+    partials: the merge takes two levels (groups of partials, then the group results)."""
+    port = orc.Checker("port")
+    c = cases.decode_case(H=32, Hk=8, D=128, n_ctx=4200, theta=1e6, qk_norm=1, pos=4100, seed=91, layer=0,
+                          kv_head0=kv_head0, kv_headn=1)
+    h = make_handle(c, kv_head0=kv_head0, kv_headn=1)
+    out, _, _, _ = gpu_decode(c, h)
+    ref, _, _ = cases.run_decode(port, c)
+    assert cases.rel_err(out, ref) <= TOL
+    h.close()
+
+
 @pytest.mark.parametrize("nranks", [2, 4, 8])
 def test_sharded_decode_matches_unsharded(gpu, nranks):
     """SARA split by KV head (cpp/ligguf_distrib.cpp:665-679): the shards' outputs, concatenated in
