@@ -160,6 +160,9 @@ struct ligguf_attn {
     cudaStream_t stream = nullptr;
     float* d_stage = nullptr;  // device staging for the host-pointer calls
     size_t stage_floats = 0;
+    float* h_stage = nullptr;  // pinned, mapped host staging for the host-pointer decode
+    float* h_stage_dev = nullptr;  // its device address
+    size_t h_stage_floats = 0;
     float* qf = nullptr;  // prefill fp32 q rows
     size_t qf_floats = 0;
     __nv_bfloat16* qb = nullptr;  // prefill bf16 q rows
@@ -602,6 +605,7 @@ int ligguf_cuda_attn_free(ligguf_attn* h) {
     for (void* p : dev_ptrs)
         if (p) cudaFree(p);
     if (h->h_err) cudaFreeHost(h->h_err);
+    if (h->h_stage) cudaFreeHost(h->h_stage);
     if (h->stream) cudaStreamDestroy(h->stream);
     delete h;
     return LIGGUF_ATTN_OK;
@@ -712,6 +716,16 @@ int ligguf_cuda_attn_decode_async(ligguf_attn* h, int layer, int pos, const floa
     return decode_enqueue(h, layer, pos, d_q, d_k, d_v, d_out, static_cast<cudaStream_t>(stream), false);
 }
 
+// The device address of pinned (page-locked, mapped) host memory, or null for any other pointer.
+static void* mapped_host(const void* p) {
+    cudaPointerAttributes at{};
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();  // pageable memory unknown to CUDA: not an error for the caller
+        return nullptr;
+    }
+    return at.type == cudaMemoryTypeHost ? at.devicePointer : nullptr;
+}
+
 int ligguf_cuda_attn_decode(ligguf_attn* h, int layer, int pos, const float* q, const float* k, const float* v,
                             float* out) {
     if (!h) return fail(LIGGUF_ATTN_EINVAL, "null handle");
@@ -720,16 +734,33 @@ int ligguf_cuda_attn_decode(ligguf_attn* h, int layer, int pos, const float* q, 
     const size_t nq = size_t(h->q_headn) * h->cfg.head_dim, nk = h->kv_dim;
     int rc = grow(&h->d_stage, &h->stage_floats, 2 * nq + 2 * nk);
     if (rc) return rc;
-    float* dq = h->d_stage;
-    float* dk = dq + nq;
-    float* dv = dk + nk;
-    float* dout = dv + nk;
-    LG_CUDA(cudaMemcpyAsync(dq, q, nq * 4, cudaMemcpyHostToDevice, h->stream));
-    LG_CUDA(cudaMemcpyAsync(dk, k, nk * 4, cudaMemcpyHostToDevice, h->stream));
-    LG_CUDA(cudaMemcpyAsync(dv, v, nk * 4, cudaMemcpyHostToDevice, h->stream));
+    // q, k, v are gathered on the host into one pinned buffer and cross in one copy (every CTA of the
+    // kernel reads q, so reading it in place over the host link would fetch it hundreds of times).
+    // The output is written once, by the last CTA of each KV head, in place over the host link:
+    // into the caller's buffer when it is pinned, else into the pinned buffer and copied from there.
+    if (h->h_stage_floats < 2 * nq + 2 * nk) {
+        if (h->h_stage) cudaFreeHost(h->h_stage);
+        h->h_stage = nullptr;
+        h->h_stage_floats = 0;
+        if (cudaHostAlloc(reinterpret_cast<void**>(&h->h_stage), (2 * nq + 2 * nk) * 4, cudaHostAllocMapped) !=
+            cudaSuccess)
+            return fail(LIGGUF_ATTN_ENOMEM, "pinned staging of %zu bytes", (2 * nq + 2 * nk) * 4);
+        h->h_stage_floats = 2 * nq + 2 * nk;
+        LG_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&h->h_stage_dev), h->h_stage, 0));
+    }
+    std::memcpy(h->h_stage, q, nq * 4);
+    std::memcpy(h->h_stage + nq, k, nk * 4);
+    std::memcpy(h->h_stage + nq + nk, v, nk * 4);
+    LG_CUDA(cudaMemcpyAsync(h->d_stage, h->h_stage, (nq + 2 * nk) * 4, cudaMemcpyHostToDevice, h->stream));
+    const float* dq = h->d_stage;
+    const float* dk = h->d_stage + nq;
+    const float* dv = h->d_stage + nq + nk;
+    float* dout = static_cast<float*>(mapped_host(out));
+    const bool out_mapped = dout != nullptr;
+    if (!out_mapped) dout = h->h_stage_dev + nq + 2 * nk;
     if ((rc = decode_enqueue(h, layer, pos, dq, dk, dv, dout, h->stream, false))) return rc;
-    LG_CUDA(cudaMemcpyAsync(out, dout, nq * 4, cudaMemcpyDeviceToHost, h->stream));
     LG_CUDA(cudaStreamSynchronize(h->stream));
+    if (!out_mapped) std::memcpy(out, h->h_stage + nq + 2 * nk, nq * 4);
     return check_err_word(h->h_err, h->counters, (2 + lg::kDecodeMaxGroups) * h->kv_dim / h->cfg.head_dim);
 }
 

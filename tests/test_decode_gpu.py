@@ -160,6 +160,35 @@ def test_decode_async_device_tensors(gpu):
     h.close()
 
 
+def test_decode_host_pinned_buffers(gpu):
+    """The host-pointer call with pinned host buffers (the output is then written in place over the
+    host link) and with pageable ones (a staging copy)."""
+    import torch
+    c = cases.decode_case(H=32, Hk=8, D=128, n_ctx=2100, theta=1e6, qk_norm=1, pos=2000, seed=23, layer=0)
+    h = make_handle(c)
+    h.kv_synth(0, 1, 0, 2000, 23, 1.0)
+    ref, _, _ = cases.run_decode(orc.Checker("port"), c)
+    q, k, v = (torch.from_numpy(c[x].copy()).pin_memory() for x in ("q", "k", "v"))
+    out = torch.full((32 * 128,), float("nan")).pin_memory()
+    rc = h.lib.ligguf_cuda_attn_decode(h.handle, 0, 2000, q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr())
+    assert rc == 0, h.lib.ligguf_cuda_attn_last_error()
+    assert cases.rel_err(out.numpy(), ref) <= TOL
+    # pageable inputs and output, then pinned inputs with a pageable output
+    h.kv_synth(0, 1, 0, 2000, 23, 1.0)
+    qp, kp, vp = (np.ascontiguousarray(c[x]) for x in ("q", "k", "v"))
+    outp = np.full(32 * 128, np.nan, dtype=np.float32)
+    rc = h.lib.ligguf_cuda_attn_decode(h.handle, 0, 2000, qp.ctypes.data, kp.ctypes.data, vp.ctypes.data,
+                                       outp.ctypes.data)
+    assert rc == 0, h.lib.ligguf_cuda_attn_last_error()
+    assert cases.rel_err(outp, ref) <= TOL
+    h.kv_synth(0, 1, 0, 2000, 23, 1.0)
+    outp[:] = np.nan
+    rc = h.lib.ligguf_cuda_attn_decode(h.handle, 0, 2000, q.data_ptr(), k.data_ptr(), v.data_ptr(), outp.ctypes.data)
+    assert rc == 0, h.lib.ligguf_cuda_attn_last_error()
+    assert cases.rel_err(outp, ref) <= TOL
+    h.close()
+
+
 def test_back_to_back_steps_read_the_rows_they_append(gpu):
     """Decode steps launched back to back on one stream with no host synchronisation, alternating two
     layers: every step reads the row its layer's previous step appended.  (A decode may start loading
