@@ -271,6 +271,32 @@ def test_kv_roundtrip_fp16_state_layout(gpu):
     h.close()
 
 
+def test_gather_wait_gives_up_and_reports(gpu):
+    """A bounded in-kernel wait that runs out: a shard holding half the KV heads opens a one-rank
+    gather, so the other half's words are never stored.  The wait kernel gives up after its limit,
+    the host reads a timeout status, and the handle stays usable."""
+    import torch
+    from ligguf_b200 import LigGufAttnError
+    c = cases.decode_case(H=32, Hk=8, D=128, n_ctx=300, theta=1e6, qk_norm=1, pos=200, seed=4, layer=0,
+                          kv_head0=0, kv_headn=4)
+    h = make_handle(c, kv_head0=0, kv_headn=4)
+    h.kv_synth(0, 1, 0, 200, 4, 1.0)
+    h.gather_open(0, [h.gather_ipc_handle()])
+    dev = torch.device("cuda", 0)
+    q, k, v = (torch.from_numpy(np.ascontiguousarray(c[x])).to(dev) for x in ("q", "k", "v"))
+    full = torch.empty(32 * 128, device=dev)
+    h.decode_gather_async(0, 200, q, k, v)
+    h.gather_wait_async(0, full)
+    torch.cuda.synchronize()  # returns once the wait has given up (about 2 s)
+    with pytest.raises(LigGufAttnError) as e:
+        h.sync()
+    assert e.value.status == -4  # LIGGUF_ATTN_ETIMEDOUT
+    ref, _, _ = cases.run_decode(orc.Checker("port"), c)
+    out, _, _, _ = gpu_decode(c, h)  # still usable
+    assert cases.rel_err(out, ref) <= TOL
+    h.close()
+
+
 def test_errors_are_reported_not_fatal(gpu):
     from ligguf_b200 import LigGufAttnError
     c = cases.decode_case(H=8, Hk=2, D=64, n_ctx=16, qk_norm=1, pos=3)
