@@ -404,8 +404,21 @@ int launch_flash_tc_t(const lg::TcArgs& t, cudaStream_t st, int device) {
     auto kern = lg::flash_tc_kernel<D>;
     static bool attr_done[64] = {};
     LG_CUDA(ensure_smem_attr(kern, device, lg::TcSmem<D>::kTotal, attr_done));
-    const dim3 grid(t.q_heads, (t.q_seq + lg::kTcRows - 1) / lg::kTcRows, t.batch);
-    kern<<<grid, lg::kTcThreads, lg::TcSmem<D>::kTotal, st>>>(tq, tk, tv, t);
+    // Persistent grid: as many CTAs as are resident at once (one per SM: the runtime places one CTA
+    // of a tcgen05 kernel per SM), each walking its share of the (head, query tile, batch entry) items.
+    static int resident[64] = {};
+    int slots = device >= 0 && device < 64 ? resident[device] : 0;
+    if (slots == 0) {
+        int sms = 0, per_sm = 0;
+        LG_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+        LG_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, lg::kTcThreads, lg::TcSmem<D>::kTotal));
+        if (per_sm < 1) return fail(LIGGUF_ATTN_ECUDA, "the tensor-core attention kernel does not fit on an SM");
+        slots = sms * per_sm;
+        if (device >= 0 && device < 64) resident[device] = slots;
+    }
+    const int n_items = t.q_heads * ((t.q_seq + lg::kTcRows - 1) / lg::kTcRows) * t.batch;
+    if (n_items <= 0) return LIGGUF_ATTN_OK;
+    kern<<<std::min(n_items, slots), lg::kTcThreads, lg::TcSmem<D>::kTotal, st>>>(tq, tk, tv, t);
     LG_CUDA(cudaGetLastError());
     return LIGGUF_ATTN_OK;
 }

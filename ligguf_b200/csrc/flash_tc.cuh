@@ -4,20 +4,24 @@
 // fast/ligguf_fast_qk.cpp:340-356; BERT = fast/vdb.cpp:189-212 per sequence), with q, k, v rounded
 // to bf16 and every product accumulated in fp32 by the tensor cores.
 //
-// CTA = 128 query rows of one q head (of one batch entry), 192 threads, two CTAs per SM (96 KB of
-// shared memory and 256 TMEM columns each) so that one CTA's MMAs run while the other's softmax
-// warps work:
-//   warp 0      TMA producer: Q tile once, then K and V tiles (64 keys each) into 2-stage rings
-//   warp 1      allocates 256 TMEM columns; lane 0 issues every tcgen05.mma and commit
-//   warps 2..5  softmax: thread = query row = TMEM lane; reads S from TMEM, online softmax with
-//               exp2, writes P as bf16 pairs back into the same TMEM columns, rescales O in TMEM
-//               when the running max moves; final O / l to global memory.
-// TMEM: S double buffer at columns [0,64) and [64,128) (P of a tile overwrites the first 32 columns
-// of its S buffer), O at [128, 128+D).  MMA order S0, S1, PV0, S2, PV1, ...: S = Q.K^T with both
-// operands in shared memory (K-major, SWIZZLE_128B); O += P.V with P read from TMEM and V from
-// shared memory (MN-major, SWIZZLE_128B).  MMAs of one CTA execute in issue order, so PV(j) has read
-// P(j) before S(j+2) overwrites that buffer.  Every wait is bounded; on a timeout the kernel records
-// an error, drains its own copies and MMAs, frees TMEM and returns.
+// Work item = 128 query rows (one tile) of one q head of one batch entry.  A kernel that uses
+// tcgen05 runs one CTA per SM, so the grid is persistent: one CTA per SM walks a fixed share of the
+// items, keeping its barriers and all 512 TMEM columns across them, and the overlap of tensor-core
+// work with softmax work comes from inside the CTA (320 threads):
+//   warp 0      TMA producer: per item the Q tile (double-buffered), then K and V tiles of 128 keys
+//               into a 2-stage ring (4 for D = 64)
+//   warp 1      allocates TMEM; lane 0 issues every tcgen05.mma and commit
+//   warps 2..5  softmax: thread = query row = TMEM lane; reads S from TMEM twice (row max, then
+//               exp2), writes P as bf16 pairs back into the same TMEM columns, rescales O in TMEM
+//               when the running max moves (rare); row sums to shared memory
+//   warps 6..9  epilogue: O / l from TMEM to global memory, so the softmax warps never wait for it
+// TMEM: S double buffer [0, 256), O double-buffered by item after it.  The issuing thread is the
+// bottleneck of this design (each MMA and each mbarrier wait costs it ~70-200 cycles), so tiles are
+// 128 keys wide: S = Q.K^T is 8 MMAs of M128 N128 K16 (Q and K from shared memory, K-major,
+// SWIZZLE_128B) and O += P.V 8 MMAs of M128 N=D K16 (P from TMEM, V from shared memory, MN-major,
+// SWIZZLE_128B).  MMA order S0, S1, PV0, S2, PV1, ... across items; MMAs of one CTA execute in issue
+// order, so PV(t) has read P(t) before S(t+2) overwrites that buffer.  Every wait is bounded; on a
+// timeout the kernel records an error, drains its own copies and MMAs, frees TMEM and returns.
 #pragma once
 
 #include "common.cuh"
@@ -80,27 +84,40 @@ __global__ void __launch_bounds__(256) bert_to_bf16_kernel(const float* __restri
 }
 
 constexpr int kTcRows = 128;  // query rows per tile (UMMA M)
-constexpr int kTcKeys = 64;   // keys per tile (UMMA N of S, K of P.V)
-constexpr int kTcThreads = 192;
-constexpr uint32_t kTcTmemCols = 256;
-constexpr uint32_t kTcTmemO = 128;  // first TMEM column of O
+constexpr int kTcKeys = 128;  // keys per tile (UMMA N of S, K of P.V)
+constexpr int kTcThreads = 320;
+// A kernel that uses tcgen05 runs one CTA per SM, which then owns all 512 TMEM columns:
+// S double buffer [0, 256) (P of a tile is packed over the first 64 columns of its S buffer),
+// O double buffer (by item) [256, 256 + 2D).
+constexpr uint32_t kTcTmemCols = 512;
+template <int D>
+struct TcTmem {
+    static constexpr uint32_t kS = 0;
+    static constexpr uint32_t kO = 2 * kTcKeys;
+    static_assert(kO + 2 * D <= kTcTmemCols, "TMEM plan exceeds 512 columns");
+};
 
 template <int D>
 struct TcSmem {
     static constexpr int kChunks = D / 64;               // 128-byte column chunks of a row
-    static constexpr int kQBytes = kTcRows * D * 2;      // the Q tile: 128 rows of bf16
-    static constexpr int kQChunkBytes = kTcRows * 128;   // one 128-byte-wide chunk of Q
-    static constexpr int kKvBytes = kTcKeys * D * 2;     // a K or V tile: 64 rows of bf16
+    static constexpr int kQBytes = kTcRows * D * 2;      // a Q tile: 128 rows of bf16
+    static constexpr int kQChunkBytes = kTcRows * 128;   // one 128-byte-wide chunk of a Q tile
+    static constexpr int kKvBytes = kTcKeys * D * 2;     // a K or V tile: 128 rows of bf16
     static constexpr int kKvChunkBytes = kTcKeys * 128;  // one 128-byte-wide chunk of a K/V tile
-    // D = 64 takes 4 stages: besides the deeper ring, 80 KB keeps a third CTA (whose TMEM allocation
-    // would have to wait for one of the two resident CTAs to finish) off the SM.
-    static constexpr int kStages = D == 128 ? 2 : 4;
-    static constexpr size_t kQ = 0;
-    static constexpr size_t kK = kQ + kQBytes;
+    static constexpr int kStages = D == 128 ? 2 : 4;     // K/V ring: 128 KB either way
+    static constexpr int kLRing = 4;                     // row-sum slots (by item)
+    static constexpr size_t kQ = 0;                      // Q double buffer (by item)
+    static constexpr size_t kK = kQ + 2 * size_t(kQBytes);
     static constexpr size_t kV = kK + size_t(kStages) * kKvBytes;
-    static constexpr size_t kBar = kV + size_t(kStages) * kKvBytes;
-    // q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], s_free[2], p_full, o_done, drain
-    static constexpr int kNumBars = 1 + 4 * kStages + 2 + 2 + 1 + 1 + 1;
+    static constexpr size_t kL = kV + size_t(kStages) * kKvBytes;  // row sums l, [kLRing][128] fp32
+    // Epilogue staging: per epilogue warp a 32 x 32 fp32 block, rows padded to 36 floats (16-byte
+    // aligned, conflict-free float4 accesses both ways).
+    static constexpr int kStageRow = 36;
+    static constexpr size_t kE = kL + size_t(kLRing) * kTcRows * 4;
+    static constexpr size_t kBar = kE + 4 * 32 * kStageRow * 4;
+    // k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2], o_done, drain, q_full[2],
+    // q_empty[2], o_final[2], o_free[2], l_full[kLRing]
+    static constexpr int kNumBars = 4 * kStages + 2 + 2 + 1 + 1 + 8 + kLRing;
     static constexpr size_t kMisc = kBar + size_t(kNumBars) * 8;  // tmem base, abort flag
     static constexpr size_t kTotal = kMisc + 16 + 1024;           // + slack to align the base to 1 KB
 };
@@ -197,6 +214,15 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
         LG_W32(r)
         : "memory");
 }
+// 16 consecutive 32-bit columns of this thread's TMEM lane from r[0..15].
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+        "%14, %15, %16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -248,57 +274,75 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
     return d;
 }
 
+// One work item: 128 query rows (one tile) of one head of one batch entry.  n_kv == 0 marks an item
+// of padded query rows only, which is written as zeros and never reaches the tensor cores.
+struct TcItem {
+    int h, b, r0, nq_valid, kv_len, n_kv;
+};
+// Items are numbered head fastest, then query tile from the last (longest under the causal mask)
+// to the first, then batch entry, so that the heaviest items come first.
+__device__ __forceinline__ TcItem tc_item(const TcArgs& a, int idx, int n_qt) {
+    TcItem it;
+    it.h = idx % a.q_heads;
+    const int y = (idx / a.q_heads) % n_qt;
+    it.b = idx / (a.q_heads * n_qt);
+    it.r0 = (n_qt - 1 - y) * kTcRows;
+    it.nq_valid = a.lens ? min(a.lens[it.b], a.q_seq) : a.q_seq;
+    it.kv_len = a.lens ? min(a.lens[it.b], a.kv_seq) : a.kv_seq;
+    int kv_eff = it.kv_len;
+    if (a.causal) kv_eff = min(kv_eff, a.q_pos0 + min(it.r0 + kTcRows, it.nq_valid));
+    it.n_kv = it.r0 >= it.nq_valid ? 0 : max(0, (kv_eff + kTcKeys - 1) / kTcKeys);
+    return it;
+}
+// The w-th item of this CTA.  The grid is persistent (as many CTAs as fit at once) and walks the
+// items in waves of gridDim.x, every other wave in reverse CTA order: with the heaviest items
+// first, the CTA that took the heaviest item of one wave takes the lightest of the next.
+__device__ __forceinline__ int tc_item_index(int w) {
+    const int G = gridDim.x;
+    return w * G + ((w & 1) ? G - 1 - static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x));
+}
+
 template <int D>
-__global__ void __launch_bounds__(kTcThreads, 2)
+__global__ void __launch_bounds__(kTcThreads, 1)
     flash_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const TcArgs a) {
     using Sm = TcSmem<D>;
+    using Tm = TcTmem<D>;
     constexpr int S = Sm::kStages;
     constexpr int NCH = Sm::kChunks;
+    constexpr int LR = Sm::kLRing;
     extern __shared__ uint8_t tc_smem_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + Sm::kBar);
-    uint64_t* q_full = bars;
-    uint64_t* k_full = bars + 1;
+    uint64_t* k_full = bars;
     uint64_t* k_empty = k_full + S;
     uint64_t* v_full = k_empty + S;
     uint64_t* v_empty = v_full + S;
     uint64_t* s_full = v_empty + S;
-    uint64_t* s_free = s_full + 2;
-    uint64_t* p_full = s_free + 2;
-    uint64_t* o_done = p_full + 1;
+    // p_full[t & 1]: the four softmax warps wrote P(t).  Two barriers, because a warp may finish tile
+    // t + 1 before a slower warp finishes tile t (it never gets two tiles ahead: S(t+2) is issued
+    // after P.V(t), which waits for all four arrivals of tile t).
+    uint64_t* p_full = s_full + 2;
+    uint64_t* o_done = p_full + 2;    // every P.V (waited by the softmax only before a rescale)
     uint64_t* drain = o_done + 1;
+    uint64_t* q_full = drain + 1;     // [2] Q tile of an item landed
+    uint64_t* q_empty = q_full + 2;   // [2] the item's last S MMA completed: its Q buffer is free
+    uint64_t* o_final = q_empty + 2;  // [2] the item's last P.V completed: O is final
+    uint64_t* o_free = o_final + 2;   // [2] the epilogue has read O
+    uint64_t* l_full = o_free + 2;    // [LR] the item's row sums are in shared memory
+    float* lsum = reinterpret_cast<float*>(sm + Sm::kL);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Sm::kMisc);
     volatile int* abort = reinterpret_cast<volatile int*>(sm + Sm::kMisc + 4);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_qt = (a.q_seq + kTcRows - 1) / kTcRows;
-    // Blocks start in linear order (x fastest): x = head, y = query tile from the last (longest under
-    // the causal mask) to the first, so every wave takes the heaviest remaining tiles of all heads.
-    const int h = blockIdx.x, b = blockIdx.z;
-    const int qt = n_qt - 1 - static_cast<int>(blockIdx.y);
-    const int g = h / a.nrep;
-    const int r0 = qt * kTcRows;
-    const int nq_valid = a.lens ? min(a.lens[b], a.q_seq) : a.q_seq;
-    const int kv_len = a.lens ? min(a.lens[b], a.kv_seq) : a.kv_seq;
-    const uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
-
-    if (r0 >= nq_valid) {  // padded query rows only: zeros (uniform for the CTA)
-        for (int i = threadIdx.x; i < kTcRows * D; i += kTcThreads) {
-            const int r = r0 + i / D;
-            if (r < a.q_seq)
-                a.out[((static_cast<size_t>(b) * a.q_seq + r) * a.q_heads + h) * D + (i % D)] = 0.f;
-        }
-        return;
-    }
-    int kv_eff = kv_len;
-    if (a.causal) kv_eff = min(kv_eff, a.q_pos0 + min(r0 + kTcRows, nq_valid));
-    const int n_kv = (kv_eff + kTcKeys - 1) / kTcKeys;
-    const int q_row0 = b * a.q_seq + r0;
-    const int kv_row0 = b * a.kv_seq;
+    const int n_items = a.q_heads * n_qt * a.batch;
+    // Every role walks the same item sequence.  Key tiles of all items are numbered in one sequence
+    // (t): stage t % S of the K/V ring, S and P buffer t & 1, one o_done phase per tile.
+    // Items that have key tiles are numbered z: Q and O buffer z & 1 (one q_full / q_empty /
+    // o_final / o_free phase per item on that buffer's barrier) and row-sum slot z % LR.
 
     if (threadIdx.x == 0) {
-        mbar_init(q_full, 1);
         for (int s = 0; s < S; ++s) {
             mbar_init(&k_full[s], 1);
             mbar_init(&k_empty[s], 1);
@@ -307,9 +351,14 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&s_full[i], 1);
-            mbar_init(&s_free[i], 4);
+            mbar_init(&q_full[i], 1);
+            mbar_init(&q_empty[i], 1);
+            mbar_init(&o_final[i], 1);
+            mbar_init(&o_free[i], 4);
         }
-        mbar_init(p_full, 4);
+        for (int i = 0; i < LR; ++i) mbar_init(&l_full[i], 4);
+        mbar_init(&p_full[0], 4);
+        mbar_init(&p_full[1], 4);
         mbar_init(o_done, 1);
         mbar_init(drain, 1);
         *abort = 0;
@@ -320,37 +369,58 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t tmem_s0 = tmem, tmem_o = tmem + kTcTmemO;
 
     if (warp == 0) {
         // ------------------------------------------------------------------ TMA producer
         if (lane == 0) {
-            int issued = 0;
-            mbar_arrive_expect_tx(q_full, Sm::kQBytes);
-            for (int c = 0; c < NCH; ++c)
-                tma_load_3d(sm + Sm::kQ + c * Sm::kQChunkBytes, &tm_q, q_full, 64 * c, h, q_row0);
-            for (int j = 0; j < n_kv; ++j) {
-                const int s = j % S;
-                const uint32_t par = ((j / S) - 1) & 1;
-                if (j >= S && !tc_wait(&k_empty[s], par, deadline, abort, a.err, KERR_TIMEOUT_EMPTY)) break;
-                mbar_arrive_expect_tx(&k_full[s], Sm::kKvBytes);
-                for (int c = 0; c < NCH; ++c)
-                    tma_load_3d(sm + Sm::kK + s * Sm::kKvBytes + c * Sm::kKvChunkBytes, &tm_k, &k_full[s], 64 * c,
-                                g, kv_row0 + j * kTcKeys);
-                if (j >= S && !tc_wait(&v_empty[s], par, deadline, abort, a.err, KERR_TIMEOUT_EMPTY)) {
-                    ++issued;  // the K half of this stage is in flight
+            int t = 0, z = 0, issued = 0;  // issued: tiles whose copies are in flight or landed
+            bool ok = true;
+            uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
+            for (int w = 0; ok; ++w) {
+                const int idx = tc_item_index(w);
+                if (idx >= n_items) break;
+                const TcItem it = tc_item(a, idx, n_qt);
+                if (it.n_kv == 0) continue;
+                deadline = globaltimer_ns() + kWaitLimitNs;
+                // Q of item z into buffer z & 1, once the last S MMA of item z - 2 has read it.
+                const int qb = z & 1;
+                if (z >= 2 && !tc_wait(&q_empty[qb], ((z >> 1) - 1) & 1, deadline, abort, a.err, KERR_TIMEOUT_EMPTY))
                     break;
-                }
-                mbar_arrive_expect_tx(&v_full[s], Sm::kKvBytes);
+                mbar_arrive_expect_tx(&q_full[qb], Sm::kQBytes);
                 for (int c = 0; c < NCH; ++c)
-                    tma_load_3d(sm + Sm::kV + s * Sm::kKvBytes + c * Sm::kKvChunkBytes, &tm_v, &v_full[s], 64 * c,
-                                g, kv_row0 + j * kTcKeys);
-                ++issued;
+                    tma_load_3d(sm + Sm::kQ + qb * Sm::kQBytes + c * Sm::kQChunkBytes, &tm_q, &q_full[qb], 64 * c,
+                                it.h, it.b * a.q_seq + it.r0);
+                ++z;
+                const int g = it.h / a.nrep, kv_row0 = it.b * a.kv_seq;
+                for (int j = 0; j < it.n_kv; ++j, ++t) {
+                    const int s = t % S;
+                    const uint32_t par = ((t / S) - 1) & 1;
+                    if (t >= S && !tc_wait(&k_empty[s], par, deadline, abort, a.err, KERR_TIMEOUT_EMPTY)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&k_full[s], Sm::kKvBytes);
+                    for (int c = 0; c < NCH; ++c)
+                        tma_load_3d(sm + Sm::kK + s * Sm::kKvBytes + c * Sm::kKvChunkBytes, &tm_k, &k_full[s],
+                                    64 * c, g, kv_row0 + j * kTcKeys);
+                    if (t >= S && !tc_wait(&v_empty[s], par, deadline, abort, a.err, KERR_TIMEOUT_EMPTY)) {
+                        ++issued;  // the K half of this stage is in flight
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&v_full[s], Sm::kKvBytes);
+                    for (int c = 0; c < NCH; ++c)
+                        tma_load_3d(sm + Sm::kV + s * Sm::kKvBytes + c * Sm::kKvChunkBytes, &tm_v, &v_full[s],
+                                    64 * c, g, kv_row0 + j * kTcKeys);
+                    ++issued;
+                }
             }
-            // Drain: the last copies issued into each stage must land before the CTA exits.
+            // Drain: the last copies issued into each buffer must land before the CTA exits.  No copy
+            // is issued after these, so each barrier rests on the phase waited for here.
             const uint64_t dd = deadline + kWaitLimitNs / 2;
-            while (!mbar_try_wait(q_full, 0) && globaltimer_ns() < dd) {
-            }
+            for (int i = max(0, z - 2); i < z; ++i)
+                while (!mbar_try_wait(&q_full[i & 1], (i >> 1) & 1) && globaltimer_ns() < dd) {
+                }
             for (int j = max(0, issued - S); j < issued; ++j) {
                 const int s = j % S;
                 const uint32_t par = (j / S) & 1;
@@ -370,170 +440,272 @@ __global__ void __launch_bounds__(kTcThreads, 2)
             const uint64_t q_desc = smem_desc_sw128(smem_u32(sm + Sm::kQ), 16, 1024);
             const uint64_t k_desc = smem_desc_sw128(smem_u32(sm + Sm::kK), 16, 1024);
             const uint64_t v_desc = smem_desc_sw128(smem_u32(sm + Sm::kV), Sm::kKvChunkBytes, 1024);
-            bool ok = tc_wait(q_full, 0, deadline, abort, a.err, KERR_TIMEOUT_FULL);
-            auto issue_pv = [&](int i) -> bool {
-                const int s = i % S;
-                if (!tc_wait(p_full, i & 1, deadline, abort, a.err, KERR_TIMEOUT_MMA)) return false;
+            bool ok = true;
+            uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
+            // The P.V of tile t - 1 is issued after the S of tile t, so that S(t) overlaps the softmax
+            // of t - 1, also across items.  pend: the tile whose P.V is still to issue (-1: none),
+            // of item pend_z, first / last tile of that item.
+            int pend = -1, pend_z = 0;
+            bool pend_first = false, pend_last = false;
+            auto issue_pv = [&]() -> bool {
+                const int i = pend, s = i % S, ob = pend_z & 1;
+                // The first P.V of item z overwrites O buffer z & 1: item z - 2's epilogue must have read it.
+                if (pend_first && pend_z >= 2 &&
+                    !tc_wait(&o_free[ob], ((pend_z >> 1) - 1) & 1, deadline, abort, a.err, KERR_TIMEOUT_MMA))
+                    return false;
+                if (!tc_wait(&p_full[i & 1], (i >> 1) & 1, deadline, abort, a.err, KERR_TIMEOUT_MMA)) return false;
                 if (!tc_wait(&v_full[s], (i / S) & 1, deadline, abort, a.err, KERR_TIMEOUT_FULL)) return false;
                 tc_fence_after();
-                const uint32_t p_tmem = tmem_s0 + (i & 1) * kTcKeys;  // P(i) packed in its S buffer
+                const uint32_t p_tmem = tmem + Tm::kS + (i & 1) * kTcKeys;  // P(i) packed in its S buffer
+                const uint32_t o_tmem = tmem + Tm::kO + ob * D;
                 const uint64_t vd = desc_advance(v_desc, s * Sm::kKvBytes);
-                umma_ts(tmem_o, p_tmem, vd, kIdO, i > 0 ? 1u : 0u);
+                umma_ts(o_tmem, p_tmem, vd, kIdO, pend_first ? 0u : 1u);
 #pragma unroll
                 for (int kk = 1; kk < kTcKeys / 16; ++kk)
-                    umma_ts(tmem_o, p_tmem + kk * 8, desc_advance(vd, kk * 2048), kIdO, 1u);
+                    umma_ts(o_tmem, p_tmem + kk * 8, desc_advance(vd, kk * 2048), kIdO, 1u);
                 umma_commit(o_done);
                 umma_commit(&v_empty[s]);
+                if (pend_last) umma_commit(&o_final[ob]);
+                pend = -1;
                 return true;
             };
-            for (int j = 0; ok && j < n_kv; ++j) {
-                const int s = j % S, bf = j & 1;
-                if (!tc_wait(&k_full[s], (j / S) & 1, deadline, abort, a.err, KERR_TIMEOUT_FULL)) break;
-                if (j >= 2 && !tc_wait(&s_free[bf], ((j >> 1) - 1) & 1, deadline, abort, a.err, KERR_TIMEOUT_MMA))
-                    break;
-                tc_fence_after();
-                const uint64_t kd = desc_advance(k_desc, s * Sm::kKvBytes);
-                const uint32_t d_tmem = tmem_s0 + bf * kTcKeys;
+            int t = 0, z = 0;
+            for (int w = 0; ok; ++w) {
+                const int idx = tc_item_index(w);
+                if (idx >= n_items) break;
+                const int n_kv = tc_item(a, idx, n_qt).n_kv;
+                if (n_kv == 0) continue;
+                deadline = globaltimer_ns() + kWaitLimitNs;
+                const int qb = z & 1;
+                if (!tc_wait(&q_full[qb], (z >> 1) & 1, deadline, abort, a.err, KERR_TIMEOUT_FULL)) break;
+                const uint64_t qd = desc_advance(q_desc, qb * Sm::kQBytes);
+                for (int j = 0; j < n_kv; ++j, ++t) {
+                    const int s = t % S, bf = t & 1;
+                    // S buffer bf held S(t-2) and P(t-2): P.V(t-2), issued above after p_full(t-2), reads
+                    // it before this S MMA writes it (MMAs of one CTA execute in issue order).
+                    if (!tc_wait(&k_full[s], (t / S) & 1, deadline, abort, a.err, KERR_TIMEOUT_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t kd = desc_advance(k_desc, s * Sm::kKvBytes);
+                    const uint32_t d_tmem = tmem + Tm::kS + bf * kTcKeys;
 #pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint32_t qoff = (kk >> 2) * Sm::kQChunkBytes + (kk & 3) * 32;
-                    const uint32_t koff = (kk >> 2) * Sm::kKvChunkBytes + (kk & 3) * 32;
-                    umma_ss(d_tmem, desc_advance(q_desc, qoff), desc_advance(kd, koff), kIdS, kk > 0 ? 1u : 0u);
+                    for (int kk = 0; kk < D / 16; ++kk) {
+                        const uint32_t qoff = (kk >> 2) * Sm::kQChunkBytes + (kk & 3) * 32;
+                        const uint32_t koff = (kk >> 2) * Sm::kKvChunkBytes + (kk & 3) * 32;
+                        umma_ss(d_tmem, desc_advance(qd, qoff), desc_advance(kd, koff), kIdS, kk > 0 ? 1u : 0u);
+                    }
+                    umma_commit(&s_full[bf]);
+                    umma_commit(&k_empty[s]);
+                    if (j == n_kv - 1) umma_commit(&q_empty[qb]);
+                    if (pend >= 0 && !issue_pv()) {
+                        ok = false;
+                        break;
+                    }
+                    pend = t;
+                    pend_first = j == 0;
+                    pend_last = j == n_kv - 1;
+                    pend_z = z;
                 }
-                umma_commit(&s_full[bf]);
-                umma_commit(&k_empty[s]);
-                if (j >= 1 && !issue_pv(j - 1)) {
-                    ok = false;
-                    break;
-                }
+                ++z;
             }
-            if (ok && !*abort) issue_pv(n_kv - 1);
+            if (ok && pend >= 0 && !*abort) issue_pv();
             // Drain: every MMA issued above completes before TMEM is freed.
             umma_commit(drain);
             const uint64_t dd = deadline + kWaitLimitNs / 2;
             while (!mbar_try_wait(drain, 0) && globaltimer_ns() < dd) {
             }
         }
-    } else {
+    } else if (warp < 6) {
         // ------------------------------------------------------------------ softmax warpgroup
-        const int quarter = warp & 3;                  // TMEM lanes [32*quarter, 32*quarter+32)
-        const int row = quarter * 32 + lane;           // query row within the tile
-        const int qr = r0 + row;                       // query row within the sequence
-        const bool row_valid = qr < nq_valid;
+        const int quarter = warp & 3;         // TMEM lanes [32*quarter, 32*quarter+32)
+        const int row = quarter * 32 + lane;  // query row within the tile
         const uint32_t lane_off = uint32_t(quarter * 32) << 16;
         const float c2 = a.scale_log2;
-        float m = -INFINITY, l = 0.f;
         bool ok = true;
-        uint32_t x[32];
-        for (int j = 0; j < n_kv; ++j) {
-            const int bf = j & 1;
-            ok = __all_sync(0xffffffffu, ok && tc_wait(&s_full[bf], (j >> 1) & 1, deadline, abort, a.err,
-                                                     KERR_TIMEOUT_MMA));
-            if (!ok) break;
-            tc_fence_after();
-            uint32_t raw[kTcKeys];
-#pragma unroll
-            for (int ch = 0; ch < kTcKeys / 32; ++ch)
-                tmem_ld32p(tmem_s0 + bf * kTcKeys + ch * 32 + lane_off, raw + ch * 32);
-            tmem_wait_ld();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s_free[bf]);
-            float sv[kTcKeys];
-#pragma unroll
-            for (int c = 0; c < kTcKeys; ++c) sv[c] = __uint_as_float(raw[c]);
-
-            const int k0 = j * kTcKeys;  // key position of column 0 (sequence-relative)
-            const bool edge = (k0 + kTcKeys > kv_len) || (a.causal && k0 + kTcKeys - 1 > a.q_pos0 + r0);
-            if (edge) {
-                const int lim_c = kv_len - k0;
-                const int lim_r = a.causal ? a.q_pos0 + qr - k0 : kTcKeys;
-#pragma unroll
-                for (int c = 0; c < kTcKeys; ++c) sv[c] = (c < lim_c && c <= lim_r) ? sv[c] : -INFINITY;
-            }
-            // Row max with 8 independent chains of three-input max.
-            float mx8[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) mx8[u] = sv[u];
-#pragma unroll
-            for (int c = 8; c < kTcKeys; c += 16)
-#pragma unroll
-                for (int u = 0; u < 8; ++u) mx8[u] = fmax3(mx8[u], sv[c + u], sv[c + 8 + u]);
-            const float mx = fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
-            // The running max (log2 units) only moves when the tile max exceeds it by more than 8:
-            // p = 2^(s*c2 - m) then stays <= 256 and O/l are rescaled rarely; the normalisation at
-            // the end uses the same m, so the result is unchanged.
-            const float mt = mx * c2;
-            const float m_new = (m == -INFINITY || mt > m + 8.0f) ? mt : m;
-            const float ms = m_new == -INFINITY ? 0.f : m_new;
-            const float corr = (m == m_new || m_new == -INFINITY) ? 1.f : fast_exp2(m - m_new);
-            // p = 2^(s*c2 - ms) for key pairs, P packed as bf16 pairs (lower key in the low half: the
-            // A-operand layout of a TMEM-sourced kind::f16 MMA), row sum over 4 pair accumulators.
-            float2 rs4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-            const float2 cc = make_float2(c2, c2), nm = make_float2(-ms, -ms);
-#pragma unroll
-            for (int c = 0; c < kTcKeys / 2; ++c) {
-                float2 t = ffma2(make_float2(sv[2 * c], sv[2 * c + 1]), cc, nm);
-                t.x = fast_exp2(t.x);
-                t.y = fast_exp2(t.y);
-                x[c] = pack_bf16(t.x, t.y);
-                rs4[c & 3] = fadd2(rs4[c & 3], t);
-            }
-            const float2 rs2 = fadd2(fadd2(rs4[0], rs4[1]), fadd2(rs4[2], rs4[3]));
-            l = l * corr + (rs2.x + rs2.y);
-            m = m_new;
-            // O holds PV(0..j-1).  Wait for PV(j-1) on every tile, also when O needs no rescale: a
-            // parity wait is only exact while the waiter never falls two phases behind the barrier
-            // or gets two ahead of it (skipping waits would let the epilogue's wait return before
-            // the last P.V landed).  O is rescaled only when the max moved by more than 2^8 (rare).
-            if (j >= 1) {
-                ok = __all_sync(0xffffffffu, ok && tc_wait(o_done, (j - 1) & 1, deadline, abort, a.err,
+        int t = 0, z = 0;
+        for (int w = 0; ok; ++w) {
+            const int idx = tc_item_index(w);
+            if (idx >= n_items) break;
+            const TcItem it = tc_item(a, idx, n_qt);
+            if (it.n_kv == 0) continue;
+            const uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
+            const int qr = it.r0 + row;  // query row within the sequence
+            const int r0 = it.r0, kv_len = it.kv_len, n_kv = it.n_kv;
+            const uint32_t o_tmem = tmem + Tm::kO + (z & 1) * D + lane_off;
+            float m = -INFINITY, l = 0.f;
+            for (int j = 0; j < n_kv; ++j, ++t) {
+                const int bf = t & 1;
+                const uint32_t s_tmem = tmem + Tm::kS + bf * kTcKeys + lane_off;
+                ok = __all_sync(0xffffffffu, ok && tc_wait(&s_full[bf], (t >> 1) & 1, deadline, abort, a.err,
                                                          KERR_TIMEOUT_MMA));
                 if (!ok) break;
                 tc_fence_after();
-            }
-            if (j >= 1 && __any_sync(0xffffffffu, corr != 1.f)) {
-                uint32_t y[32];
-#pragma unroll 1
-                for (int ch = 0; ch < D / 32; ++ch) {
-                    tmem_ld32(tmem_o + ch * 32 + lane_off, y);
-                    tmem_wait_ld();
+                const int k0 = j * kTcKeys;  // key position of column 0 (sequence-relative)
+                const bool edge = (k0 + kTcKeys > kv_len) || (a.causal && k0 + kTcKeys - 1 > a.q_pos0 + r0);
+                // Columns c < lim of this tile are visible to this row (key < kv_len, and key <= the
+                // row's position under the causal mask).
+                const int lim = min(kv_len - k0, a.causal ? a.q_pos0 + qr - k0 + 1 : kTcKeys);
+                // Pass 1, row max: 64 columns per TMEM load, 8 independent chains of three-input max.
+                float mx8[8];
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) y[i] = __float_as_uint(__uint_as_float(y[i]) * corr);
-                    tmem_st32(tmem_o + ch * 32 + lane_off, y);
+                for (int u = 0; u < 8; ++u) mx8[u] = -INFINITY;
+#pragma unroll
+                for (int hc = 0; hc < kTcKeys / 64; ++hc) {
+                    uint32_t r[64];
+                    tmem_ld32p(s_tmem + hc * 64, r);
+                    tmem_ld32p(s_tmem + hc * 64 + 32, r + 32);
+                    tmem_wait_ld();
+                    if (edge)
+#pragma unroll
+                        for (int c = 0; c < 64; ++c)
+                            if (hc * 64 + c >= lim) r[c] = __float_as_uint(-INFINITY);
+#pragma unroll
+                    for (int c = 0; c < 64; c += 16)
+#pragma unroll
+                        for (int u = 0; u < 8; ++u)
+                            mx8[u] = fmax3(mx8[u], __uint_as_float(r[c + u]), __uint_as_float(r[c + 8 + u]));
                 }
+                const float mx =
+                    fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
+                // The running max (log2 units) only moves when the tile max exceeds it by more than 8:
+                // p = 2^(s*c2 - m) then stays <= 256 and O/l are rescaled rarely; the normalisation at
+                // the end uses the same m, so the result is unchanged.
+                const float mt = mx * c2;
+                const float m_new = (m == -INFINITY || mt > m + 8.0f) ? mt : m;
+                const float ms = m_new == -INFINITY ? 0.f : m_new;
+                const float corr = (m == m_new || m_new == -INFINITY) ? 1.f : fast_exp2(m - m_new);
+                m = m_new;
+                // O holds P.V of tiles 0..j-1 of this item once o_done's phase t-1 has completed.  It is
+                // waited for only before a rescale (rare).  That wait is exact: s_full(t), waited above,
+                // was committed after P.V(t-2) was issued, so phase t-2 is complete, and P.V(t) cannot
+                // start before this warp's p_full(t) below, so phase t is not.
+                if (j >= 1 && __any_sync(0xffffffffu, corr != 1.f)) {
+                    ok = __all_sync(0xffffffffu, ok && tc_wait(o_done, (t - 1) & 1, deadline, abort, a.err,
+                                                             KERR_TIMEOUT_MMA));
+                    if (!ok) break;
+                    tc_fence_after();
+                    uint32_t y[32];
+#pragma unroll 1
+                    for (int ch = 0; ch < D / 32; ++ch) {
+                        tmem_ld32(o_tmem + ch * 32, y);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) y[i] = __float_as_uint(__uint_as_float(y[i]) * corr);
+                        tmem_st32(o_tmem + ch * 32, y);
+                    }
+                    tmem_wait_st();
+                }
+                // Pass 2: p = 2^(s*c2 - ms) for key pairs, P packed as bf16 pairs (lower key in the low
+                // half: the A-operand layout of a TMEM-sourced kind::f16 MMA) over the first kTcKeys/2
+                // columns of the S buffer.  P of columns [64h, 64h+64) lands in columns [32h, 32h+32),
+                // at or below the columns already read.  Row sum over 4 pair accumulators.
+                float2 rs4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                                 make_float2(0.f, 0.f)};
+                const float2 cc = make_float2(c2, c2), nm = make_float2(-ms, -ms);
+#pragma unroll
+                for (int hc = 0; hc < kTcKeys / 64; ++hc) {
+                    uint32_t r[64];
+                    tmem_ld32p(s_tmem + hc * 64, r);
+                    tmem_ld32p(s_tmem + hc * 64 + 32, r + 32);
+                    tmem_wait_ld();
+                    if (edge)
+#pragma unroll
+                        for (int c = 0; c < 64; ++c)
+                            if (hc * 64 + c >= lim) r[c] = __float_as_uint(-INFINITY);
+                    uint32_t pk[32];
+#pragma unroll
+                    for (int c = 0; c < 32; ++c) {
+                        float2 e = ffma2(make_float2(__uint_as_float(r[2 * c]), __uint_as_float(r[2 * c + 1])), cc, nm);
+                        e.x = fast_exp2(e.x);
+                        e.y = fast_exp2(e.y);
+                        pk[c] = pack_bf16(e.x, e.y);
+                        rs4[c & 3] = fadd2(rs4[c & 3], e);
+                    }
+                    tmem_st32(s_tmem + hc * 32, pk);
+                }
+                const float2 rs2 = fadd2(fadd2(rs4[0], rs4[1]), fadd2(rs4[2], rs4[3]));
+                l = l * corr + (rs2.x + rs2.y);
                 tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&p_full[bf]);
             }
-            // P row -> TMEM over the S buffer just read.
-            tmem_st32(tmem_s0 + bf * kTcKeys + lane_off, x);
-            tmem_wait_st();
+            if (!ok) break;
+            // The row sums go to the epilogue warps through shared memory.
+            lsum[(z % LR) * kTcRows + row] = l;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&l_full[z % LR]);
+            ++z;
+        }
+        tc_fence_before();
+    } else {
+        // ------------------------------------------------------------------ epilogue warpgroup
+        // Per item z: row sums from shared memory, O buffer z & 1 from TMEM once the last P.V has
+        // completed, O / l to the output rows, then O buffer z & 1 is handed back to the MMA issuer.
+        // A thread holds one row of O, so each warp passes 32 x 32 blocks through a padded staging
+        // block and stores whole 128-byte row segments (8 lanes per row, 4 rows per instruction):
+        // row-per-lane stores would touch 32 rows per instruction and crowd the shared-memory path
+        // that the MMAs read their operands through.
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        const uint32_t lane_off = uint32_t(quarter * 32) << 16;
+        float* stg = reinterpret_cast<float*>(sm + Sm::kE) + quarter * 32 * Sm::kStageRow;
+        const int sub = lane >> 3, quad = lane & 7;  // transposed access: row 4k + sub, columns 4*quad..
+        bool ok = true;
+        uint32_t x[32];
+        int z = 0;
+        for (int w = 0; ok; ++w) {
+            const int idx = tc_item_index(w);
+            if (idx >= n_items) break;
+            const TcItem it = tc_item(a, idx, n_qt);
+            const int row0 = it.r0 + quarter * 32;  // first sequence row of this warp's 32 rows
+            float* obase = a.out + ((static_cast<size_t>(it.b) * a.q_seq + row0) * a.q_heads + it.h) * D;
+            const size_t ostride = static_cast<size_t>(a.q_heads) * D;  // floats between rows
+            if (it.n_kv == 0) {  // padded query rows only: zeros, D/4 lanes per row
+                constexpr int F4 = D / 4, RPI = 32 / F4;
+#pragma unroll
+                for (int rr = lane / F4; rr < 32; rr += RPI)
+                    if (row0 + rr < a.q_seq)
+                        *reinterpret_cast<float4*>(obase + rr * ostride + 4 * (lane % F4)) =
+                            make_float4(0.f, 0.f, 0.f, 0.f);
+                continue;
+            }
+            const uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
+            const int ob = z & 1;
+            ok = __all_sync(0xffffffffu, tc_wait(&l_full[z % LR], (z / LR) & 1, deadline, abort, a.err,
+                                                 KERR_TIMEOUT_MMA));
+            if (!ok) break;
+            // Padded rows (past the valid ones) are written as zeros.
+            const float inv = it.r0 + row < it.nq_valid ? 1.0f / lsum[(z % LR) * kTcRows + row] : 0.f;
+            ok = __all_sync(0xffffffffu, tc_wait(&o_final[ob], (z >> 1) & 1, deadline, abort, a.err,
+                                                 KERR_TIMEOUT_MMA));
+            if (!ok) break;
+            tc_fence_after();
+#pragma unroll 1
+            for (int ch = 0; ch < D / 32; ++ch) {
+                tmem_ld32(tmem + Tm::kO + ob * D + ch * 32 + lane_off, x);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; i += 4)
+                    *reinterpret_cast<float4*>(stg + lane * Sm::kStageRow + i) =
+                        make_float4(__uint_as_float(x[i]) * inv, __uint_as_float(x[i + 1]) * inv,
+                                    __uint_as_float(x[i + 2]) * inv, __uint_as_float(x[i + 3]) * inv);
+                __syncwarp();
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const int rr = 4 * k + sub;
+                    if (row0 + rr < a.q_seq)
+                        *reinterpret_cast<float4*>(obase + rr * ostride + ch * 32 + 4 * quad) =
+                            *reinterpret_cast<const float4*>(stg + rr * Sm::kStageRow + 4 * quad);
+                }
+                __syncwarp();
+            }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
-        }
-        if (ok && !*abort) {
-            ok = __all_sync(0xffffffffu, tc_wait(o_done, (n_kv - 1) & 1, deadline, abort, a.err, KERR_TIMEOUT_MMA));
-            if (ok) {
-                tc_fence_after();
-                const float inv = 1.0f / l;
-                float* orow = a.out + ((static_cast<size_t>(b) * a.q_seq + qr) * a.q_heads + h) * D;
-#pragma unroll
-                for (int ch = 0; ch < D / 32; ++ch) {
-                    tmem_ld32(tmem_o + ch * 32 + lane_off, x);
-                    tmem_wait_ld();
-                    if (row_valid) {
-#pragma unroll
-                        for (int i = 0; i < 32; i += 4)
-                            *reinterpret_cast<float4*>(orow + ch * 32 + i) =
-                                make_float4(__uint_as_float(x[i]) * inv, __uint_as_float(x[i + 1]) * inv,
-                                            __uint_as_float(x[i + 2]) * inv, __uint_as_float(x[i + 3]) * inv);
-                    } else if (qr < a.q_seq) {
-#pragma unroll
-                        for (int i = 0; i < 32; i += 4)
-                            *reinterpret_cast<float4*>(orow + ch * 32 + i) = make_float4(0.f, 0.f, 0.f, 0.f);
-                    }
-                }
-            }
+            if (lane == 0) mbar_arrive(&o_free[ob]);
+            ++z;
         }
         tc_fence_before();
     }
