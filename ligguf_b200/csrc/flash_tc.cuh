@@ -85,7 +85,8 @@ __global__ void __launch_bounds__(256) bert_to_bf16_kernel(const float* __restri
 
 constexpr int kTcRows = 128;  // query rows per tile (UMMA M)
 constexpr int kTcKeys = 128;  // keys per tile (UMMA N of S, K of P.V)
-constexpr int kTcThreads = 320;
+constexpr int kTcThreads = 352;
+constexpr int kTcPvWarp = 10;  // the warp that issues the P.V MMAs
 // A kernel that uses tcgen05 runs one CTA per SM, which then owns all 512 TMEM columns:
 // S double buffer [0, 256) (P of a tile is packed over the first 64 columns of its S buffer),
 // O double buffer (by item) [256, 256 + 2D).
@@ -115,9 +116,9 @@ struct TcSmem {
     static constexpr int kStageRow = 36;
     static constexpr size_t kE = kL + size_t(kLRing) * kTcRows * 4;
     static constexpr size_t kBar = kE + 4 * 32 * kStageRow * 4;
-    // k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2], o_done, drain, q_full[2],
+    // k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2], pv_done[2], drain, q_full[2],
     // q_empty[2], o_final[2], o_free[2], l_full[kLRing]
-    static constexpr int kNumBars = 4 * kStages + 2 + 2 + 1 + 1 + 8 + kLRing;
+    static constexpr int kNumBars = 4 * kStages + 2 + 2 + 2 + 1 + 8 + kLRing;
     static constexpr size_t kMisc = kBar + size_t(kNumBars) * 8;  // tmem base, abort flag
     static constexpr size_t kTotal = kMisc + 16 + 1024;           // + slack to align the base to 1 KB
 };
@@ -323,8 +324,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // t + 1 before a slower warp finishes tile t (it never gets two tiles ahead: S(t+2) is issued
     // after P.V(t), which waits for all four arrivals of tile t).
     uint64_t* p_full = s_full + 2;
-    uint64_t* o_done = p_full + 2;    // every P.V (waited by the softmax only before a rescale)
-    uint64_t* drain = o_done + 1;
+    uint64_t* pv_done = p_full + 2;   // [t & 1] P.V(t) completed (waited by the S issuer, and by the
+                                      // softmax before a rescale)
+    uint64_t* drain = pv_done + 2;
     uint64_t* q_full = drain + 1;     // [2] Q tile of an item landed
     uint64_t* q_empty = q_full + 2;   // [2] the item's last S MMA completed: its Q buffer is free
     uint64_t* o_final = q_empty + 2;  // [2] the item's last P.V completed: O is final
@@ -338,7 +340,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int n_qt = (a.q_seq + kTcRows - 1) / kTcRows;
     const int n_items = a.q_heads * n_qt * a.batch;
     // Every role walks the same item sequence.  Key tiles of all items are numbered in one sequence
-    // (t): stage t % S of the K/V ring, S and P buffer t & 1, one o_done phase per tile.
+    // (t): stage t % S of the K/V ring, S and P buffer t & 1 (with its p_full / pv_done barrier).
     // Items that have key tiles are numbered z: Q and O buffer z & 1 (one q_full / q_empty /
     // o_final / o_free phase per item on that buffer's barrier) and row-sum slot z % LR.
 
@@ -359,8 +361,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int i = 0; i < LR; ++i) mbar_init(&l_full[i], 4);
         mbar_init(&p_full[0], 4);
         mbar_init(&p_full[1], 4);
-        mbar_init(o_done, 1);
-        mbar_init(drain, 1);
+        mbar_init(&pv_done[0], 1);
+        mbar_init(&pv_done[1], 1);
+        mbar_init(drain, 2);
         *abort = 0;
         fence_mbar_init();
     }
@@ -430,45 +433,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
             }
         }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------------ MMA issuer
+    } else if (warp == 1 || warp == kTcPvWarp) {
+        // ------------------------------------------------------------------ MMA issuers
+        // Two issuing threads on different SM sub-partitions: warp 1 issues S = Q.K^T, warp
+        // kTcPvWarp issues O += P.V.  (An issuing thread shares its sub-partition with a softmax
+        // warp, which slows its issue; two threads halve the MMAs each has to issue.)  MMAs of
+        // different threads are not ordered, so S(t), which overwrites the S buffer that P(t-2) was
+        // packed into, waits for pv_done(t-2).
         if (lane == 0) {
             constexpr uint32_t kIdS = idesc_bf16(kTcRows, kTcKeys, 0, 0);
             constexpr uint32_t kIdO = idesc_bf16(kTcRows, D, 0, 1);
-            // Descriptors are built once and advanced by constant offsets: a single issuing thread
-            // pays the latency of every instruction between two MMAs.
+            // Descriptors are built once and advanced by constant offsets: an issuing thread pays
+            // the latency of every instruction between two MMAs.
             const uint64_t q_desc = smem_desc_sw128(smem_u32(sm + Sm::kQ), 16, 1024);
             const uint64_t k_desc = smem_desc_sw128(smem_u32(sm + Sm::kK), 16, 1024);
             const uint64_t v_desc = smem_desc_sw128(smem_u32(sm + Sm::kV), Sm::kKvChunkBytes, 1024);
+            const bool is_s = warp == 1;
             bool ok = true;
             uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
-            // The P.V of tile t - 1 is issued after the S of tile t, so that S(t) overlaps the softmax
-            // of t - 1, also across items.  pend: the tile whose P.V is still to issue (-1: none),
-            // of item pend_z, first / last tile of that item.
-            int pend = -1, pend_z = 0;
-            bool pend_first = false, pend_last = false;
-            auto issue_pv = [&]() -> bool {
-                const int i = pend, s = i % S, ob = pend_z & 1;
-                // The first P.V of item z overwrites O buffer z & 1: item z - 2's epilogue must have read it.
-                if (pend_first && pend_z >= 2 &&
-                    !tc_wait(&o_free[ob], ((pend_z >> 1) - 1) & 1, deadline, abort, a.err, KERR_TIMEOUT_MMA))
-                    return false;
-                if (!tc_wait(&p_full[i & 1], (i >> 1) & 1, deadline, abort, a.err, KERR_TIMEOUT_MMA)) return false;
-                if (!tc_wait(&v_full[s], (i / S) & 1, deadline, abort, a.err, KERR_TIMEOUT_FULL)) return false;
-                tc_fence_after();
-                const uint32_t p_tmem = tmem + Tm::kS + (i & 1) * kTcKeys;  // P(i) packed in its S buffer
-                const uint32_t o_tmem = tmem + Tm::kO + ob * D;
-                const uint64_t vd = desc_advance(v_desc, s * Sm::kKvBytes);
-                umma_ts(o_tmem, p_tmem, vd, kIdO, pend_first ? 0u : 1u);
-#pragma unroll
-                for (int kk = 1; kk < kTcKeys / 16; ++kk)
-                    umma_ts(o_tmem, p_tmem + kk * 8, desc_advance(vd, kk * 2048), kIdO, 1u);
-                umma_commit(o_done);
-                umma_commit(&v_empty[s]);
-                if (pend_last) umma_commit(&o_final[ob]);
-                pend = -1;
-                return true;
-            };
             int t = 0, z = 0;
             for (int w = 0; ok; ++w) {
                 const int idx = tc_item_index(w);
@@ -476,42 +458,59 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const int n_kv = tc_item(a, idx, n_qt).n_kv;
                 if (n_kv == 0) continue;
                 deadline = globaltimer_ns() + kWaitLimitNs;
-                const int qb = z & 1;
-                if (!tc_wait(&q_full[qb], (z >> 1) & 1, deadline, abort, a.err, KERR_TIMEOUT_FULL)) break;
-                const uint64_t qd = desc_advance(q_desc, qb * Sm::kQBytes);
-                for (int j = 0; j < n_kv; ++j, ++t) {
-                    const int s = t % S, bf = t & 1;
-                    // S buffer bf held S(t-2) and P(t-2): P.V(t-2), issued above after p_full(t-2), reads
-                    // it before this S MMA writes it (MMAs of one CTA execute in issue order).
-                    if (!tc_wait(&k_full[s], (t / S) & 1, deadline, abort, a.err, KERR_TIMEOUT_FULL)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint64_t kd = desc_advance(k_desc, s * Sm::kKvBytes);
-                    const uint32_t d_tmem = tmem + Tm::kS + bf * kTcKeys;
+                const int qb = z & 1, ob = z & 1;
+                if (is_s) {
+                    if (!tc_wait(&q_full[qb], (z >> 1) & 1, deadline, abort, a.err, KERR_TIMEOUT_FULL)) break;
+                    const uint64_t qd = desc_advance(q_desc, qb * Sm::kQBytes);
+                    for (int j = 0; j < n_kv; ++j, ++t) {
+                        const int s = t % S, bf = t & 1;
+                        if (!tc_wait(&k_full[s], (t / S) & 1, deadline, abort, a.err, KERR_TIMEOUT_FULL) ||
+                            (t >= 2 && !tc_wait(&pv_done[bf], ((t >> 1) - 1) & 1, deadline, abort, a.err,
+                                                KERR_TIMEOUT_MMA))) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint64_t kd = desc_advance(k_desc, s * Sm::kKvBytes);
+                        const uint32_t d_tmem = tmem + Tm::kS + bf * kTcKeys;
 #pragma unroll
-                    for (int kk = 0; kk < D / 16; ++kk) {
-                        const uint32_t qoff = (kk >> 2) * Sm::kQChunkBytes + (kk & 3) * 32;
-                        const uint32_t koff = (kk >> 2) * Sm::kKvChunkBytes + (kk & 3) * 32;
-                        umma_ss(d_tmem, desc_advance(qd, qoff), desc_advance(kd, koff), kIdS, kk > 0 ? 1u : 0u);
+                        for (int kk = 0; kk < D / 16; ++kk) {
+                            const uint32_t qoff = (kk >> 2) * Sm::kQChunkBytes + (kk & 3) * 32;
+                            const uint32_t koff = (kk >> 2) * Sm::kKvChunkBytes + (kk & 3) * 32;
+                            umma_ss(d_tmem, desc_advance(qd, qoff), desc_advance(kd, koff), kIdS, kk > 0 ? 1u : 0u);
+                        }
+                        umma_commit(&s_full[bf]);
+                        umma_commit(&k_empty[s]);
+                        if (j == n_kv - 1) umma_commit(&q_empty[qb]);
                     }
-                    umma_commit(&s_full[bf]);
-                    umma_commit(&k_empty[s]);
-                    if (j == n_kv - 1) umma_commit(&q_empty[qb]);
-                    if (pend >= 0 && !issue_pv()) {
-                        ok = false;
-                        break;
+                } else {
+                    for (int j = 0; j < n_kv; ++j, ++t) {
+                        const int s = t % S, bf = t & 1;
+                        // The first P.V of item z overwrites O buffer z & 1: item z - 2's epilogue must
+                        // have read it.
+                        if ((j == 0 && z >= 2 &&
+                             !tc_wait(&o_free[ob], ((z >> 1) - 1) & 1, deadline, abort, a.err, KERR_TIMEOUT_MMA)) ||
+                            !tc_wait(&p_full[bf], (t >> 1) & 1, deadline, abort, a.err, KERR_TIMEOUT_MMA) ||
+                            !tc_wait(&v_full[s], (t / S) & 1, deadline, abort, a.err, KERR_TIMEOUT_FULL)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t p_tmem = tmem + Tm::kS + bf * kTcKeys;  // P(t) packed in its S buffer
+                        const uint32_t o_tmem = tmem + Tm::kO + ob * D;
+                        const uint64_t vd = desc_advance(v_desc, s * Sm::kKvBytes);
+                        umma_ts(o_tmem, p_tmem, vd, kIdO, j > 0 ? 1u : 0u);
+#pragma unroll
+                        for (int kk = 1; kk < kTcKeys / 16; ++kk)
+                            umma_ts(o_tmem, p_tmem + kk * 8, desc_advance(vd, kk * 2048), kIdO, 1u);
+                        umma_commit(&pv_done[bf]);
+                        umma_commit(&v_empty[s]);
+                        if (j == n_kv - 1) umma_commit(&o_final[ob]);
                     }
-                    pend = t;
-                    pend_first = j == 0;
-                    pend_last = j == n_kv - 1;
-                    pend_z = z;
                 }
                 ++z;
             }
-            if (ok && pend >= 0 && !*abort) issue_pv();
-            // Drain: every MMA issued above completes before TMEM is freed.
+            // Drain: every MMA issued by either thread completes before TMEM is freed.
             umma_commit(drain);
             const uint64_t dd = deadline + kWaitLimitNs / 2;
             while (!mbar_try_wait(drain, 0) && globaltimer_ns() < dd) {
@@ -577,13 +576,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const float ms = m_new == -INFINITY ? 0.f : m_new;
                 const float corr = (m == m_new || m_new == -INFINITY) ? 1.f : fast_exp2(m - m_new);
                 m = m_new;
-                // O holds P.V of tiles 0..j-1 of this item once o_done's phase t-1 has completed.  It is
-                // waited for only before a rescale (rare).  That wait is exact: s_full(t), waited above,
-                // was committed after P.V(t-2) was issued, so phase t-2 is complete, and P.V(t) cannot
-                // start before this warp's p_full(t) below, so phase t is not.
+                // O holds P.V of tiles 0..j-1 of this item once pv_done(t-1) has completed.  It is
+                // waited for only before a rescale (rare).  That wait is exact: the S issuer waited for
+                // pv_done(t-3) before issuing S(t-1), which this warp has seen, and P.V(t+1) cannot
+                // start before this warp's p_full(t+1).
                 if (j >= 1 && __any_sync(0xffffffffu, corr != 1.f)) {
-                    ok = __all_sync(0xffffffffu, ok && tc_wait(o_done, (t - 1) & 1, deadline, abort, a.err,
-                                                             KERR_TIMEOUT_MMA));
+                    ok = __all_sync(0xffffffffu, ok && tc_wait(&pv_done[(t - 1) & 1], ((t - 1) >> 1) & 1, deadline,
+                                                             abort, a.err, KERR_TIMEOUT_MMA));
                     if (!ok) break;
                     tc_fence_after();
                     uint32_t y[32];
