@@ -50,3 +50,24 @@ def test_bert_full_config_layer(gpu, mode, tol):
     out = gpu_bert(c, mode)
     ref = cases.run_bert(orc.Checker("port"), c)
     assert cases.rel_err(out, ref) <= tol
+
+
+@pytest.mark.parametrize("mode,tol", [(0, 1e-4), (1, 2e-2)])
+def test_bert_scores_growing_along_the_sequence(gpu, mode, tol):
+    """Scores that rise by ~16 (natural log units) per 128 keys in half of the heads: the running
+    max moves on every key tile, so the tensor-core softmax rescales O and l in TMEM each time (its
+    rare path); the other heads fall along the sequence (the max never moves after the first tile).
+    48 sequences give each persistent CTA many work items."""
+    H, D, L = 12, 64, 512
+    rng = np.random.default_rng(2024)
+    lens = rng.integers(200, L + 1, size=48).astype(np.int32)
+    B, E = lens.size, H * D
+    q = (0.5 + 0.01 * rng.standard_normal((B, L, E))).astype(np.float32)
+    ramp = (np.arange(L, dtype=np.float32) / 32.0)[None, :, None]                 # key position / 32
+    sign = np.where(np.arange(H) % 2 == 0, 1.0, -1.0).astype(np.float32).repeat(D)[None, None, :]
+    k = (sign * ramp * (1.0 + 0.01 * rng.standard_normal((B, L, E)))).astype(np.float32)
+    v = rng.standard_normal((B, L, E)).astype(np.float32)
+    c = dict(H=H, D=D, lens=lens, max_len=L, scale=0.125, q=q, k=k, v=v)
+    out = gpu_bert(c, mode)
+    ref = cases.run_bert(orc.Checker("port"), c)
+    assert cases.rel_err(out, ref) <= tol
