@@ -243,69 +243,116 @@ struct PrepArgs {
     float eps;
 };
 
-// Two consecutive elements to a cache row of type KV (one 8- or 4-byte store).
-template <typename KV>
-__device__ __forceinline__ void store_pair(KV* p, float x, float y) {
-    if constexpr (sizeof(KV) == 4) {
-        *reinterpret_cast<float2*>(p) = make_float2(x, y);
+// E = 2 or 4 consecutive floats of one lane: loads and stores of one row segment.
+template <int E>
+__device__ __forceinline__ void load_vec(const float* p, float (&x)[E]) {
+    if constexpr (E == 4) {
+        const float4 v = *reinterpret_cast<const float4*>(p);
+        x[0] = v.x, x[1] = v.y, x[2] = v.z, x[3] = v.w;
     } else {
-        const KV lo = KvTraits<KV>::from_float(x), hi = KvTraits<KV>::from_float(y);
-        const uint32_t w = uint32_t(*reinterpret_cast<const uint16_t*>(&lo)) |
-                           (uint32_t(*reinterpret_cast<const uint16_t*>(&hi)) << 16);
-        *reinterpret_cast<uint32_t*>(p) = w;
+        const float2 v = *reinterpret_cast<const float2*>(p);
+        x[0] = v.x, x[1] = v.y;
     }
 }
-__device__ __forceinline__ void store_pair_bf16(__nv_bfloat16* p, float x, float y) {
-    const __nv_bfloat162 v = __floats2bfloat162_rn(x, y);
-    *reinterpret_cast<__nv_bfloat162*>(p) = v;
+template <int E>
+__device__ __forceinline__ void store_vec_f32(float* p, const float (&x)[E]) {
+    if constexpr (E == 4)
+        *reinterpret_cast<float4*>(p) = make_float4(x[0], x[1], x[2], x[3]);
+    else
+        *reinterpret_cast<float2*>(p) = make_float2(x[0], x[1]);
+}
+// Two floats as one 32-bit word of 16-bit values of type T (lower element in the low half).
+template <typename T>
+__device__ __forceinline__ uint32_t pack16(float x, float y) {
+    const T lo = KvTraits<T>::from_float(x), hi = KvTraits<T>::from_float(y);
+    return uint32_t(*reinterpret_cast<const uint16_t*>(&lo)) | (uint32_t(*reinterpret_cast<const uint16_t*>(&hi)) << 16);
+}
+template <typename T, int E>
+__device__ __forceinline__ void store_vec16(T* p, const float (&x)[E]) {
+    if constexpr (E == 4)
+        *reinterpret_cast<uint2*>(p) = make_uint2(pack16<T>(x[0], x[1]), pack16<T>(x[2], x[3]));
+    else
+        *reinterpret_cast<uint32_t*>(p) = pack16<T>(x[0], x[1]);
+}
+template <typename KV, int E>
+__device__ __forceinline__ void store_vec_kv(KV* p, const float (&x)[E]) {
+    if constexpr (sizeof(KV) == 4)
+        store_vec_f32<E>(reinterpret_cast<float*>(p), x);
+    else
+        store_vec16<KV, E>(p, x);
+}
+
+// Qwen3 per-head RMS norm (with gamma) and RoPE of one head row held as E = D/32 consecutive
+// elements per lane: elements [E*lane, E*lane + E), pairs m = lane*E/2 + i rotated by (cs[m], sn[m]).
+// Same arithmetic as norm_rope_regs (sum of squares, 1/sqrt, gamma, rotation); only the partial
+// sums of squares are formed in another order.
+template <int D>
+__device__ __forceinline__ void norm_rope_vec(float (&x)[D / 32], const float* __restrict__ gamma, int norm,
+                                              float eps, const float* cs, const float* sn, int rope_pairs,
+                                              int lane) {
+    constexpr int E = D / 32;
+    if (norm) {
+        float ss = 0.f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) ss = fmaf(x[e], x[e], ss);
+        ss = warp_sum(ss);
+        const float rs = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
+        float g[E];
+        load_vec<E>(gamma + lane * E, g);
+#pragma unroll
+        for (int e = 0; e < E; ++e) x[e] = (x[e] * rs) * g[e];
+    }
+#pragma unroll
+    for (int i = 0; i < E / 2; ++i) {
+        const int m = lane * (E / 2) + i;
+        if (m < rope_pairs) {
+            const float c = cs[m], sn_ = sn[m];
+            const float x0 = x[2 * i], x1 = x[2 * i + 1];
+            x[2 * i] = x0 * c - x1 * sn_;
+            x[2 * i + 1] = x0 * sn_ + x1 * c;
+        }
+    }
 }
 
 // Prompt rows before attention: per token, the q heads (norm + RoPE; fp32 and/or bf16 out), the k
 // heads (norm + RoPE) and the v heads into this layer's cache rows (and their bf16 shadow).  One warp
-// per head: block (token, group of kPrepWarps heads), the token's cos/sin table in shared memory; each
-// lane holds element pairs (2m, 2m+1), m = lane + 32 u, loaded and stored 8 bytes at a time.
+// per head: block (token, group of kPrepWarps heads), each lane holding E = D/32 consecutive elements
+// (one 16- or 8-byte load).  The row is loaded before the token's cos/sin table is computed into
+// shared memory, so the load's latency overlaps that computation and the block barrier.
 constexpr int kPrepWarps = 16;
 template <typename KV, int D>
 __global__ void __launch_bounds__(kPrepWarps * 32) prefill_prep_kernel(const PrepArgs a) {
-    constexpr int kPairs = D / 64;
+    constexpr int E = D / 32;
     __shared__ float cs[D / 2], sn[D / 2];  // RoPE rotation of this token, shared by all heads
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int i = blockIdx.x;
     const int pos = a.pos0 + i;
+    const int job = blockIdx.y * kPrepWarps + warp;
+    const bool active = job < a.q_headn + 2 * a.kv_headn;
+    const bool is_q = job < a.q_headn, is_k = !is_q && job < a.q_headn + a.kv_headn;
+    const int gi = is_q ? job : (is_k ? job - a.q_headn : job - a.q_headn - a.kv_headn);
+    float x[E];
+    if (active) {
+        const float* src = is_q ? a.q + (static_cast<size_t>(i) * a.q_headn + gi) * D
+                                : (is_k ? a.k : a.v) + (static_cast<size_t>(i) * a.kv_headn + gi) * D;
+        load_vec<E>(src + lane * E, x);
+    }
     for (int m = threadIdx.x; m < a.rope_pairs; m += blockDim.x)
         sincosf(static_cast<float>(pos) * a.freq[m], &sn[m], &cs[m]);
     __syncthreads();
-    const int job = blockIdx.y * kPrepWarps + warp;
-    if (job >= a.q_headn + 2 * a.kv_headn) return;
-    float2 x[kPairs];
-    if (job < a.q_headn) {
-        const size_t o = (static_cast<size_t>(i) * a.q_headn + job) * D;
-#pragma unroll
-        for (int u = 0; u < kPairs; ++u) x[u] = reinterpret_cast<const float2*>(a.q + o)[lane + 32 * u];
-        norm_rope_regs<D>(x, a.qg, a.qk_norm, a.eps, cs, sn, a.rope_pairs, lane);
-#pragma unroll
-        for (int u = 0; u < kPairs; ++u) {
-            const int e = 2 * (lane + 32 * u);
-            if (a.qf) *reinterpret_cast<float2*>(a.qf + o + e) = x[u];
-            if (a.qb) store_pair_bf16(a.qb + o + e, x[u].x, x[u].y);
-        }
+    if (!active) return;
+    if (is_q) {
+        norm_rope_vec<D>(x, a.qg, a.qk_norm, a.eps, cs, sn, a.rope_pairs, lane);
+        const size_t o = (static_cast<size_t>(i) * a.q_headn + gi) * D + lane * E;
+        if (a.qf) store_vec_f32<E>(a.qf + o, x);
+        if (a.qb) store_vec16<__nv_bfloat16, E>(a.qb + o, x);
         return;
     }
-    const bool is_k = job < a.q_headn + a.kv_headn;
-    const int gi = is_k ? job - a.q_headn : job - a.q_headn - a.kv_headn;
-    const float* src = (is_k ? a.k : a.v) + (static_cast<size_t>(i) * a.kv_headn + gi) * D;
-#pragma unroll
-    for (int u = 0; u < kPairs; ++u) x[u] = reinterpret_cast<const float2*>(src)[lane + 32 * u];
-    if (is_k) norm_rope_regs<D>(x, a.kg, a.qk_norm, a.eps, cs, sn, a.rope_pairs, lane);
-    const size_t o = static_cast<size_t>(pos) * a.kv_dim + static_cast<size_t>(gi) * D;
-    KV* cache = reinterpret_cast<KV*>(is_k ? a.kc : a.vc);
+    if (is_k) norm_rope_vec<D>(x, a.kg, a.qk_norm, a.eps, cs, sn, a.rope_pairs, lane);
+    const size_t o = static_cast<size_t>(pos) * a.kv_dim + static_cast<size_t>(gi) * D + lane * E;
+    store_vec_kv<KV, E>(reinterpret_cast<KV*>(is_k ? a.kc : a.vc) + o, x);
     __nv_bfloat16* shadow = is_k ? a.kb : a.vb;
-#pragma unroll
-    for (int u = 0; u < kPairs; ++u) {
-        const int e = 2 * (lane + 32 * u);
-        store_pair<KV>(cache + o + e, x[u].x, x[u].y);
-        if (shadow) store_pair_bf16(shadow + o + e, x[u].x, x[u].y);
-    }
+    if (shadow) store_vec16<__nv_bfloat16, E>(shadow + o, x);
 }
 
 // Cache rows [0, n_rows) of one layer -> bf16 shadow (tensor-core prefill over earlier positions).
