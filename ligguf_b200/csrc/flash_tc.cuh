@@ -7,21 +7,24 @@
 // Work item = 128 query rows (one tile) of one q head of one batch entry.  A kernel that uses
 // tcgen05 runs one CTA per SM, so the grid is persistent: one CTA per SM walks a fixed share of the
 // items, keeping its barriers and all 512 TMEM columns across them, and the overlap of tensor-core
-// work with softmax work comes from inside the CTA (320 threads):
+// work with softmax work comes from inside the CTA (352 threads):
 //   warp 0      TMA producer: per item the Q tile (double-buffered), then K and V tiles of 128 keys
-//               into a 2-stage ring (4 for D = 64)
-//   warp 1      allocates TMEM; lane 0 issues every tcgen05.mma and commit
+//               into 2-stage rings (4 for D = 64)
+//   warp 1      allocates TMEM; lane 0 issues S = Q.K^T: D/16 MMAs of M128 N128 K16 per tile, Q and
+//               K from shared memory (K-major, SWIZZLE_128B)
+//   warp 10     lane 0 issues O += P.V: 8 MMAs of M128 N=D K16 per tile, P from TMEM, V from shared
+//               memory (MN-major, SWIZZLE_128B)
 //   warps 2..5  softmax: thread = query row = TMEM lane; reads S from TMEM twice (row max, then
 //               exp2), writes P as bf16 pairs back into the same TMEM columns, rescales O in TMEM
 //               when the running max moves (rare); row sums to shared memory
-//   warps 6..9  epilogue: O / l from TMEM to global memory, so the softmax warps never wait for it
-// TMEM: S double buffer [0, 256), O double-buffered by item after it.  The issuing thread is the
-// bottleneck of this design (each MMA and each mbarrier wait costs it ~70-200 cycles), so tiles are
-// 128 keys wide: S = Q.K^T is 8 MMAs of M128 N128 K16 (Q and K from shared memory, K-major,
-// SWIZZLE_128B) and O += P.V 8 MMAs of M128 N=D K16 (P from TMEM, V from shared memory, MN-major,
-// SWIZZLE_128B).  MMA order S0, S1, PV0, S2, PV1, ... across items; MMAs of one CTA execute in issue
-// order, so PV(t) has read P(t) before S(t+2) overwrites that buffer.  Every wait is bounded; on a
-// timeout the kernel records an error, drains its own copies and MMAs, frees TMEM and returns.
+//   warps 6..9  epilogue: O / l from TMEM to global memory through a padded staging block (whole
+//               128-byte row segments per store), so the softmax warps never wait for it
+// TMEM: S double buffer [0, 256), O double-buffered by item after it.  An issuing thread loses
+// issue slots to the softmax warp on its SM sub-partition, so S and P.V are issued by two threads
+// on different sub-partitions, and tiles are 128 keys wide to halve the MMAs and barrier waits per
+// key.  MMAs of different threads are not ordered: S(t+2), which overwrites the buffer that P(t) was
+// packed into, waits for P.V(t) to complete (pv_done).  Every wait is bounded; on a timeout the
+// kernel records an error, drains its own copies and MMAs, frees TMEM and returns.
 #pragma once
 
 #include "common.cuh"
