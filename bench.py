@@ -334,11 +334,14 @@ def bench_decode_e2e(args, w, h, s, q, k, v, world, local, pg):
     steps = max(3, args.steps // 3)
     if world == 1:
         outh = torch.empty(L, s["q_headn"] * D).pin_memory()
+        # Host pointers of each layer's rows, taken once: the engine passes its own buffers' pointers,
+        # so the timed loop holds only the C-ABI calls.
+        fn, hd = lib.ligguf_cuda_attn_decode, h.handle
+        rows = [(l, qh[l].data_ptr(), kh[l].data_ptr(), vh[l].data_ptr(), outh[l].data_ptr()) for l in range(L)]
 
         def step():
-            for l in range(L):
-                rc = lib.ligguf_cuda_attn_decode(h.handle, l, w.pos, qh[l].data_ptr(), kh[l].data_ptr(),
-                                                 vh[l].data_ptr(), outh[l].data_ptr())
+            for l, pq, pk, pv, po in rows:
+                rc = fn(hd, l, w.pos, pq, pk, pv, po)
                 if rc:
                     raise RuntimeError(f"decode failed {rc}")
         h2d = L * (qh.shape[1] + 2 * kh.shape[1]) * 4
