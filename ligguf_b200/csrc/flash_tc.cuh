@@ -49,9 +49,14 @@ __global__ void to_bf16_kernel(const float* __restrict__ src, __nv_bfloat16* __r
         dst[i] = __float2bfloat16_rn(src[i]);
 }
 
-// BERT operands to bf16 in one pass, valid rows only: rows r < lens[b] of q, k and v are converted;
-// padded rows of v are written as zeros (P.V multiplies them by P = 0, so they must be finite), while
-// padded rows of q and k are left as they are (their scores are masked or their outputs discarded).
+constexpr int kTcRows = 128;  // query rows per tile (UMMA M)
+constexpr int kTcKeys = 128;  // keys per tile (UMMA N of S, K of P.V)
+
+// BERT operands to bf16 in one pass, valid rows only: rows r < lens[b] of q, k and v are converted.
+// Padded rows of v inside the last key tile that holds valid keys are written as zeros (P.V
+// multiplies them by P = 0, so they must be finite); the tensor-core kernel reads no key tile past
+// that one.  Padded rows of q and k are left as they are (their scores are masked or their outputs
+// discarded).
 // Block = kBertConvRows rows of one batch entry; 8 values per thread step (two 16-byte loads, one
 // 16-byte store).  Needs E % 8 == 0 and 16-byte aligned bases.
 constexpr int kBertConvRows = 8;
@@ -62,6 +67,7 @@ __global__ void __launch_bounds__(256) bert_to_bf16_kernel(const float* __restri
     const int b = blockIdx.y;
     const int r0 = blockIdx.x * kBertConvRows;
     const int len = min(lens[b], max_len);
+    const int v_zero_end = min(max_len, (len + kTcKeys - 1) / kTcKeys * kTcKeys);  // end of the last key tile read
     const int units = E / 8;  // 16-byte output units per row
     const int per_tensor = kBertConvRows * units;
     for (int u = threadIdx.x; u < 3 * per_tensor; u += blockDim.x) {
@@ -72,7 +78,7 @@ __global__ void __launch_bounds__(256) bert_to_bf16_kernel(const float* __restri
         const size_t off = (static_cast<size_t>(b) * max_len + r) * E + size_t(rem % units) * 8;
         __nv_bfloat16* dst = t == 0 ? bq : (t == 1 ? bk : bv);
         if (r >= len) {
-            if (t == 2) *reinterpret_cast<uint4*>(dst + off) = make_uint4(0u, 0u, 0u, 0u);
+            if (t == 2 && r < v_zero_end) *reinterpret_cast<uint4*>(dst + off) = make_uint4(0u, 0u, 0u, 0u);
             continue;
         }
         const float* src = t == 0 ? q : (t == 1 ? k : v);
@@ -86,8 +92,6 @@ __global__ void __launch_bounds__(256) bert_to_bf16_kernel(const float* __restri
     }
 }
 
-constexpr int kTcRows = 128;  // query rows per tile (UMMA M)
-constexpr int kTcKeys = 128;  // keys per tile (UMMA N of S, K of P.V)
 constexpr int kTcThreads = 352;
 constexpr int kTcPvWarp = 10;  // the warp that issues the P.V MMAs
 // A kernel that uses tcgen05 runs one CTA per SM, which then owns all 512 TMEM columns:
