@@ -409,6 +409,13 @@ int launch_flash_tc_t(const lg::TcArgs& t, cudaStream_t st, int device) {
     static int resident[64] = {};
     int slots = device >= 0 && device < 64 ? resident[device] : 0;
     if (slots == 0) {
+        // The warpgroups' register shares (setmaxnreg) come out of the registers the CTA launched
+        // with; a smaller launch count would leave the softmax warpgroup's increase waiting forever.
+        cudaFuncAttributes fa{};
+        LG_CUDA(cudaFuncGetAttributes(&fa, kern));
+        if (fa.numRegs * 3 < lg::kTcRegsIssue + lg::kTcRegsSoftmax + lg::kTcRegsEpilogue)
+            return fail(LIGGUF_ATTN_ECUDA, "tensor-core attention kernel built with %d registers per thread, %d needed",
+                        fa.numRegs, (lg::kTcRegsIssue + lg::kTcRegsSoftmax + lg::kTcRegsEpilogue + 2) / 3);
         int sms = 0, per_sm = 0;
         LG_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
         LG_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, lg::kTcThreads, lg::TcSmem<D>::kTotal));

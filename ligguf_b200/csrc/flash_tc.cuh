@@ -7,17 +7,20 @@
 // Work item = 128 query rows (one tile) of one q head of one batch entry.  A kernel that uses
 // tcgen05 runs one CTA per SM, so the grid is persistent: one CTA per SM walks a fixed share of the
 // items, keeping its barriers and all 512 TMEM columns across them, and the overlap of tensor-core
-// work with softmax work comes from inside the CTA (352 threads):
+// work with softmax work comes from inside the CTA (384 threads, three warpgroups whose register
+// budgets are rebalanced with setmaxnreg):
 //   warp 0      TMA producer: per item the Q tile (double-buffered), then K and V tiles of 128 keys
 //               into 2-stage rings (4 for D = 64)
 //   warp 1      allocates TMEM; lane 0 issues S = Q.K^T: D/16 MMAs of M128 N128 K16 per tile, Q and
 //               K from shared memory (K-major, SWIZZLE_128B)
-//   warp 10     lane 0 issues O += P.V: 8 MMAs of M128 N=D K16 per tile, P from TMEM, V from shared
+//   warp 2      lane 0 issues O += P.V: 8 MMAs of M128 N=D K16 per tile, P from TMEM, V from shared
 //               memory (MN-major, SWIZZLE_128B)
-//   warps 2..5  softmax: thread = query row = TMEM lane; reads S from TMEM twice (row max, then
-//               exp2), writes P as bf16 pairs back into the same TMEM columns, rescales O in TMEM
-//               when the running max moves (rare); row sums to shared memory
-//   warps 6..9  epilogue: O / l from TMEM to global memory through a padded staging block (whole
+//   warp 3      idle (completes the first warpgroup)
+//   warps 4..7  softmax: thread = query row = TMEM lane; reads the 128 columns of its S row from
+//               TMEM once into registers (row max, then exp2), writes P as bf16 pairs back into the
+//               same TMEM columns, rescales O in TMEM when the running max moves (rare); row sums
+//               to shared memory
+//   warps 8..11 epilogue: O / l from TMEM to global memory through a padded staging block (whole
 //               128-byte row segments per store), so the softmax warps never wait for it
 // TMEM: S double buffer [0, 256), O double-buffered by item after it.  An issuing thread loses
 // issue slots to the softmax warp on its SM sub-partition, so S and P.V are issued by two threads
@@ -87,8 +90,20 @@ __global__ void __launch_bounds__(256) bert_to_bf16_kernel(const float* __restri
     }
 }
 
-constexpr int kTcThreads = 352;
-constexpr int kTcPvWarp = 10;  // the warp that issues the P.V MMAs
+// Three warpgroups: 0 = TMA producer (warp 0), S issuer (warp 1), P.V issuer (warp 2), warp 3 idle;
+// 1 = softmax (warps 4-7); 2 = epilogue (warps 8-11).  A warp reaches only TMEM lanes
+// [32 * (warp % 4), +32), so each of the softmax and epilogue warpgroups covers all 128 lanes.
+constexpr int kTcThreads = 384;
+constexpr int kTcPvWarp = 2;  // the warp that issues the P.V MMAs
+// Register split (setmaxnreg) from the 168 per thread that 384 threads at one CTA per SM launch with:
+// the softmax holds a whole 128-column S row in registers.  The sum of the three shares must not
+// exceed 3 x 168, or the increase waits forever; the launcher checks the kernel's register count.
+constexpr int kTcRegsLaunch = 168;
+constexpr int kTcRegsIssue = 88;
+constexpr int kTcRegsSoftmax = 240;
+constexpr int kTcRegsEpilogue = 160;
+static_assert(kTcRegsIssue + kTcRegsSoftmax + kTcRegsEpilogue <= 3 * kTcRegsLaunch, "register split too large");
+static_assert(kTcThreads * kTcRegsLaunch <= 65536, "launch register count does not fit an SM");
 // A kernel that uses tcgen05 runs one CTA per SM, which then owns all 512 TMEM columns:
 // S double buffer [0, 256) (P of a tile is packed over the first 64 columns of its S buffer),
 // O double buffer (by item) [256, 256 + 2D).
@@ -262,6 +277,15 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
         : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
     return d;
 }
+// Warpgroup-wide register budget change (all 128 threads of the warpgroup execute it together).
+template <int R>
+__device__ __forceinline__ void reg_dec() {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(R));
+}
+template <int R>
+__device__ __forceinline__ void reg_inc() {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(R));
+}
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
     float d;
     asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
@@ -366,150 +390,155 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 0) {
-        // ------------------------------------------------------------------ TMA producer
-        if (lane == 0) {
-            int t = 0, z = 0, issued = 0;  // issued: tiles whose copies are in flight or landed
-            bool ok = true;
-            uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
-            for (int w = 0; ok; ++w) {
-                const int idx = tc_item_index(w);
-                if (idx >= n_items) break;
-                const TcItem it = tc_item(a, idx, n_qt);
-                if (it.n_kv == 0) continue;
-                deadline = globaltimer_ns() + kWaitLimitNs;
-                // Q of item z into buffer z & 1, once the last S MMA of item z - 2 has read it.
-                const int qb = z & 1;
-                if (z >= 2 && !tc_wait(&q_empty[qb], ((z >> 1) - 1) & 1, deadline, abort, a.err, KERR_TIMEOUT_EMPTY))
-                    break;
-                mbar_arrive_expect_tx(&q_full[qb], Sm::kQBytes);
-                for (int c = 0; c < NCH; ++c)
-                    tma_load_3d(sm + Sm::kQ + qb * Sm::kQBytes + c * Sm::kQChunkBytes, &tm_q, &q_full[qb], 64 * c,
-                                it.h, it.b * a.q_seq + it.r0);
-                ++z;
-                const int g = it.h / a.nrep, kv_row0 = it.b * a.kv_seq;
-                for (int j = 0; j < it.n_kv; ++j, ++t) {
-                    const int s = t % S;
-                    const uint32_t par = ((t / S) - 1) & 1;
-                    if (t >= S && !tc_wait(&k_empty[s], par, deadline, abort, a.err, KERR_TIMEOUT_EMPTY)) {
-                        ok = false;
+    if (warp < 4) {
+        reg_dec<kTcRegsIssue>();
+        if (warp == 0) {
+            // ------------------------------------------------------------------ TMA producer
+            if (lane == 0) {
+                int t = 0, z = 0, issued = 0;  // issued: tiles whose copies are in flight or landed
+                bool ok = true;
+                uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
+                for (int w = 0; ok; ++w) {
+                    const int idx = tc_item_index(w);
+                    if (idx >= n_items) break;
+                    const TcItem it = tc_item(a, idx, n_qt);
+                    if (it.n_kv == 0) continue;
+                    deadline = globaltimer_ns() + kWaitLimitNs;
+                    // Q of item z into buffer z & 1, once the last S MMA of item z - 2 has read it.
+                    const int qb = z & 1;
+                    if (z >= 2 &&
+                        !tc_wait(&q_empty[qb], ((z >> 1) - 1) & 1, deadline, abort, a.err, KERR_TIMEOUT_EMPTY))
                         break;
-                    }
-                    mbar_arrive_expect_tx(&k_full[s], Sm::kKvBytes);
+                    mbar_arrive_expect_tx(&q_full[qb], Sm::kQBytes);
                     for (int c = 0; c < NCH; ++c)
-                        tma_load_3d(sm + Sm::kK + s * Sm::kKvBytes + c * Sm::kKvChunkBytes, &tm_k, &k_full[s],
-                                    64 * c, g, kv_row0 + j * kTcKeys);
-                    if (t >= S && !tc_wait(&v_empty[s], par, deadline, abort, a.err, KERR_TIMEOUT_EMPTY)) {
-                        ++issued;  // the K half of this stage is in flight
-                        ok = false;
-                        break;
-                    }
-                    mbar_arrive_expect_tx(&v_full[s], Sm::kKvBytes);
-                    for (int c = 0; c < NCH; ++c)
-                        tma_load_3d(sm + Sm::kV + s * Sm::kKvBytes + c * Sm::kKvChunkBytes, &tm_v, &v_full[s],
-                                    64 * c, g, kv_row0 + j * kTcKeys);
-                    ++issued;
-                }
-            }
-            // Drain: the last copies issued into each buffer must land before the CTA exits.  No copy
-            // is issued after these, so each barrier rests on the phase waited for here.
-            const uint64_t dd = deadline + kWaitLimitNs / 2;
-            for (int i = max(0, z - 2); i < z; ++i)
-                while (!mbar_try_wait(&q_full[i & 1], (i >> 1) & 1) && globaltimer_ns() < dd) {
-                }
-            for (int j = max(0, issued - S); j < issued; ++j) {
-                const int s = j % S;
-                const uint32_t par = (j / S) & 1;
-                while (!mbar_try_wait(&k_full[s], par) && globaltimer_ns() < dd) {
-                }
-                while (!mbar_try_wait(&v_full[s], par) && globaltimer_ns() < dd) {
-                }
-            }
-        }
-    } else if (warp == 1 || warp == kTcPvWarp) {
-        // ------------------------------------------------------------------ MMA issuers
-        // Two issuing threads on different SM sub-partitions: warp 1 issues S = Q.K^T, warp
-        // kTcPvWarp issues O += P.V.  (An issuing thread shares its sub-partition with a softmax
-        // warp, which slows its issue; two threads halve the MMAs each has to issue.)  MMAs of
-        // different threads are not ordered, so S(t), which overwrites the S buffer that P(t-2) was
-        // packed into, waits for pv_done(t-2).
-        if (lane == 0) {
-            constexpr uint32_t kIdS = idesc_bf16(kTcRows, kTcKeys, 0, 0);
-            constexpr uint32_t kIdO = idesc_bf16(kTcRows, D, 0, 1);
-            // Descriptors are built once and advanced by constant offsets: an issuing thread pays
-            // the latency of every instruction between two MMAs.
-            const uint64_t q_desc = smem_desc_sw128(smem_u32(sm + Sm::kQ), 16, 1024);
-            const uint64_t k_desc = smem_desc_sw128(smem_u32(sm + Sm::kK), 16, 1024);
-            const uint64_t v_desc = smem_desc_sw128(smem_u32(sm + Sm::kV), Sm::kKvChunkBytes, 1024);
-            const bool is_s = warp == 1;
-            bool ok = true;
-            uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
-            int t = 0, z = 0;
-            for (int w = 0; ok; ++w) {
-                const int idx = tc_item_index(w);
-                if (idx >= n_items) break;
-                const int n_kv = tc_item(a, idx, n_qt).n_kv;
-                if (n_kv == 0) continue;
-                deadline = globaltimer_ns() + kWaitLimitNs;
-                const int qb = z & 1, ob = z & 1;
-                if (is_s) {
-                    if (!tc_wait(&q_full[qb], (z >> 1) & 1, deadline, abort, a.err, KERR_TIMEOUT_FULL)) break;
-                    const uint64_t qd = desc_advance(q_desc, qb * Sm::kQBytes);
-                    for (int j = 0; j < n_kv; ++j, ++t) {
-                        const int s = t % S, bf = t & 1;
-                        if (!tc_wait(&k_full[s], (t / S) & 1, deadline, abort, a.err, KERR_TIMEOUT_FULL) ||
-                            (t >= 2 && !tc_wait(&pv_done[bf], ((t >> 1) - 1) & 1, deadline, abort, a.err,
-                                                KERR_TIMEOUT_MMA))) {
+                        tma_load_3d(sm + Sm::kQ + qb * Sm::kQBytes + c * Sm::kQChunkBytes, &tm_q, &q_full[qb], 64 * c,
+                                    it.h, it.b * a.q_seq + it.r0);
+                    ++z;
+                    const int g = it.h / a.nrep, kv_row0 = it.b * a.kv_seq;
+                    for (int j = 0; j < it.n_kv; ++j, ++t) {
+                        const int s = t % S;
+                        const uint32_t par = ((t / S) - 1) & 1;
+                        if (t >= S && !tc_wait(&k_empty[s], par, deadline, abort, a.err, KERR_TIMEOUT_EMPTY)) {
                             ok = false;
                             break;
                         }
-                        tc_fence_after();
-                        const uint64_t kd = desc_advance(k_desc, s * Sm::kKvBytes);
-                        const uint32_t d_tmem = tmem + Tm::kS + bf * kTcKeys;
-#pragma unroll
-                        for (int kk = 0; kk < D / 16; ++kk) {
-                            const uint32_t qoff = (kk >> 2) * Sm::kQChunkBytes + (kk & 3) * 32;
-                            const uint32_t koff = (kk >> 2) * Sm::kKvChunkBytes + (kk & 3) * 32;
-                            umma_ss(d_tmem, desc_advance(qd, qoff), desc_advance(kd, koff), kIdS, kk > 0 ? 1u : 0u);
-                        }
-                        umma_commit(&s_full[bf]);
-                        umma_commit(&k_empty[s]);
-                        if (j == n_kv - 1) umma_commit(&q_empty[qb]);
-                    }
-                } else {
-                    for (int j = 0; j < n_kv; ++j, ++t) {
-                        const int s = t % S, bf = t & 1;
-                        // The first P.V of item z overwrites O buffer z & 1: item z - 2's epilogue must
-                        // have read it.
-                        if ((j == 0 && z >= 2 &&
-                             !tc_wait(&o_free[ob], ((z >> 1) - 1) & 1, deadline, abort, a.err, KERR_TIMEOUT_MMA)) ||
-                            !tc_wait(&p_full[bf], (t >> 1) & 1, deadline, abort, a.err, KERR_TIMEOUT_MMA) ||
-                            !tc_wait(&v_full[s], (t / S) & 1, deadline, abort, a.err, KERR_TIMEOUT_FULL)) {
+                        mbar_arrive_expect_tx(&k_full[s], Sm::kKvBytes);
+                        for (int c = 0; c < NCH; ++c)
+                            tma_load_3d(sm + Sm::kK + s * Sm::kKvBytes + c * Sm::kKvChunkBytes, &tm_k, &k_full[s],
+                                        64 * c, g, kv_row0 + j * kTcKeys);
+                        if (t >= S && !tc_wait(&v_empty[s], par, deadline, abort, a.err, KERR_TIMEOUT_EMPTY)) {
+                            ++issued;  // the K half of this stage is in flight
                             ok = false;
                             break;
                         }
-                        tc_fence_after();
-                        const uint32_t p_tmem = tmem + Tm::kS + bf * kTcKeys;  // P(t) packed in its S buffer
-                        const uint32_t o_tmem = tmem + Tm::kO + ob * D;
-                        const uint64_t vd = desc_advance(v_desc, s * Sm::kKvBytes);
-                        umma_ts(o_tmem, p_tmem, vd, kIdO, j > 0 ? 1u : 0u);
-#pragma unroll
-                        for (int kk = 1; kk < kTcKeys / 16; ++kk)
-                            umma_ts(o_tmem, p_tmem + kk * 8, desc_advance(vd, kk * 2048), kIdO, 1u);
-                        umma_commit(&pv_done[bf]);
-                        umma_commit(&v_empty[s]);
-                        if (j == n_kv - 1) umma_commit(&o_final[ob]);
+                        mbar_arrive_expect_tx(&v_full[s], Sm::kKvBytes);
+                        for (int c = 0; c < NCH; ++c)
+                            tma_load_3d(sm + Sm::kV + s * Sm::kKvBytes + c * Sm::kKvChunkBytes, &tm_v, &v_full[s],
+                                        64 * c, g, kv_row0 + j * kTcKeys);
+                        ++issued;
                     }
                 }
-                ++z;
+                // Drain: the last copies issued into each buffer must land before the CTA exits.  No copy
+                // is issued after these, so each barrier rests on the phase waited for here.
+                const uint64_t dd = deadline + kWaitLimitNs / 2;
+                for (int i = max(0, z - 2); i < z; ++i)
+                    while (!mbar_try_wait(&q_full[i & 1], (i >> 1) & 1) && globaltimer_ns() < dd) {
+                    }
+                for (int j = max(0, issued - S); j < issued; ++j) {
+                    const int s = j % S;
+                    const uint32_t par = (j / S) & 1;
+                    while (!mbar_try_wait(&k_full[s], par) && globaltimer_ns() < dd) {
+                    }
+                    while (!mbar_try_wait(&v_full[s], par) && globaltimer_ns() < dd) {
+                    }
+                }
             }
-            // Drain: every MMA issued by either thread completes before TMEM is freed.
-            umma_commit(drain);
-            const uint64_t dd = deadline + kWaitLimitNs / 2;
-            while (!mbar_try_wait(drain, 0) && globaltimer_ns() < dd) {
+        } else if (warp == 1 || warp == kTcPvWarp) {
+            // ------------------------------------------------------------------ MMA issuers
+            // Two issuing threads on different SM sub-partitions: warp 1 issues S = Q.K^T, warp
+            // kTcPvWarp issues O += P.V.  (An issuing thread shares its sub-partition with a softmax
+            // warp, which slows its issue; two threads halve the MMAs each has to issue.)  MMAs of
+            // different threads are not ordered, so S(t), which overwrites the S buffer that P(t-2) was
+            // packed into, waits for pv_done(t-2).
+            if (lane == 0) {
+                constexpr uint32_t kIdS = idesc_bf16(kTcRows, kTcKeys, 0, 0);
+                constexpr uint32_t kIdO = idesc_bf16(kTcRows, D, 0, 1);
+                // Descriptors are built once and advanced by constant offsets: an issuing thread pays
+                // the latency of every instruction between two MMAs.
+                const uint64_t q_desc = smem_desc_sw128(smem_u32(sm + Sm::kQ), 16, 1024);
+                const uint64_t k_desc = smem_desc_sw128(smem_u32(sm + Sm::kK), 16, 1024);
+                const uint64_t v_desc = smem_desc_sw128(smem_u32(sm + Sm::kV), Sm::kKvChunkBytes, 1024);
+                const bool is_s = warp == 1;
+                bool ok = true;
+                uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
+                int t = 0, z = 0;
+                for (int w = 0; ok; ++w) {
+                    const int idx = tc_item_index(w);
+                    if (idx >= n_items) break;
+                    const int n_kv = tc_item(a, idx, n_qt).n_kv;
+                    if (n_kv == 0) continue;
+                    deadline = globaltimer_ns() + kWaitLimitNs;
+                    const int qb = z & 1, ob = z & 1;
+                    if (is_s) {
+                        if (!tc_wait(&q_full[qb], (z >> 1) & 1, deadline, abort, a.err, KERR_TIMEOUT_FULL)) break;
+                        const uint64_t qd = desc_advance(q_desc, qb * Sm::kQBytes);
+                        for (int j = 0; j < n_kv; ++j, ++t) {
+                            const int s = t % S, bf = t & 1;
+                            if (!tc_wait(&k_full[s], (t / S) & 1, deadline, abort, a.err, KERR_TIMEOUT_FULL) ||
+                                (t >= 2 && !tc_wait(&pv_done[bf], ((t >> 1) - 1) & 1, deadline, abort, a.err,
+                                                    KERR_TIMEOUT_MMA))) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+                            const uint64_t kd = desc_advance(k_desc, s * Sm::kKvBytes);
+                            const uint32_t d_tmem = tmem + Tm::kS + bf * kTcKeys;
+#pragma unroll
+                            for (int kk = 0; kk < D / 16; ++kk) {
+                                const uint32_t qoff = (kk >> 2) * Sm::kQChunkBytes + (kk & 3) * 32;
+                                const uint32_t koff = (kk >> 2) * Sm::kKvChunkBytes + (kk & 3) * 32;
+                                umma_ss(d_tmem, desc_advance(qd, qoff), desc_advance(kd, koff), kIdS, kk > 0 ? 1u : 0u);
+                            }
+                            umma_commit(&s_full[bf]);
+                            umma_commit(&k_empty[s]);
+                            if (j == n_kv - 1) umma_commit(&q_empty[qb]);
+                        }
+                    } else {
+                        for (int j = 0; j < n_kv; ++j, ++t) {
+                            const int s = t % S, bf = t & 1;
+                            // The first P.V of item z overwrites O buffer z & 1: item z - 2's epilogue must
+                            // have read it.
+                            if ((j == 0 && z >= 2 &&
+                                 !tc_wait(&o_free[ob], ((z >> 1) - 1) & 1, deadline, abort, a.err, KERR_TIMEOUT_MMA)) ||
+                                !tc_wait(&p_full[bf], (t >> 1) & 1, deadline, abort, a.err, KERR_TIMEOUT_MMA) ||
+                                !tc_wait(&v_full[s], (t / S) & 1, deadline, abort, a.err, KERR_TIMEOUT_FULL)) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+                            const uint32_t p_tmem = tmem + Tm::kS + bf * kTcKeys;  // P(t) packed in its S buffer
+                            const uint32_t o_tmem = tmem + Tm::kO + ob * D;
+                            const uint64_t vd = desc_advance(v_desc, s * Sm::kKvBytes);
+                            umma_ts(o_tmem, p_tmem, vd, kIdO, j > 0 ? 1u : 0u);
+#pragma unroll
+                            for (int kk = 1; kk < kTcKeys / 16; ++kk)
+                                umma_ts(o_tmem, p_tmem + kk * 8, desc_advance(vd, kk * 2048), kIdO, 1u);
+                            umma_commit(&pv_done[bf]);
+                            umma_commit(&v_empty[s]);
+                            if (j == n_kv - 1) umma_commit(&o_final[ob]);
+                        }
+                    }
+                    ++z;
+                }
+                // Drain: every MMA issued by either thread completes before TMEM is freed.
+                umma_commit(drain);
+                const uint64_t dd = deadline + kWaitLimitNs / 2;
+                while (!mbar_try_wait(drain, 0) && globaltimer_ns() < dd) {
+                }
             }
         }
-    } else if (warp < 6) {
+    } else if (warp < 8) {
+        reg_inc<kTcRegsSoftmax>();
         // ------------------------------------------------------------------ softmax warpgroup
         const int quarter = warp & 3;         // TMEM lanes [32*quarter, 32*quarter+32)
         const int row = quarter * 32 + lane;  // query row within the tile
@@ -539,26 +568,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 // Columns c < lim of this tile are visible to this row (key < kv_len, and key <= the
                 // row's position under the causal mask).
                 const int lim = min(kv_len - k0, a.causal ? a.q_pos0 + qr - k0 + 1 : kTcKeys);
-                // Pass 1, row max: 64 columns per TMEM load, 8 independent chains of three-input max.
+                // The tile's row in registers (one read of TMEM; the softmax warpgroup's register
+                // share holds it), then the row max over 8 independent chains of three-input max.
+                uint32_t r[kTcKeys];
+#pragma unroll
+                for (int c = 0; c < kTcKeys; c += 32) tmem_ld32p(s_tmem + c, r + c);
+                tmem_wait_ld();
+                if (edge)
+#pragma unroll
+                    for (int c = 0; c < kTcKeys; ++c)
+                        if (c >= lim) r[c] = __float_as_uint(-INFINITY);
                 float mx8[8];
 #pragma unroll
-                for (int u = 0; u < 8; ++u) mx8[u] = -INFINITY;
+                for (int u = 0; u < 8; ++u) mx8[u] = fmaxf(__uint_as_float(r[u]), __uint_as_float(r[8 + u]));
 #pragma unroll
-                for (int hc = 0; hc < kTcKeys / 64; ++hc) {
-                    uint32_t r[64];
-                    tmem_ld32p(s_tmem + hc * 64, r);
-                    tmem_ld32p(s_tmem + hc * 64 + 32, r + 32);
-                    tmem_wait_ld();
-                    if (edge)
+                for (int c = 16; c < kTcKeys; c += 16)
 #pragma unroll
-                        for (int c = 0; c < 64; ++c)
-                            if (hc * 64 + c >= lim) r[c] = __float_as_uint(-INFINITY);
-#pragma unroll
-                    for (int c = 0; c < 64; c += 16)
-#pragma unroll
-                        for (int u = 0; u < 8; ++u)
-                            mx8[u] = fmax3(mx8[u], __uint_as_float(r[c + u]), __uint_as_float(r[c + 8 + u]));
-                }
+                    for (int u = 0; u < 8; ++u)
+                        mx8[u] = fmax3(mx8[u], __uint_as_float(r[c + u]), __uint_as_float(r[c + 8 + u]));
                 const float mx =
                     fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
                 // The running max (log2 units) only moves when the tile max exceeds it by more than 8:
@@ -589,27 +616,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     }
                     tmem_wait_st();
                 }
-                // Pass 2: p = 2^(s*c2 - ms) for key pairs, P packed as bf16 pairs (lower key in the low
-                // half: the A-operand layout of a TMEM-sourced kind::f16 MMA) over the first kTcKeys/2
-                // columns of the S buffer.  P of columns [64h, 64h+64) lands in columns [32h, 32h+32),
-                // at or below the columns already read.  Row sum over 4 pair accumulators.
+                // p = 2^(s*c2 - ms) for key pairs, P packed as bf16 pairs (lower key in the low half:
+                // the A-operand layout of a TMEM-sourced kind::f16 MMA) over the first kTcKeys/2
+                // columns of the S buffer, which this thread has already read in full.  P of columns
+                // [64h, 64h+64) lands in columns [32h, 32h+32).  Row sum over 4 pair accumulators.
                 float2 rs4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                                  make_float2(0.f, 0.f)};
                 const float2 cc = make_float2(c2, c2), nm = make_float2(-ms, -ms);
 #pragma unroll
                 for (int hc = 0; hc < kTcKeys / 64; ++hc) {
-                    uint32_t r[64];
-                    tmem_ld32p(s_tmem + hc * 64, r);
-                    tmem_ld32p(s_tmem + hc * 64 + 32, r + 32);
-                    tmem_wait_ld();
-                    if (edge)
-#pragma unroll
-                        for (int c = 0; c < 64; ++c)
-                            if (hc * 64 + c >= lim) r[c] = __float_as_uint(-INFINITY);
                     uint32_t pk[32];
 #pragma unroll
                     for (int c = 0; c < 32; ++c) {
-                        float2 e = ffma2(make_float2(__uint_as_float(r[2 * c]), __uint_as_float(r[2 * c + 1])), cc, nm);
+                        const int i = hc * 64 + 2 * c;
+                        float2 e = ffma2(make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), cc, nm);
                         e.x = fast_exp2(e.x);
                         e.y = fast_exp2(e.y);
                         pk[c] = pack_bf16(e.x, e.y);
@@ -633,6 +653,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         tc_fence_before();
     } else {
+        reg_dec<kTcRegsEpilogue>();
         // ------------------------------------------------------------------ epilogue warpgroup
         // Per item z: row sums from shared memory, O buffer z & 1 from TMEM once the last P.V has
         // completed, O / l to the output rows, then O buffer z & 1 is handed back to the MMA issuer.
