@@ -184,6 +184,7 @@ struct ligguf_bert_attn {
     int* d_lens = nullptr;
     float* d_buf = nullptr;  // q, k, v, out staging for the host-pointer call
     __nv_bfloat16* bf = nullptr;  // bf16 q, k, v for the tensor-core path
+    int* d_order = nullptr;       // the tensor-core kernel's work order (bert_item_order)
     int* h_err = nullptr;
     int* d_err = nullptr;
     cudaStream_t stream = nullptr;
@@ -566,11 +567,14 @@ int prefill_enqueue(ligguf_attn* h, int layer, int pos0, int n, const float* dq,
 // ============================================================================== no-allocation scratch
 // Scratch of ligguf_cuda_bert_attn_tc_noalloc, reserved in every GPU that loads this library for as
 // long as the process lives: the bf16 copies of q, k and v (LIGGUF_NOALLOC_MAX_ELEMS elements
-// each, 8 MiB apiece) followed by 256 bytes holding the kernel's error word.  Host code must not
-// hand the symbol itself to a kernel (on the host it is only a stand-in for the device array); the
-// device address comes from cudaGetSymbolAddress, once per device.
+// each, 8 MiB apiece), 256 bytes holding the kernel's error word, then the tensor-core kernel's work
+// order (one int per work item: n_heads * ceil(max_len / 128) * batch <= elements / 64, since
+// head_dim >= 64).  Host code must not hand the symbol itself to a kernel (on the host it is only a
+// stand-in for the device array); the device address comes from cudaGetSymbolAddress, once per
+// device.
 constexpr size_t kNoallocOperandBytes = size_t(LIGGUF_NOALLOC_MAX_ELEMS) * sizeof(__nv_bfloat16);
-constexpr size_t kNoallocBytes = 3 * kNoallocOperandBytes + 256;
+constexpr size_t kNoallocOrderInts = size_t(LIGGUF_NOALLOC_MAX_ELEMS) / 64;
+constexpr size_t kNoallocBytes = 3 * kNoallocOperandBytes + 256 + kNoallocOrderInts * sizeof(int);
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocBytes];
 
 namespace {
@@ -975,6 +979,7 @@ int ligguf_cuda_bert_free(ligguf_bert_attn* b) {
     if (b->d_lens) cudaFree(b->d_lens);
     if (b->d_buf) cudaFree(b->d_buf);
     if (b->bf) cudaFree(b->bf);
+    if (b->d_order) cudaFree(b->d_order);
     if (b->h_err) cudaFreeHost(b->h_err);
     if (b->stream) cudaStreamDestroy(b->stream);
     delete b;
@@ -1011,13 +1016,24 @@ int ligguf_cuda_bert_init(int n_heads, int head_dim, int max_batch, int max_len,
 }
 
 // q, k, v (fp32, [batch][max_len][E]) to the bf16 operands of the tensor-core path, valid rows only
-// (one pass; padded v rows zeroed).  E is n_heads * head_dim, a multiple of 64.
+// (one pass; padded v rows zeroed).  E is n_heads * head_dim, a multiple of 64.  The same launch
+// writes the tensor-core kernel's work order into `order` (bert_order_ints(...) ints) when it is
+// not null.
 static cudaError_t bert_convert(const float* q, const float* k, const float* v, const int* lens, int batch,
-                               int max_len, int E, __nv_bfloat16* bq, __nv_bfloat16* bk, __nv_bfloat16* bv,
-                               cudaStream_t st) {
-    const dim3 grid(ceil_div(max_len, lg::kBertConvRows), batch);
-    lg::bert_to_bf16_kernel<<<grid, 256, 0, st>>>(q, k, v, lens, max_len, E, bq, bk, bv);
+                               int max_len, int n_heads, int head_dim, __nv_bfloat16* bq, __nv_bfloat16* bk,
+                               __nv_bfloat16* bv, int* order, cudaStream_t st) {
+    const dim3 grid(ceil_div(max_len, lg::kBertConvRows) + (order ? 1 : 0), batch);
+    lg::bert_to_bf16_kernel<<<grid, 256, 0, st>>>(q, k, v, lens, max_len, n_heads * head_dim, bq, bk, bv, n_heads,
+                                                  order);
     return cudaGetLastError();
+}
+
+// Length of the work order of a BERT batch (one int per tensor-core work item), or 0 when the
+// lengths could reach more key tiles than the order's counting sort has bins for (then the kernel
+// walks its items in their natural order).
+static size_t bert_order_ints(int n_heads, int batch, int max_len) {
+    if (ceil_div(max_len, lg::kTcKeys) >= lg::kOrderBins) return 0;
+    return size_t(n_heads) * ceil_div(max_len, lg::kTcRows) * batch;
 }
 
 int ligguf_cuda_bert_attn_async(ligguf_bert_attn* b, int batch, int max_len, const int* d_lens, const float* d_q,
@@ -1058,12 +1074,19 @@ int ligguf_cuda_bert_attn_async(ligguf_bert_attn* b, int batch, int max_len, con
         cap = size_t(b->max_batch) * b->max_len * E * 3;
         if (cudaMalloc(&b->bf, cap * sizeof(__nv_bfloat16)) != cudaSuccess)
             return fail(LIGGUF_ATTN_ENOMEM, "BERT bf16 operand buffers");
+        const size_t oc = bert_order_ints(b->n_heads, b->max_batch, b->max_len);
+        if (oc && cudaMalloc(&b->d_order, oc * sizeof(int)) != cudaSuccess)
+            return fail(LIGGUF_ATTN_ENOMEM, "BERT work-order buffer");
     }
+    // A smaller batch or max_len never needs more order entries than the handle's maxima.
+    int* order = bert_order_ints(b->n_heads, batch, max_len) ? b->d_order : nullptr;
     lg::TcArgs t = {};
     t.q = b->bf;
     t.k = b->bf + elems;
     t.v = b->bf + 2 * elems;
-    LG_CUDA(bert_convert(d_q, d_k, d_v, d_lens, batch, max_len, E, b->bf, b->bf + elems, b->bf + 2 * elems, st));
+    t.order = order;
+    LG_CUDA(bert_convert(d_q, d_k, d_v, d_lens, batch, max_len, b->n_heads, D, b->bf, b->bf + elems,
+                         b->bf + 2 * elems, order, st));
     t.out = d_out;
     t.q_rows = batch * max_len;
     t.q_heads = b->n_heads;
@@ -1133,13 +1156,18 @@ int ligguf_cuda_bert_attn_tc_noalloc(int n_heads, int head_dim, int batch, int m
     __nv_bfloat16* bk = reinterpret_cast<__nv_bfloat16*>(base + kNoallocOperandBytes);
     __nv_bfloat16* bv = reinterpret_cast<__nv_bfloat16*>(base + 2 * kNoallocOperandBytes);
     int* err = reinterpret_cast<int*>(base + 3 * kNoallocOperandBytes);
+    const size_t n_order = bert_order_ints(n_heads, batch, max_len);
+    int* order = n_order && n_order <= kNoallocOrderInts
+                     ? reinterpret_cast<int*>(base + 3 * kNoallocOperandBytes + 256)
+                     : nullptr;
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     LG_CUDA(cudaMemsetAsync(err, 0, sizeof(int), st));  // the previous call's error word must not leak
-    LG_CUDA(bert_convert(d_q, d_k, d_v, d_lens, batch, max_len, n_heads * head_dim, bq, bk, bv, st));
+    LG_CUDA(bert_convert(d_q, d_k, d_v, d_lens, batch, max_len, n_heads, head_dim, bq, bk, bv, order, st));
     lg::TcArgs t = {};
     t.q = bq;
     t.k = bk;
     t.v = bv;
+    t.order = order;
     t.out = d_out;
     t.q_rows = batch * max_len;
     t.q_heads = n_heads;

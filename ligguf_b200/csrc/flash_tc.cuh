@@ -45,10 +45,50 @@ struct TcArgs {
     int causal, q_pos0, nrep;
     float scale_log2;          // softmax scale times log2(e)
     int* err;
+    const int* order;  // null, or order[p] = the item taken at walk position p (a permutation)
 };
 
 constexpr int kTcRows = 128;  // query rows per tile (UMMA M)
 constexpr int kTcKeys = 128;  // keys per tile (UMMA N of S, K of P.V)
+
+// Work order for a BERT batch.  The items (head, query tile, batch entry; numbered as in tc_item)
+// are sorted by their number of key tiles, most first, so that the persistent CTAs' snake walk
+// (tc_item_index) deals out even shares whatever the sequence lengths: with lengths in the walk's
+// natural order the busiest CTA gets 13-37 % more key tiles than the mean on U[16, 512] lengths,
+// sorted 2-4 %.  A counting sort by one block; items of equal cost land in arbitrary order
+// (shared-memory atomics), which decides only which CTA computes an item, never its result.
+constexpr int kOrderBins = 1025;  // key-tile counts 0..1024: max_len up to 131072
+__device__ __forceinline__ int bert_group_cost(const int* lens, int g, int n_qt, int max_len) {
+    const int b = g / n_qt, y = g - b * n_qt;
+    const int r0 = (n_qt - 1 - y) * kTcRows;  // tc_item: y = 0 is the last query tile
+    const int len = min(lens[b], max_len);
+    return r0 >= len ? 0 : (len + kTcKeys - 1) / kTcKeys;
+}
+__device__ void bert_item_order(const int* __restrict__ lens, int batch, int max_len, int n_heads,
+                                int* __restrict__ order) {
+    __shared__ int bins[kOrderBins];
+    const int n_qt = (max_len + kTcRows - 1) / kTcRows;
+    const int top = (max_len + kTcKeys - 1) / kTcKeys;  // largest cost; the host keeps it < kOrderBins
+    const int groups = n_qt * batch;                    // group g = y + n_qt * b: n_heads items each
+    for (int i = threadIdx.x; i <= top; i += blockDim.x) bins[i] = 0;
+    __syncthreads();
+    for (int g = threadIdx.x; g < groups; g += blockDim.x)
+        atomicAdd(&bins[bert_group_cost(lens, g, n_qt, max_len)], 1);
+    __syncthreads();
+    if (threadIdx.x == 0) {  // exclusive scan, the largest cost first
+        int run = 0;
+        for (int c = top; c >= 0; --c) {
+            const int n = bins[c];
+            bins[c] = run;
+            run += n;
+        }
+    }
+    __syncthreads();
+    for (int g = threadIdx.x; g < groups; g += blockDim.x) {
+        const int p = atomicAdd(&bins[bert_group_cost(lens, g, n_qt, max_len)], 1);
+        for (int h = 0; h < n_heads; ++h) order[p * n_heads + h] = g * n_heads + h;
+    }
+}
 
 // BERT operands to bf16 in one pass, valid rows only: rows r < lens[b] of q, k and v are converted.
 // Padded rows of v inside the last key tile that holds valid keys are written as zeros (P.V
@@ -56,12 +96,18 @@ constexpr int kTcKeys = 128;  // keys per tile (UMMA N of S, K of P.V)
 // that one.  Padded rows of q and k are left as they are (their scores are masked or their outputs
 // discarded).
 // Block = kBertConvRows rows of one batch entry; 8 values per thread step (two 16-byte loads, one
-// 16-byte store).  Needs E % 8 == 0 and 16-byte aligned bases.
+// 16-byte store).  Needs E % 8 == 0 and 16-byte aligned bases.  With `order` set, the grid has one
+// more column of blocks, and its first block writes the work order (bert_item_order) instead.
 constexpr int kBertConvRows = 8;
 __global__ void __launch_bounds__(256) bert_to_bf16_kernel(const float* __restrict__ q, const float* __restrict__ k,
                                                            const float* __restrict__ v, const int* __restrict__ lens,
                                                            int max_len, int E, __nv_bfloat16* __restrict__ bq,
-                                                           __nv_bfloat16* __restrict__ bk, __nv_bfloat16* __restrict__ bv) {
+                                                           __nv_bfloat16* __restrict__ bk, __nv_bfloat16* __restrict__ bv,
+                                                           int n_heads, int* __restrict__ order) {
+    if (order && blockIdx.x == gridDim.x - 1) {
+        if (blockIdx.y == 0) bert_item_order(lens, gridDim.y, max_len, n_heads, order);
+        return;
+    }
     const int b = blockIdx.y;
     const int r0 = blockIdx.x * kBertConvRows;
     const int len = min(lens[b], max_len);
@@ -99,9 +145,9 @@ constexpr int kTcPvWarp = 2;  // the warp that issues the P.V MMAs
 // the softmax holds a whole 128-column S row in registers.  The sum of the three shares must not
 // exceed 3 x 168, or the increase waits forever; the launcher checks the kernel's register count.
 constexpr int kTcRegsLaunch = 168;
-constexpr int kTcRegsIssue = 88;
+constexpr int kTcRegsIssue = 96;
 constexpr int kTcRegsSoftmax = 240;
-constexpr int kTcRegsEpilogue = 160;
+constexpr int kTcRegsEpilogue = 152;
 static_assert(kTcRegsIssue + kTcRegsSoftmax + kTcRegsEpilogue <= 3 * kTcRegsLaunch, "register split too large");
 static_assert(kTcThreads * kTcRegsLaunch <= 65536, "launch register count does not fit an SM");
 // A kernel that uses tcgen05 runs one CTA per SM, which then owns all 512 TMEM columns:
@@ -292,6 +338,32 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
     return d;
 }
 
+// 2^x for a pair, on the FMA pipe instead of the MUFU unit, which the softmax otherwise saturates:
+// Cody-Waite reduction x = n + f (n = x rounded to an integer by adding 1.5 * 2^23, |f| <= 1/2),
+// 2^f from a cubic p(f) = 1 + f (c1 + f (c2 + f c3)) fitted to 2^f on [-1/2, 1/2] by minimax-
+// weighted least squares (max relative error 1.03e-4, below the 2^-9 rounding of P to bf16), and
+// 2^n added into the exponent field.  x <= -127 gives 0 (x is clamped there: n = -127, f = 0);
+// -126 > x > -127 gives a value below 2^-126 that is not exact, and bf16 P then holds zero or a
+// subnormal either way.  The softmax's x never exceeds +8.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+    x.x = fmaxf(x.x, -127.f);
+    x.y = fmaxf(x.y, -127.f);
+    const float2 t = fadd2(x, make_float2(12582912.f, 12582912.f));  // 1.5 * 2^23 + n
+    const float2 n = fadd2(t, make_float2(-12582912.f, -12582912.f));
+    const float2 f = ffma2(n, make_float2(-1.f, -1.f), x);
+    float2 p = ffma2(f, make_float2(0.05500665679574013f, 0.05500665679574013f),
+                     make_float2(0.24220559000968933f, 0.24220559000968933f));
+    p = ffma2(p, f, make_float2(0.6932826042175293f, 0.6932826042175293f));
+    p = ffma2(p, f, make_float2(1.f, 1.f));
+    // The low 9 bits of t's pattern hold n (two's complement); shifted into the exponent field they
+    // add n to p's exponent (the bits above wrap out of the word).
+    return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                       __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
+// Key pairs (c mod 8, in a row's 64 pairs) whose exp2 takes the polynomial: 2 of 8 (a quarter of
+// the elements).  Measured: a quarter beats none, three eighths and a half.
+constexpr unsigned kTcPolyPairs = 0x88u;
+
 // One work item: 128 query rows (one tile) of one head of one batch entry.  n_kv == 0 marks an item
 // of padded query rows only, which is written as zeros and never reaches the tensor cores.
 struct TcItem {
@@ -318,6 +390,13 @@ __device__ __forceinline__ TcItem tc_item(const TcArgs& a, int idx, int n_qt) {
 __device__ __forceinline__ int tc_item_index(int w) {
     const int G = gridDim.x;
     return w * G + ((w & 1) ? G - 1 - static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x));
+}
+// The item at walk position w of this CTA (through the work order when there is one), or -1 past
+// the last item.  Every role of the CTA walks the same sequence.
+__device__ __forceinline__ int tc_walk(const TcArgs& a, int w, int n_items) {
+    const int p = tc_item_index(w);
+    if (p >= n_items) return -1;
+    return a.order ? __ldg(a.order + p) : p;
 }
 
 template <int D>
@@ -399,8 +478,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 bool ok = true;
                 uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
                 for (int w = 0; ok; ++w) {
-                    const int idx = tc_item_index(w);
-                    if (idx >= n_items) break;
+                    const int idx = tc_walk(a, w, n_items);
+                    if (idx < 0) break;
                     const TcItem it = tc_item(a, idx, n_qt);
                     if (it.n_kv == 0) continue;
                     deadline = globaltimer_ns() + kWaitLimitNs;
@@ -473,8 +552,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
                 int t = 0, z = 0;
                 for (int w = 0; ok; ++w) {
-                    const int idx = tc_item_index(w);
-                    if (idx >= n_items) break;
+                    const int idx = tc_walk(a, w, n_items);
+                    if (idx < 0) break;
                     const int n_kv = tc_item(a, idx, n_qt).n_kv;
                     if (n_kv == 0) continue;
                     deadline = globaltimer_ns() + kWaitLimitNs;
@@ -547,8 +626,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         bool ok = true;
         int t = 0, z = 0;
         for (int w = 0; ok; ++w) {
-            const int idx = tc_item_index(w);
-            if (idx >= n_items) break;
+            const int idx = tc_walk(a, w, n_items);
+            if (idx < 0) break;
             const TcItem it = tc_item(a, idx, n_qt);
             if (it.n_kv == 0) continue;
             const uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
@@ -630,8 +709,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     for (int c = 0; c < 32; ++c) {
                         const int i = hc * 64 + 2 * c;
                         float2 e = ffma2(make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), cc, nm);
-                        e.x = fast_exp2(e.x);
-                        e.y = fast_exp2(e.y);
+                        if ((kTcPolyPairs >> (c & 7)) & 1u) {
+                            e = exp2_poly2(e);
+                        } else {
+                            e.x = fast_exp2(e.x);
+                            e.y = fast_exp2(e.y);
+                        }
                         pk[c] = pack_bf16(e.x, e.y);
                         rs4[c & 3] = fadd2(rs4[c & 3], e);
                     }
@@ -670,8 +753,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         uint32_t x[32];
         int z = 0;
         for (int w = 0; ok; ++w) {
-            const int idx = tc_item_index(w);
-            if (idx >= n_items) break;
+            const int idx = tc_walk(a, w, n_items);
+            if (idx < 0) break;
             const TcItem it = tc_item(a, idx, n_qt);
             const int row0 = it.r0 + quarter * 32;  // first sequence row of this warp's 32 rows
             float* obase = a.out + ((static_cast<size_t>(it.b) * a.q_seq + row0) * a.q_heads + it.h) * D;
