@@ -22,6 +22,8 @@
 //               to shared memory
 //   warps 8..11 epilogue: O / l from TMEM to global memory through a padded staging block (whole
 //               128-byte row segments per store), so the softmax warps never wait for it
+// Items are walked heaviest first: causal prefill by their numbering, BERT through a work order
+// sorted by key-tile count that the operand conversion kernel writes (bert_item_order).
 // TMEM: S double buffer [0, 256), O double-buffered by item after it.  An issuing thread loses
 // issue slots to the softmax warp on its SM sub-partition, so S and P.V are issued by two threads
 // on different sub-partitions, and tiles are 128 keys wide to halve the MMAs and barrier waits per
