@@ -185,8 +185,8 @@ int ligguf_cuda_bert_attn_async(ligguf_bert_attn* b, int batch, int max_len, con
  * Same computation as ligguf_cuda_bert_attn_async with LIGGUF_MODE_TC (bf16 operands on the
  * tcgen05 tensor cores, fp32 accumulation), but with no handle and no allocation: the bf16 copies
  * of q, k and v live in a fixed array inside the library, reserved on every GPU that loads it
- * (24 MiB + 256 B, held until the process exits).  Device pointers, enqueued on `stream`, on the
- * current device; layouts as ligguf_cuda_bert_attn.
+ * (24.25 MiB + 256 B with the kernel's work order, held until the process exits).  Device pointers,
+ * enqueued on `stream`, on the current device; layouts as ligguf_cuda_bert_attn.
  *   - Limit: batch*max_len*n_heads*head_dim <= LIGGUF_NOALLOC_MAX_ELEMS per tensor; larger calls
  *     return LIGGUF_ATTN_EINVAL without touching the GPU.
  *   - The first call on a device looks up the array's device address (cudaGetSymbolAddress); make
