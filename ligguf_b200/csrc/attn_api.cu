@@ -426,8 +426,20 @@ int launch_flash_tc_t(const lg::TcArgs& t, cudaStream_t st, int device) {
     }
     const int n_items = t.q_heads * ((t.q_seq + lg::kTcRows - 1) / lg::kTcRows) * t.batch;
     if (n_items <= 0) return LIGGUF_ATTN_OK;
-    kern<<<std::min(n_items, slots), lg::kTcThreads, lg::TcSmem<D>::kTotal, st>>>(tq, tk, tv, t);
-    LG_CUDA(cudaGetLastError());
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(std::min(n_items, slots), 1, 1);
+    lc.blockDim = dim3(lg::kTcThreads, 1, 1);
+    lc.dynamicSmemBytes = lg::TcSmem<D>::kTotal;
+    lc.stream = st;
+    // Programmatic dependent of the operand kernel launched just before it (prefill_prep_kernel or
+    // bert_to_bf16_kernel, which trigger at entry): the CTAs' set-up overlaps that grid's tail, and
+    // the kernel waits for it (griddepcontrol.wait) before any global access.
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    LG_CUDA(cudaLaunchKernelEx(&lc, kern, tq, tk, tv, t));
     return LIGGUF_ATTN_OK;
 }
 

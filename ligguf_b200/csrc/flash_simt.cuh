@@ -322,6 +322,9 @@ __device__ __forceinline__ void norm_rope_vec(float (&x)[D / 32], const float* _
 constexpr int kPrepWarps = 16;
 template <typename KV, int D>
 __global__ void __launch_bounds__(kPrepWarps * 32) prefill_prep_kernel(const PrepArgs a) {
+    // Launched in stream order (its predecessor has completed); the tensor-core kernel that follows
+    // is a programmatic dependent and may start its set-up once every block of this grid has begun.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     constexpr int E = D / 32;
     __shared__ float cs[D / 2], sn[D / 2];  // RoPE rotation of this token, shared by all heads
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

@@ -106,6 +106,9 @@ __global__ void __launch_bounds__(256) bert_to_bf16_kernel(const float* __restri
                                                            int max_len, int E, __nv_bfloat16* __restrict__ bq,
                                                            __nv_bfloat16* __restrict__ bk, __nv_bfloat16* __restrict__ bv,
                                                            int n_heads, int* __restrict__ order) {
+    // Launched in stream order (its predecessor has completed); the tensor-core kernel that follows
+    // is a programmatic dependent and may start its set-up once every block of this grid has begun.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (order && blockIdx.x == gridDim.x - 1) {
         if (blockIdx.y == 0) bert_item_order(lens, gridDim.y, max_len, n_heads, order);
         return;
@@ -470,6 +473,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // Launched as a programmatic dependent of the kernel that wrote the bf16 operands (and the work
+    // order): the set-up above touches only this CTA's shared memory and TMEM, and every global
+    // access below comes after that grid has completed.  This kernel does not trigger its own
+    // dependents early: they launch when it exits.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 
     if (warp < 4) {
         reg_dec<kTcRegsIssue>();
