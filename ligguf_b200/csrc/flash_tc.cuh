@@ -56,8 +56,8 @@ constexpr int kTcKeys = 128;  // keys per tile (UMMA N of S, K of P.V)
 // Work order for a BERT batch.  The items (head, query tile, batch entry; numbered as in tc_item)
 // are sorted by their number of key tiles, most first, so that the persistent CTAs' snake walk
 // (tc_item_index) deals out even shares whatever the sequence lengths: with lengths in the walk's
-// natural order the busiest CTA gets 13-37 % more key tiles than the mean on U[16, 512] lengths,
-// sorted 2-4 %.  A counting sort by one block; items of equal cost land in arbitrary order
+// natural order the busiest CTA gets 14-39 % more key tiles than the mean on U[16, 512] lengths,
+// sorted 1-4 %.  A counting sort by one block; items of equal cost land in arbitrary order
 // (shared-memory atomics), which decides only which CTA computes an item, never its result.
 constexpr int kOrderBins = 1025;  // key-tile counts 0..1024: max_len up to 131072
 __device__ __forceinline__ int bert_group_cost(const int* lens, int g, int n_qt, int max_len) {
