@@ -118,11 +118,31 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------------ CPU side
-def cpu_baseline(w, target_s: float = 10.0, max_layers: int = 2):
-    """The reference's CPU attention (oracle/_ref: its fast/lil_math.cpp built from source, AVX2 dots,
-    `omp parallel for` over heads) on a bounded sample of the workload: one decode step of up to
-    `max_layers` layers with a full-length fp32 cache, repeated for about `target_s` seconds; tokens/s
-    extrapolated to all layers.  Falls back to the C restatement when the reference build is absent."""
+def host_cores() -> int:
+    """Cores this process may run on (the reference arm and the CPU baseline use all of them,
+    whatever OMP_NUM_THREADS a launcher such as torchrun exported)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
+def bench_config(w, world: int, gather: str) -> dict:
+    """The `config` of the JSON line, identical in both arms."""
+    return {"workload": WORKLOAD, "layers": w.n_layers, "ctx": w.pos + 1, "kv": "fp32",
+            "heads": [w.n_heads, w.n_kv_heads, w.head_dim],
+            "parallelism": (f"kv-head shards x{world} + per-layer all-gather of head outputs "
+                            f"({'decode-kernel NVLink peer stores' if gather == 'p2p' else 'NCCL'})")
+            if world > 1 else "single GPU",
+            "l2": "inputs larger than L2 (KV bytes per step >> 126 MB); no flush"}
+
+
+def cpu_step_runner(w):
+    """The reference's CPU attention (oracle/_ref: its fast/lil_math.cpp built from source with its
+    flags, AVX2 dots, `omp parallel for` over the heads as its MULTITHREAD) set up for full decode
+    steps of workload `w`: every layer's fp32 cache [0, pos) in host memory (9.66 GB at 32K), the
+    step's q, k, v and QK-norm weights.  Falls back to the C restatement when the reference build is
+    absent.  Returns (run_one_step, info)."""
     import numpy as np
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     from oracle import oracle as orc
@@ -130,13 +150,14 @@ def cpu_baseline(w, target_s: float = 10.0, max_layers: int = 2):
         chk, kind = orc.Checker("ref"), "reference"
     except FileNotFoundError:
         chk, kind = orc.Checker("port"), "port"
-    nl = max(1, min(max_layers, w.n_layers))
+    cores = host_cores()
+    threads = chk.set_threads(min(cores, w.n_heads))  # the loop is over the heads: more threads idle
     kv_dim = w.n_kv_heads * w.head_dim
     cfg = orc.Checker.cfg(w.n_heads, w.n_kv_heads, w.head_dim, w.n_context, w.rope_dim, w.eps, int(w.qk_norm),
                           0, 0)
     freq = orc.rope_table(w.rope_dim, w.rope_base)
     layers = []
-    for l in range(nl):
+    for l in range(w.n_layers):
         kc = np.empty((w.n_context, kv_dim), dtype=np.float32)
         vc = np.empty_like(kc)
         orc.kv_synth(kc, 0, kv_dim, kv_dim, 0, l, 1, 0, w.pos, w.seed, w.scale)
@@ -148,23 +169,52 @@ def cpu_baseline(w, target_s: float = 10.0, max_layers: int = 2):
         qg = orc.synth_f32(w.head_dim, w.seed, sid(6), 0, 0.02, 1.0)
         kg = orc.synth_f32(w.head_dim, w.seed, sid(7), 0, 0.02, 1.0)
         layers.append((kc, vc, q, k, v, qg, kg))
-    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
-    times = []
-    t_end = time.perf_counter() + target_s
-    chk.decode_layer(cfg, *layers[0][:2], freq, layers[0][5], layers[0][6], w.pos, *layers[0][2:5])  # warm
-    while time.perf_counter() < t_end or not times:
-        t0 = time.perf_counter()
+
+    def step():
         for (kc, vc, q, k, v, qg, kg) in layers:
             chk.decode_layer(cfg, kc, vc, freq, qg, kg, w.pos, q, k, v)
-        times.append((time.perf_counter() - t0) / nl)
-    per_layer = statistics.median(times)
-    tok_s = 1.0 / (per_layer * w.n_layers)
-    return {"value": tok_s, "unit": "tokens/s", "cores": min(threads, w.n_heads), "kind": kind,
-            "sample": f"{nl} of {w.n_layers} layers, full {w.pos + 1}-position fp32 cache, {len(times)} repeats "
-                      f"(median {per_layer * 1e3:.1f} ms/layer), tokens/s extrapolated to {w.n_layers} layers; "
-                      f"OpenMP over the {w.n_heads} heads as the reference's MULTITHREAD",
-            "threads_available": threads,
-            "gbs": w.kv_bytes_per_token() * tok_s / 1e9}
+
+    return step, {"kind": kind, "cores": threads, "cores_available": cores}
+
+
+def cpu_timed_steps(w, steps: int, warmup: int):
+    """`warmup` untimed, then `steps` timed full decode steps (all layers) of the reference's CPU path."""
+    step, info = cpu_step_runner(w)
+    for _ in range(warmup):
+        step()
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    info.update(value=steps / total, ms_per_step=1e3 * total / steps, steps=steps, warmup=warmup,
+                sample=f"{steps} timed full decode steps ({w.n_layers} layers, {w.pos + 1}-position fp32 cache "
+                       f"each) after {warmup} untimed; OpenMP over the {w.n_heads} heads (the reference's "
+                       f"MULTITHREAD) on {info['cores']} threads of {info['cores_available']} host cores")
+    return info
+
+
+def cpu_baseline(w, target_s: float = 10.0):
+    """The CPU baseline beside the GPU line: full decode steps of the reference's CPU path for about
+    `target_s` seconds (after one warm-up step)."""
+    step, info = cpu_step_runner(w)
+    step()
+    times = []
+    t_end = time.perf_counter() + target_s
+    while time.perf_counter() < t_end or not times:
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    tok_s = len(times) / total
+    info.update(value=tok_s, unit="tokens/s",
+                sample=f"{len(times)} full decode steps ({w.n_layers} layers, {w.pos + 1}-position fp32 cache "
+                       f"each, {1e3 * total / len(times):.0f} ms per step) after one untimed; OpenMP over the "
+                       f"{w.n_heads} heads (the reference's MULTITHREAD) on {info['cores']} threads of "
+                       f"{info['cores_available']} host cores",
+                gbs=w.kv_bytes_per_token() * tok_s / 1e9)
+    return info
 
 
 def run_reference_arm(args):
@@ -173,16 +223,17 @@ def run_reference_arm(args):
     if rank != 0:
         return 0
     w = DECODE_WORKLOADS[WORKLOAD]
-    per_step = max(1.0, 30.0 / max(1, args.steps + args.warmup))
-    cb = cpu_baseline(w, target_s=per_step * (args.steps + args.warmup))
-    line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tokens/s",
+    r = cpu_timed_steps(w, args.steps, args.warmup)
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    line = {"impl": "reference", "metric": METRIC, "value": r["value"], "unit": "tokens/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1e3 / cb["value"], "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
-            "config": {"workload": WORKLOAD, "layers": w.n_layers, "ctx": w.pos + 1, "kv": "fp32",
-                       "heads": [w.n_heads, w.n_kv_heads, w.head_dim], "parallelism": "cpu"},
-            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
-            "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded generator, ~N(0,1)); random-init "
+                                                         "QK-norm weights",
+            "config": bench_config(w, world, args.gather),
+            "cpu_baseline": {"value": r["value"], "unit": "tokens/s", "cores": r["cores"], "kind": r["kind"],
+                             "sample": r["sample"]},
+            "e2e": {"value": r["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "gpu_launches": 0}
     print(json.dumps(line), flush=True)
     return 0
@@ -237,6 +288,60 @@ def decode_setup(w, rank, world, local):
     return h, s, q, k, v
 
 
+def port_decode_layer(w, layer: int):
+    """The C restatement of the reference's decode (oracle, port) of one whole layer of workload `w`,
+    unsharded: the checker for the parity line."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from oracle import oracle as orc
+    chk = orc.Checker("port")
+    chk.set_threads(host_cores())
+    kv_dim = w.n_kv_heads * w.head_dim
+    kc = np.empty((w.n_context, kv_dim), dtype=np.float32)
+    vc = np.empty_like(kc)
+    orc.kv_synth(kc, 0, kv_dim, kv_dim, 0, layer, 1, 0, w.pos, w.seed, w.scale)
+    orc.kv_synth(vc, 0, kv_dim, kv_dim, 0, layer, 2, 0, w.pos, w.seed, w.scale)
+    sid = lambda t: (t << 32) | layer  # noqa: E731
+    q = orc.synth_f32(w.n_heads * w.head_dim, w.seed, sid(3), 0, w.scale)
+    k = orc.synth_f32(kv_dim, w.seed, sid(4), 0, w.scale)
+    v = orc.synth_f32(kv_dim, w.seed, sid(5), 0, w.scale)
+    qg = orc.synth_f32(w.head_dim, w.seed, sid(6), 0, 0.02, 1.0) if w.qk_norm else None
+    kg = orc.synth_f32(w.head_dim, w.seed, sid(7), 0, 0.02, 1.0) if w.qk_norm else None
+    cfg = orc.Checker.cfg(w.n_heads, w.n_kv_heads, w.head_dim, w.n_context, w.rope_dim, w.eps, int(w.qk_norm),
+                          0, 0)
+    return chk.decode_layer(cfg, kc, vc, orc.rope_table(w.rope_dim, w.rope_base), qg, kg, w.pos, q, k, v)
+
+
+def decode_parity(args, w, h, q, k, v, out, full, rank, world, pg, layer: int = 0):
+    """Untimed, before the timed region: one layer through the same path as the timed steps (at N > 1
+    the same sharded decode and the same gather), then rank 0's whole [n_heads*head_dim] output against
+    the unsharded decode of the C restatement of the reference.  Every rank takes the same steps."""
+    import numpy as np
+    import torch
+    if world > 1 and args.gather == "p2p":
+        h.decode_gather_async(layer, w.pos, q[layer], k[layer], v[layer])
+        h.gather_wait_async(layer, full[layer])
+    else:
+        h.decode_async(layer, w.pos, q[layer], k[layer], v[layer], out[layer])
+        if world > 1:
+            pg.all_gather_into_tensor(full[layer], out[layer])
+    torch.cuda.synchronize()
+    h.sync()
+    res = None
+    if rank == 0:
+        got = full[layer].cpu().numpy()
+        ref = port_decode_layer(w, layer)
+        err = float(np.abs(got.astype(np.float64) - ref).max() / max(float(np.abs(ref).max()), 1e-30))
+        res = {"max_rel_err": err, "tol": 1e-4, "ok": bool(err <= 1e-4), "layer": layer,
+               "checked": f"the whole {w.n_heads}x{w.head_dim} output of layer {layer} on rank 0"
+                          + (f" after the {'peer-store' if args.gather == 'p2p' else 'NCCL'} gather of {world} "
+                             f"shards" if world > 1 else ""),
+               "against": "oracle port (C restatement of the reference), unsharded"}
+    if world > 1:
+        pg.barrier()
+    return res
+
+
 def bench_decode(args, w, rank, world, local, pg, peaks):
     import torch
     h, s, q, k, v = decode_setup(w, rank, world, local)
@@ -250,6 +355,7 @@ def bench_decode(args, w, rank, world, local, pg, peaks):
         handles = [None] * world
         pg.all_gather_object(handles, mine)
         h.gather_open(rank, handles)
+    parity = decode_parity(args, w, h, q, k, v, out, full, rank, world, pg)
 
     def step(gather=args.gather):
         for l in range(L):
@@ -319,7 +425,7 @@ def bench_decode(args, w, rank, world, local, pg, peaks):
                      "algorithmic_bytes_per_launch": bytes_launch,
                      "peak_source": f"{peaks['source']} hbm_gbs (copy)"},
         "hbm_gbs_step": w.kv_bytes_per_token() * tok_s / 1e9,
-        "e2e": e2e, "gpu_launches": args.steps * L * per_layer, "other_gather": other,
+        "e2e": e2e, "gpu_launches": args.steps * L * per_layer, "other_gather": other, "parity": parity,
     }
 
 
@@ -403,12 +509,18 @@ def _time_ms(fn, iters, warm=3):
     return a.elapsed_time(b) / iters
 
 
-def extra_decode_4k(peaks):
-    """qwen3_8b_decode_4k: one token step (36 layer launches) captured in a CUDA graph."""
+def extra_decode_graph(peaks, w):
+    """A decode workload that fits L2 poorly or not at all: one token step (a launch per layer)
+    captured in a CUDA graph and replayed.  The replays run back to back, so a layer's cache rows may
+    still be in L2 from the previous replay only when the whole step's cache fits L2 (the 4K step
+    is 1.2 GB, the TinyLlama step 23 MB: that one is reported with an L2 flush between replays)."""
     import torch
-    from ligguf_b200.workloads import QWEN3_DECODE_4K as w
     h, s, q, k, v = decode_setup(w, 0, 1, torch.cuda.current_device())
     out = torch.empty(w.n_layers, w.n_heads * w.head_dim, device=q.device)
+    step_bytes = w.kv_bytes_per_token()
+    flush = None
+    if step_bytes < 512 << 20:  # fits (or nearly fits) the 126 MB L2: flush it between replays
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=q.device)
 
     def step():
         for l in range(w.n_layers):
@@ -418,13 +530,29 @@ def extra_decode_4k(peaks):
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
         step()
-    ms = _time_ms(g.replay, 50)
+    if flush is None:
+        ms = _time_ms(g.replay, 50)
+    else:  # time each replay alone, after writing a buffer twice the L2 size
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(50)]
+        for _ in range(3):
+            flush.zero_()
+            g.replay()
+        for a, b in ev:
+            flush.zero_()
+            a.record()
+            g.replay()
+            b.record()
+        torch.cuda.synchronize()
+        ms = statistics.median(a.elapsed_time(b) for a, b in ev)
     h.sync()
     del g
     h.close()
-    gbs = w.kv_bytes_per_token() / (ms * 1e-3) / 1e9
+    gbs = step_bytes / (ms * 1e-3) / 1e9
     return {"tokens_s": 1e3 / ms, "ms_per_token": ms, "hbm_gbs": gbs, "frac_of_hbm": gbs / peaks["hbm_gbs"],
-            "note": "CUDA-graph replay of the 36 per-layer launches; GB/s counts algorithmic K+V bytes"}
+            "layers": w.n_layers, "ctx": w.pos + 1,
+            "note": "CUDA-graph replay of the per-layer launches; GB/s counts algorithmic K+V bytes"
+                    + ("; L2 flushed (256 MB write) before each timed replay" if flush is not None else
+                       "; inputs larger than L2, replays back to back")}
 
 
 def extra_prefill(peaks, mode):
@@ -494,7 +622,9 @@ def extra_bert(peaks, mode):
 
 def run_extras(peaks):
     extra = {}
-    jobs = [("qwen3_8b_decode_4k", lambda: extra_decode_4k(peaks)),
+    from ligguf_b200.workloads import QWEN3_DECODE_4K, TINYLLAMA_DECODE
+    jobs = [("tinyllama_decode_512", lambda: extra_decode_graph(peaks, TINYLLAMA_DECODE)),
+            ("qwen3_8b_decode_4k", lambda: extra_decode_graph(peaks, QWEN3_DECODE_4K)),
             ("qwen3_8b_prefill_2048_simt_fp32", lambda: extra_prefill(peaks, 0)),
             ("qwen3_8b_prefill_2048_tc_bf16", lambda: extra_prefill(peaks, 1)),
             ("bert_base_attn_simt_fp32", lambda: extra_bert(peaks, 0)),
@@ -586,15 +716,10 @@ def main():
             "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded generator, ~N(0,1)); random-init QK-norm weights",
-            "config": {"workload": WORKLOAD, "layers": w.n_layers, "ctx": w.pos + 1, "kv": "fp32",
-                       "heads": [w.n_heads, w.n_kv_heads, w.head_dim],
-                       "parallelism": (f"kv-head shards x{world} + per-layer all-gather of head outputs "
-                                       f"({'decode-kernel NVLink peer stores' if args.gather == 'p2p' else 'NCCL'})")
-                       if world > 1 else "single GPU",
-                       "l2": "inputs larger than L2 (KV bytes per step >> 126 MB); no flush"},
+            "config": bench_config(w, world, args.gather),
             "hbm_gbs": res["hbm_gbs_step"],
             "roofline": res["roofline"], "clocks": res["clocks"], "e2e": res["e2e"],
-            "gpu_launches": res["gpu_launches"],
+            "gpu_launches": res["gpu_launches"], "parity": res["parity"],
         }
         if res.get("other_gather"):
             line["other_gather"] = res["other_gather"]

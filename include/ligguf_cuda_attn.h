@@ -190,15 +190,20 @@ int ligguf_cuda_bert_attn_async(ligguf_bert_attn* b, int batch, int max_len, con
  *   - Limit: batch*max_len*n_heads*head_dim <= LIGGUF_NOALLOC_MAX_ELEMS per tensor; larger calls
  *     return LIGGUF_ATTN_EINVAL without touching the GPU.
  *   - The first call on a device looks up the array's device address (cudaGetSymbolAddress); make
- *     that first call before any stream capture.
+ *     that first call before any stream capture.  The address is looked up again when the device's
+ *     context changes (after a cudaDeviceReset); a call must not be in flight across a reset.
  *   - Every call reuses the same array: calls whose work overlaps on the GPU (other streams, other
  *     host threads) race and corrupt each other; serialise them.  The kernel's error word is cleared
- *     at the start of each call; a bounded in-kernel wait that gives up leaves `d_out` unwritten and
- *     is not reported back through this call. */
+ *     at the start of each call.  A bounded in-kernel wait that gives up leaves `d_out` unwritten;
+ *     the call itself has already returned, so ask ligguf_cuda_bert_attn_tc_noalloc_status. */
 #define LIGGUF_NOALLOC_MAX_ELEMS (1 << 22)
 int ligguf_cuda_bert_attn_tc_noalloc(int n_heads, int head_dim, int batch, int max_len, const int* d_lens,
                                      const float* d_q, const float* d_k, const float* d_v, float* d_out,
                                      void* stream);
+/* Outcome of the no-allocation calls enqueued on the current device: waits for `stream` (a
+ * cudaStream_t, NULL = legacy default), then returns LIGGUF_ATTN_ETIMEDOUT (and clears the word) if a
+ * bounded wait in one of them gave up since the last call began, else 0.  Allocates nothing. */
+int ligguf_cuda_bert_attn_tc_noalloc_status(void* stream);
 
 /* ---- seeded synthetic inputs ------------------------------------------------------------- */
 /* Tensor ids of the synthetic generator's streams. */

@@ -72,6 +72,7 @@ _PROTOS = {
     "ligguf_cuda_bert_attn": [_vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _i],
     "ligguf_cuda_bert_attn_async": [_vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _i, _vp],
     "ligguf_cuda_bert_attn_tc_noalloc": [_i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp],
+    "ligguf_cuda_bert_attn_tc_noalloc_status": [_vp],
     "ligguf_cuda_synth_fill": [_vp, _i, _sz, _u64, _u64, _u64, _f, _f, _vp],
 }
 

@@ -592,12 +592,36 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocBytes];
 namespace {
 std::mutex g_noalloc_mu;
 void* g_noalloc_addr[64] = {};
+CUcontext g_noalloc_ctx[64] = {};  // the context each cached address belongs to
 
-// Device address of g_noalloc_scratch on the current device (looked up on the first call there).
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+CtxGetCurrentFn ctx_get_current() {
+    static CtxGetCurrentFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<CtxGetCurrentFn>(p);
+    }
+    return fn;
+}
+
+CUcontext current_ctx() {
+    CUcontext c = nullptr;
+    if (auto f = ctx_get_current()) {
+        if (f(&c) != CUDA_SUCCESS) c = nullptr;
+    }
+    return c;
+}
+
+// Device address of g_noalloc_scratch on the current device.  Looked up on the first call there, and
+// again whenever the current context is not the one the cached address came from (after a
+// cudaDeviceReset the module is loaded anew and the old address is stale).
 int noalloc_scratch(int device, unsigned char** out) {
     if (device < 0 || device >= 64) return fail(LIGGUF_ATTN_EINVAL, "device %d", device);
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (!g_noalloc_addr[device]) {
+    if (!g_noalloc_addr[device] || current_ctx() != g_noalloc_ctx[device]) {
         void* p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess || !p) {
@@ -606,6 +630,7 @@ int noalloc_scratch(int device, unsigned char** out) {
                         cudaGetErrorString(e));
         }
         g_noalloc_addr[device] = p;
+        g_noalloc_ctx[device] = current_ctx();  // the lookup made the device's context current
     }
     *out = static_cast<unsigned char*>(g_noalloc_addr[device]);
     return LIGGUF_ATTN_OK;
@@ -1195,6 +1220,26 @@ int ligguf_cuda_bert_attn_tc_noalloc(int n_heads, int head_dim, int batch, int m
     t.scale_log2 = (1.0f / sqrtf(static_cast<float>(head_dim))) * 1.4426950408889634f;
     t.err = err;
     return launch_flash_tc(t, head_dim, st, device);
+}
+
+int ligguf_cuda_bert_attn_tc_noalloc_status(void* stream) {
+    int device = 0;
+    LG_CUDA(cudaGetDevice(&device));
+    unsigned char* base = nullptr;
+    int rc = noalloc_scratch(device, &base);
+    if (rc) return rc;
+    int* err = reinterpret_cast<int*>(base + 3 * kNoallocOperandBytes);
+    LG_CUDA(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+    int code = 0;
+    LG_CUDA(cudaMemcpy(&code, err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (code) {
+        LG_CUDA(cudaMemset(err, 0, sizeof(int)));
+        return fail(LIGGUF_ATTN_ETIMEDOUT,
+                    "a bounded wait in the no-allocation BERT kernel gave up (kernel error code %d); its output "
+                    "was not written",
+                    code);
+    }
+    return LIGGUF_ATTN_OK;
 }
 
 // ---------------------------------------------------------------------------- synth

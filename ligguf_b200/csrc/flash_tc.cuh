@@ -93,10 +93,12 @@ __device__ void bert_item_order(const int* __restrict__ lens, int batch, int max
 }
 
 // BERT operands to bf16 in one pass, valid rows only: rows r < lens[b] of q, k and v are converted.
-// Padded rows of v inside the last key tile that holds valid keys are written as zeros (P.V
-// multiplies them by P = 0, so they must be finite); the tensor-core kernel reads no key tile past
-// that one.  Padded rows of q and k are left as they are (their scores are masked or their outputs
-// discarded).
+// Every padded v row that some key tile reads is written as zeros (P.V multiplies it by P = 0, and
+// 0 * NaN is NaN, so it must be finite whatever the buffer held before): the rows inside this
+// entry's last key tile that holds valid keys, and - when max_len is not a multiple of the tile -
+// the first rows of this entry that the previous entry's last tile runs into.  The tensor-core
+// kernel reads no other padded row.  Padded rows of q and k are left as they are (their scores are
+// masked or their outputs discarded).
 // Block = kBertConvRows rows of one batch entry; 8 values per thread step (two 16-byte loads, one
 // 16-byte store).  Needs E % 8 == 0 and 16-byte aligned bases.  With `order` set, the grid has one
 // more column of blocks, and its first block writes the work order (bert_item_order) instead.
@@ -116,7 +118,11 @@ __global__ void __launch_bounds__(256) bert_to_bf16_kernel(const float* __restri
     const int b = blockIdx.y;
     const int r0 = blockIdx.x * kBertConvRows;
     const int len = min(lens[b], max_len);
-    const int v_zero_end = min(max_len, (len + kTcKeys - 1) / kTcKeys * kTcKeys);  // end of the last key tile read
+    // Key tiles of entry b start at multiples of kTcKeys from its first row, so its last tile may
+    // run up to round_up(max_len) - max_len rows into entry b + 1.
+    const int tile_end = (len + kTcKeys - 1) / kTcKeys * kTcKeys;
+    const int overhang = b > 0 ? (max_len + kTcKeys - 1) / kTcKeys * kTcKeys - max_len : 0;
+    const int v_zero_end = min(max_len, max(tile_end, overhang));
     const int units = E / 8;  // 16-byte output units per row
     const int per_tensor = kBertConvRows * units;
     for (int u = threadIdx.x; u < 3 * per_tensor; u += blockDim.x) {

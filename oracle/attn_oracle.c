@@ -30,6 +30,9 @@
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
 
 #define LO_KV_F32 0
 #define LO_KV_F16 1
@@ -359,4 +362,17 @@ void lo_kv_synth(void* cache, int kv_type, int kv_dim_shard, int kv_dim_full, in
             kv_store(cache, kv_type, (size_t)t * kv_dim_shard + c, lo_synth_one(base, idx, mul, 0.0f));
         }
     }
+}
+
+/* OpenMP thread count of this library's parallel loops (a process launcher may have exported
+ * OMP_NUM_THREADS=1 before the library loaded); returns the count now in effect. */
+int lo_set_threads(int n)
+{
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+    return omp_get_max_threads();
+#else
+    (void)n;
+    return 1;
+#endif
 }

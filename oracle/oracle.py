@@ -90,6 +90,7 @@ def port_lib():
         lib.lo_split_even.argtypes = [_c_int, _c_int, _c_int, ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]
         lib.lo_kv_synth.argtypes = [_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
                                     _c_u64, _c_float]
+        lib.lo_set_threads.argtypes = [_c_int]
         _port = lib
     return _port
 
@@ -201,6 +202,12 @@ class Checker:
 
     def _f(self, name):
         return getattr(self.lib, self.p + name)
+
+    def set_threads(self, n: int) -> int:
+        """OpenMP threads of this library's loops (independent of OMP_NUM_THREADS); returns the count."""
+        f = self._f("set_threads")
+        f.argtypes = [_c_int]
+        return int(f(int(n)))
 
     @staticmethod
     def cfg(n_heads, n_kv_heads, head_dim, n_context, rope_dim, eps=1e-6, qk_norm=0, kv_type=KV_F32,

@@ -22,6 +22,8 @@
 #include <string.h>
 #include <vector>
 
+#include <omp.h>
+
 #include "lil_gguf.h"
 #include "lil_math.h"
 
@@ -188,4 +190,12 @@ extern "C" int rf_bert_attn(int n_heads, int head_dim, int batch, int max_len, c
         }
     }
     return 0;
+}
+
+/* Thread count of the `omp parallel for` over heads (the reference's MULTITHREAD), whatever
+ * OMP_NUM_THREADS the process was started with; returns the count now in effect. */
+extern "C" int rf_set_threads(int n)
+{
+    if (n > 0) omp_set_num_threads(n);
+    return omp_get_max_threads();
 }

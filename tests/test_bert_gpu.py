@@ -71,3 +71,21 @@ def test_bert_scores_growing_along_the_sequence(gpu, mode, tol):
     out = gpu_bert(c, mode)
     ref = cases.run_bert(orc.Checker("port"), c)
     assert cases.rel_err(out, ref) <= tol
+
+
+def test_bert_tc_stale_operand_rows_cannot_poison_a_later_call(gpu):
+    """The handle keeps its bf16 operand buffer across calls.  A call whose q, k and v are all NaN
+    fills it with NaN; the next call has lens (200, 0) at max_len 200, so the first sequence's second
+    key tile (rows 128..255) runs 56 rows into the empty second sequence.  Those v rows are
+    multiplied by P = 0 and must have been zeroed by the conversion, not left stale (0 * NaN = NaN)."""
+    from ligguf_b200 import CudaBertAttention
+    H, D = 8, 128
+    h = CudaBertAttention(H, D, 2, 512)
+    poison = cases.bert_case(H=H, D=D, lens=(512, 512), max_len=512, scale=0.125, seed=905)
+    nan = np.full_like(poison["q"], np.nan)
+    h.attn(poison["lens"], nan, nan, nan, 1)
+    c = cases.bert_case(H=H, D=D, lens=(200, 0), max_len=200, scale=0.125, seed=906)
+    out = h.attn(c["lens"], c["q"], c["k"], c["v"], 1)
+    h.close()
+    assert np.isfinite(out).all()
+    assert cases.rel_err(out, cases.run_bert(orc.Checker("port"), c)) <= 2e-2
