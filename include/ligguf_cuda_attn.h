@@ -133,6 +133,23 @@ int ligguf_cuda_attn_kv_download(ligguf_attn* h, int layer, int pos0, int n, voi
                                  void* host_v);
 int ligguf_cuda_attn_kv_upload(ligguf_attn* h, int layer, int pos0, int n, const void* host_k,
                                const void* host_v);
+/* FAST engine state file (`model_file`, fast/common.h:26-31) straight from / into the HBM cache,
+ * byte for byte what save_model_state / load_model_state write and read
+ * (fast/ligguf_fast_qk.cpp:216-302): the packed 24-byte header {int pos; int n_context;
+ * uint64_t kv_size; uint64_t logits_size}, then for K and then V, each layer's rows [0, pos) as
+ * [pos][kv_dim] fp16, then logits_size fp32 logits.  The handle must hold the whole model (no SARA
+ * shard) with kv_type LIGGUF_KV_F16, the format's element type.
+ *   save: `pos` cached rows (1 <= pos <= n_context) and the caller's `logits` (host, n_logits
+ *         floats; the reference saves nothing when pos or the logits are empty).
+ *   load: checks the header as the reference does (non-zero sizes, kv_size = n_layers*pos*kv_dim,
+ *         logits_size = n_logits) and that pos fits the handle's n_context; uploads the rows and
+ *         fills `logits`; *pos_out / *n_context_out (either may be NULL) get the header's values.
+ *         A file that fails a check leaves the cache and `logits` untouched (LIGGUF_ATTN_EINVAL).
+ * Synchronous; errors in opening, reading or writing the file return LIGGUF_ATTN_EINVAL. */
+int ligguf_cuda_attn_state_save(ligguf_attn* h, const char* path, int pos, const float* logits,
+                                uint64_t n_logits);
+int ligguf_cuda_attn_state_load(ligguf_attn* h, const char* path, int* pos_out, int* n_context_out,
+                                float* logits, uint64_t n_logits);
 /* Fills cache rows [pos0, pos0+n) of layers [layer0, layer0+n_layers) with the library's seeded
  * synthetic generator (ligguf_cuda_synth_fill, tensor ids LIGGUF_SYNTH_K / _V), indexed by the
  * unsharded element (row*n_kv_heads*head_dim + kv_head*head_dim + d) so that every sharding of

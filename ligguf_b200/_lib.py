@@ -61,6 +61,8 @@ _PROTOS = {
     "ligguf_cuda_attn_prefill_async": [_vp, _i, _i, _i, _vp, _vp, _vp, _vp, _i, _vp],
     "ligguf_cuda_attn_kv_download": [_vp, _i, _i, _i, _vp, _vp],
     "ligguf_cuda_attn_kv_upload": [_vp, _i, _i, _i, _vp, _vp],
+    "ligguf_cuda_attn_state_save": [_vp, _cp, _i, _vp, _u64],
+    "ligguf_cuda_attn_state_load": [_vp, _cp, ctypes.POINTER(_i), ctypes.POINTER(_i), _vp, _u64],
     "ligguf_cuda_attn_kv_synth": [_vp, _i, _i, _i, _i, _u64, _f],
     "ligguf_cuda_attn_sync": [_vp],
     "ligguf_cuda_attn_gather_ipc_handle": [_vp, _vp, _sz],

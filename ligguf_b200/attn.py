@@ -13,6 +13,7 @@ Errors raise ``LigGufAttnError`` carrying the library's status code and reason.
 from __future__ import annotations
 
 import ctypes
+import os
 from dataclasses import dataclass
 
 import numpy as np
@@ -190,6 +191,22 @@ class CudaAttention:
         n = k.size // self.kv_dim
         check(self.lib.ligguf_cuda_attn_kv_upload(self._h, layer, pos0, n, k.ctypes.data, v.ctypes.data),
               "ligguf_cuda_attn_kv_upload")
+
+    def state_save(self, path: str, pos: int, logits) -> None:
+        """The engine's state file (save_model_state, fast/ligguf_fast_qk.cpp:266-302) from the HBM
+        cache: header, fp16 K rows [0, pos) per layer, V rows, then ``logits``."""
+        lg = np.ascontiguousarray(logits, dtype=np.float32)
+        check(self.lib.ligguf_cuda_attn_state_save(self._h, os.fsencode(path), pos, lg.ctypes.data, lg.size),
+              "ligguf_cuda_attn_state_save")
+
+    def state_load(self, path: str, n_logits: int):
+        """load_model_state (fast/ligguf_fast_qk.cpp:216-264) into the HBM cache; returns
+        (pos, n_context, logits) from the file."""
+        lg = np.empty(n_logits, dtype=np.float32)
+        pos, n_ctx = ctypes.c_int(), ctypes.c_int()
+        check(self.lib.ligguf_cuda_attn_state_load(self._h, os.fsencode(path), ctypes.byref(pos), ctypes.byref(n_ctx),
+                                                   lg.ctypes.data, n_logits), "ligguf_cuda_attn_state_load")
+        return pos.value, n_ctx.value, lg
 
     def kv_synth(self, layer0: int, n_layers: int, pos0: int, n: int, seed: int, scale: float):
         check(self.lib.ligguf_cuda_attn_kv_synth(self._h, layer0, n_layers, pos0, n, seed, scale),

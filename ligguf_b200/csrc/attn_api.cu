@@ -309,7 +309,20 @@ int decode_enqueue(ligguf_attn* h, int layer, int pos, const float* dq, const fl
     // kDecodeMaxGroups counters per head.
     const int mg = lg::decode_merge_group(h->nrep, D);
     a.n_split = std::min(a.n_split, std::min(lg::kDecodeMaxSplit, mg * std::min(lg::kDecodeMaxGroups, mg)));
-    a.chunk = std::max(1, a.n_tiles / (a.n_split * 48));
+    // Few tiles per CTA (short contexts, one KV head per GPU): static contiguous chunks of equal size
+    // cover every tile; a CTA then requests its whole chunk (up to the ring's depth) before the
+    // previous kernel completes, and no CTA waits on a grab.  More tiles per CTA: a static first
+    // chunk, then dynamic grabs, single tiles up to ~48 tiles per CTA, larger chunks beyond.
+    const int per_cta = ceil_div(a.n_tiles, a.n_split);
+    if (per_cta <= lg::kDecodeStaticMaxTiles) {
+        a.chunk = std::max(1, per_cta);
+        a.n_split = ceil_div(a.n_tiles, a.chunk);
+        a.dynamic = 0;
+    } else {
+        a.chunk = std::max(1, a.n_tiles / (a.n_split * 48));
+        a.dynamic = a.n_split > 1;
+    }
+    a.n_split = std::max(1, a.n_split);
     a.chunk_ctr = h->counters + kvh;
     a.kv_dim = h->kv_dim;
     a.rope_pairs = h->rope_pairs;
@@ -877,6 +890,114 @@ int ligguf_cuda_attn_kv_upload(ligguf_attn* h, int layer, int pos0, int n, const
     note_cache_write(h, layer, 1, pos0);
     LG_CUDA(cudaMemcpy(static_cast<char*>(h->kc) + off, host_k, bytes, cudaMemcpyHostToDevice));
     LG_CUDA(cudaMemcpy(static_cast<char*>(h->vc) + off, host_v, bytes, cudaMemcpyHostToDevice));
+    return LIGGUF_ATTN_OK;
+}
+
+// ---------------------------------------------------------------------------- FAST state file
+// The engine's `model_file` header (fast/common.h:26-31): packed, 24 bytes.
+#pragma pack(push, 1)
+struct FastStateHeader {
+    int pos;
+    int n_context;
+    uint64_t kv_size;      // cache elements per tensor over all layers: n_layers * pos * kv_dim
+    uint64_t logits_size;  // fp32 logits after the cache
+};
+#pragma pack(pop)
+static_assert(sizeof(FastStateHeader) == 24, "model_file header is 24 packed bytes");
+
+static int state_handle_check(const ligguf_attn* h, const char* path) {
+    if (!h || !path) return fail(LIGGUF_ATTN_EINVAL, "null handle or path");
+    if (h->cfg.kv_type != LIGGUF_KV_F16)
+        return fail(LIGGUF_ATTN_EUNSUPPORTED, "the engine state file holds fp16 cache rows: needs kv_type F16");
+    if (h->kv_dim != h->kv_dim_full)
+        return fail(LIGGUF_ATTN_EUNSUPPORTED, "the engine state file holds every KV head: not a shard's handle");
+    return LIGGUF_ATTN_OK;
+}
+
+int ligguf_cuda_attn_state_save(ligguf_attn* h, const char* path, int pos, const float* logits, uint64_t n_logits) {
+    int rc = state_handle_check(h, path);
+    if (rc) return rc;
+    if (!logits || n_logits == 0 || pos < 1 || pos > h->cfg.n_context)  // fast/ligguf_fast_qk.cpp:268-271
+        return fail(LIGGUF_ATTN_EINVAL, "empty state (pos %d, %llu logits): nothing to save", pos,
+                    static_cast<unsigned long long>(n_logits));
+    DeviceGuard dg(h->cfg.device);
+    LG_CUDA(cudaStreamSynchronize(h->stream));
+    FILE* f = fopen(path, "wb");
+    if (!f) return fail(LIGGUF_ATTN_EINVAL, "cannot create %s", path);
+    FastStateHeader hdr{};
+    hdr.kv_size = uint64_t(h->cfg.n_layers) * uint64_t(pos) * uint64_t(h->kv_dim);
+    hdr.logits_size = n_logits;
+    hdr.n_context = h->cfg.n_context;
+    hdr.pos = pos;
+    bool ok = fwrite(&hdr, sizeof(hdr), 1, f) == 1;
+    const size_t bytes = size_t(pos) * h->kv_dim * sizeof(__half);  // one layer's rows [0, pos)
+    std::vector<uint8_t> buf(bytes);
+    for (int t = 0; t < 2 && ok; ++t) {  // K of every layer, then V (fast/ligguf_fast_qk.cpp:286-293)
+        const char* base = static_cast<const char*>(t ? h->vc : h->kc);
+        for (int l = 0; l < h->cfg.n_layers && ok; ++l) {
+            if (cudaMemcpy(buf.data(), base + size_t(l) * h->layer_elems * h->es, bytes, cudaMemcpyDeviceToHost) !=
+                cudaSuccess) {
+                (void)cudaGetLastError();
+                fclose(f);
+                return fail(LIGGUF_ATTN_ECUDA, "cache download for the state file failed");
+            }
+            ok = fwrite(buf.data(), bytes, 1, f) == 1;
+        }
+    }
+    ok = ok && fwrite(logits, n_logits * sizeof(float), 1, f) == 1;
+    ok = (fclose(f) == 0) && ok;
+    if (!ok) return fail(LIGGUF_ATTN_EINVAL, "writing %s failed", path);
+    return LIGGUF_ATTN_OK;
+}
+
+int ligguf_cuda_attn_state_load(ligguf_attn* h, const char* path, int* pos_out, int* n_context_out, float* logits,
+                                uint64_t n_logits) {
+    int rc = state_handle_check(h, path);
+    if (rc) return rc;
+    if (!logits || n_logits == 0) return fail(LIGGUF_ATTN_EINVAL, "no logits buffer");
+    FILE* f = fopen(path, "rb");
+    if (!f) return fail(LIGGUF_ATTN_EINVAL, "cannot read %s", path);
+    auto bad = [&](const char* why) {
+        fclose(f);
+        return fail(LIGGUF_ATTN_EINVAL, "%s: %s", path, why);
+    };
+    FastStateHeader hdr{};
+    if (fread(&hdr, sizeof(hdr), 1, f) != 1) return bad("no header");
+    // The reference's checks (fast/ligguf_fast_qk.cpp:228-233,251), then this handle's room.
+    if (!hdr.kv_size || !hdr.logits_size || !hdr.pos) return bad("empty state");
+    if (hdr.pos < 0 || hdr.pos > h->cfg.n_context) return bad("pos beyond this handle's n_context");
+    const uint64_t lsz = uint64_t(hdr.pos) * uint64_t(h->kv_dim);
+    if (hdr.kv_size != uint64_t(h->cfg.n_layers) * lsz) return bad("cache size does not match this model");
+    if (hdr.logits_size != n_logits) return bad("logits size does not match");
+    // The whole file is checked before anything is touched: a short file changes nothing.
+    const uint64_t want = sizeof(hdr) + 2 * hdr.kv_size * sizeof(__half) + hdr.logits_size * sizeof(float);
+    if (fseek(f, 0, SEEK_END) != 0) return bad("cannot seek");
+    const long have = ftell(f);
+    if (have < 0 || uint64_t(have) != want) return bad("file size does not match its header");
+    if (fseek(f, long(sizeof(hdr)), SEEK_SET) != 0) return bad("cannot seek");
+    DeviceGuard dg(h->cfg.device);
+    LG_CUDA(cudaStreamSynchronize(h->stream));
+    const size_t bytes = size_t(lsz) * sizeof(__half);
+    std::vector<uint8_t> buf(bytes);
+    for (int t = 0; t < 2; ++t) {  // fast/ligguf_fast_qk.cpp:238-248
+        char* base = static_cast<char*>(t ? h->vc : h->kc);
+        for (int l = 0; l < h->cfg.n_layers; ++l) {
+            if (fread(buf.data(), bytes, 1, f) != 1) return bad("short read of the cache");
+            if (cudaMemcpy(base + size_t(l) * h->layer_elems * h->es, buf.data(), bytes, cudaMemcpyHostToDevice) !=
+                cudaSuccess) {
+                (void)cudaGetLastError();
+                fclose(f);
+                return fail(LIGGUF_ATTN_ECUDA, "cache upload from the state file failed");
+            }
+        }
+    }
+    std::vector<float> lg(n_logits);
+    if (fread(lg.data(), n_logits * sizeof(float), 1, f) != 1) return bad("short read of the logits");
+    fclose(f);
+    note_cache_write(h, 0, h->cfg.n_layers, 0);
+    std::memcpy(logits, lg.data(), n_logits * sizeof(float));
+    if (pos_out) *pos_out = hdr.pos;
+    if (n_context_out) *n_context_out = hdr.n_context;
     return LIGGUF_ATTN_OK;
 }
 

@@ -12,7 +12,9 @@
 // Grid (n_split, kv_headn), one resident wave.  CTA (split, g) works on KV head g: it starts on a
 // static chunk of 16 KB tiles of cached positions [0, pos) and then takes further chunks of the
 // head from an atomic counter (so CTAs that stream faster take more tiles; one static wave left SMs
-// idle for a fifth of the kernel).  It computes all nrep q heads of the group, so each K/V byte is
+// idle for a fifth of the kernel at 32K).  When each CTA has only a few tiles (short contexts, or
+// one KV head per GPU), the static chunks cover everything instead: no grabs, and the whole chunk
+// (up to the ring's depth) is requested before the previous kernel in the stream has finished.  It computes all nrep q heads of the group, so each K/V byte is
 // read from HBM once.  Warp 8 is the producer: one lane grabs chunks and streams their K and V tiles
 // with TMA into a 3-stage shared-memory ring, publishing each stage's tile index in shared memory.  Warps 0..7 consume: scores (each lane dots 16 B of a row with
 // the nrep q vectors, a transposed butterfly reduces nrep*4 dot products with one shuffle per
@@ -35,6 +37,7 @@ constexpr int kDecodeStages = 3;
 constexpr int kDecodeTileBytes = 16384;
 constexpr int kDecodeMaxSplit = 1024;
 constexpr int kDecodeMaxGroups = 32;   // first-level merge groups per KV head (the host bounds n_split)
+constexpr int kDecodeStaticMaxTiles = 8;  // up to this many tiles per CTA: static chunks, no grabs
 
 // One partial (o[NREP][D], m[NREP], l[NREP]) in floats, padded to 16 bytes so that a run of
 // partials can be fetched with one bulk copy.
@@ -74,6 +77,7 @@ struct DecodeArgs {
     int n_tiles;        // tiles covering [0, pos)
     int chunk;          // tiles per grab: CTA `split` starts with tiles [split*chunk, +chunk), then takes
                         // further chunks from chunk_ctr[g] (first dynamic chunk = n_split*chunk)
+    int dynamic;        // 0: the static chunks cover all tiles (n_split*chunk >= n_tiles), no grabs
     int* chunk_ctr;     // = counters + kv_headn
     int n_split;
     int kv_dim;
@@ -505,11 +509,11 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
             bool first = true;
             while (!fail && base < a.n_tiles) {
                 const int lim = min(base + a.chunk, a.n_tiles);
-                int next = lim;
+                int next = a.dynamic ? lim : a.n_tiles;
                 int t = base;
                 if (first && t0 > base) {  // part of the first chunk is already on its way
                     t = t0;
-                    if (a.n_split > 1) next = first_dyn + atomicAdd(&a.chunk_ctr[g], a.chunk);
+                    if (a.dynamic) next = first_dyn + atomicAdd(&a.chunk_ctr[g], a.chunk);
                 }
                 first = false;
                 for (; t < lim; ++t, ++it) {
@@ -524,7 +528,7 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
                     issue(t, s);
                     // Fetch the next chunk once this chunk's first copy is on its way: the grab's
                     // latency overlaps the remaining waits and copies instead of delaying them.
-                    if (t == base && a.n_split > 1) next = first_dyn + atomicAdd(&a.chunk_ctr[g], a.chunk);
+                    if (t == base && a.dynamic) next = first_dyn + atomicAdd(&a.chunk_ctr[g], a.chunk);
                 }
                 base = next;
             }

@@ -199,3 +199,52 @@ extern "C" int rf_set_threads(int n)
     if (n > 0) omp_set_num_threads(n);
     return omp_get_max_threads();
 }
+
+/* ---- the QKV projection (matmul3, lil_math.cpp:827-899) and its activation quantizers ------- */
+/* quantize_q8_K (lil_math.cpp:352-385): n/256 blocks {float d; int8 qs[256]; int16 bsums[16]},
+ * 292 bytes each, written to `out` in the struct's layout. */
+extern "C" void rf_quantize_q8_K(const float* x, int n, void* out)
+{
+    ftensor xv(x, x + n);
+    ktensor y(n / QK_K);
+    quantize_q8_K(y, xv);
+    memcpy(out, y.data(), y.size() * sizeof(block_q8_K));
+}
+/* quantize_q8_0 (lil_math.cpp:329-350): n/32 blocks {fp16 d; int8 qs[32]}, 34 bytes each. */
+extern "C" void rf_quantize_q8_0(const float* x, int n, void* out)
+{
+    ftensor xv(x, x + n);
+    qtensor y(n / QK8_0);
+    quantize_q8_0(y, xv);
+    memcpy(out, y.data(), y.size() * sizeof(block_q8_0));
+}
+/* The engine's QKV step (fast/ligguf_fast_qk.cpp:39-40): quantize_q8_K of the normed activation,
+ * then matmul3 over three weight matrices of GGUF type t0..t2 (rows of rsz0..2 bytes). */
+extern "C" void rf_matmul3(float* out0, float* out1, float* out2, const float* x, int n, int t0, const void* w0,
+                           int rsz0, int d0, int t1, const void* w1, int rsz1, int d1, int t2, const void* w2,
+                           int rsz2, int d2)
+{
+    rf_init();
+    ftensor xv(x, x + n), o0(d0), o1(d1), o2(d2);
+    ktensor xq(n / QK_K > 0 ? n / QK_K : 1);
+    if (n % QK_K == 0) quantize_q8_K(xq, xv);
+    wtensor a = {(uint8_t*)w0, (gguf_type)t0, (uint32_t)rsz0};
+    wtensor b = {(uint8_t*)w1, (gguf_type)t1, (uint32_t)rsz1};
+    wtensor c = {(uint8_t*)w2, (gguf_type)t2, (uint32_t)rsz2};
+    matmul3(o0, o1, o2, &xv, &xq, NULL, a, b, c, n, d0, d1, d2);
+    memcpy(out0, o0.data(), d0 * sizeof(float));
+    memcpy(out1, o1.data(), d1 * sizeof(float));
+    memcpy(out2, o2.data(), d2 * sizeof(float));
+}
+/* matmul (lil_math.cpp) over one matrix: the attn_output projection of the block
+ * (fast/ligguf_fast_qk.cpp:108-109). */
+extern "C" void rf_matmul(float* out, const float* x, int n, int t, const void* w, int rsz, int d)
+{
+    rf_init();
+    ftensor xv(x, x + n), o(d);
+    ktensor xq(n / QK_K > 0 ? n / QK_K : 1);
+    if (n % QK_K == 0) quantize_q8_K(xq, xv);
+    wtensor a = {(uint8_t*)w, (gguf_type)t, (uint32_t)rsz};
+    matmul(o, &xv, &xq, NULL, a, n, d);
+    memcpy(out, o.data(), d * sizeof(float));
+}
