@@ -620,6 +620,54 @@ def extra_bert(peaks, mode):
     return r
 
 
+def extra_qkv(peaks, types, n_distinct: int = 12, n_tok: int = 1):
+    """The Qwen3-8B QKV projection (x [4096] -> q [4096], k [1024], v [1024];
+    fast/ligguf_fast_qk.cpp:39-40) with weights of the given GGUF types.  n_tok = 1: one decode token,
+    36 launches per step (one per layer) over `n_distinct` synthetic weight sets used in turn (more
+    bytes than L2 holds), CUDA-graph replay.  n_tok > 1: the batched prompt form, one call per layer
+    for n_tok tokens (the weights stream once per group of up to 8 tokens).  GB/s counts the weight
+    bytes of one pass per layer; the batched form also reports the int8 MAC rate."""
+    import numpy as np
+    import torch
+    from ligguf_b200.qmat import QT, QuantMatrix, matmul3_async, matmul3_batch_async, row_bytes, synthetic_rows
+    n, dims, L = 4096, (4096, 1024, 1024), 36
+    dev = torch.device("cuda", torch.cuda.current_device())
+    layers = [[QuantMatrix(QT[t], n, synthetic_rows(QT[t], n, d, seed=97 * i + j), dev.index)
+               for j, (t, d) in enumerate(zip(types, dims))] for i in range(n_distinct)]
+    nx = L if n_tok == 1 else 1  # the prompt form reuses one [n_tok][n] activation for every layer
+    x = torch.from_numpy(np.random.default_rng(1).standard_normal((nx, n_tok, n)).astype(np.float32)).to(dev)
+    outs = [torch.empty(nx, n_tok, d, device=dev) for d in dims]
+
+    def step():
+        for l in range(L):
+            w = layers[l % n_distinct]
+            if n_tok == 1:
+                matmul3_async(w[0], w[1], w[2], x[l, 0], outs[0][l, 0], outs[1][l, 0], outs[2][l, 0])
+            else:
+                matmul3_batch_async(w[0], w[1], w[2], x[0], n_tok, outs[0][0], outs[1][0], outs[2][0])
+    step()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    ms = _time_ms(g.replay, 30 if n_tok == 1 else 3)
+    del g
+    for ws in layers:
+        for m in ws:
+            m.close()
+    wbytes = sum(row_bytes(QT[t], n) * d for t, d in zip(types, dims))
+    r = {"types": list(types), "tokens": n_tok, "us_per_layer": ms * 1e3 / L, "weight_bytes_per_layer": wbytes}
+    if n_tok == 1:
+        gbs = wbytes * L / (ms * 1e-3) / 1e9
+        r.update(hbm_gbs=gbs, frac_of_hbm=gbs / peaks["hbm_gbs"])
+    else:
+        r.update(tokens_s=n_tok * L / (ms * 1e-3) / L, int8_tmacs=n_tok * n * sum(dims) * L / (ms * 1e-3) / 1e12)
+    r["note"] = (f"36 per-layer launches over {n_distinct} distinct synthetic weight sets "
+                 f"({n_distinct * wbytes / 1e6:.0f} MB, more than L2), CUDA-graph replay; x quantized on the device "
+                 f"as the reference does")
+    return r
+
+
 def run_extras(peaks):
     extra = {}
     from ligguf_b200.workloads import QWEN3_DECODE_4K, TINYLLAMA_DECODE
@@ -628,7 +676,10 @@ def run_extras(peaks):
             ("qwen3_8b_prefill_2048_simt_fp32", lambda: extra_prefill(peaks, 0)),
             ("qwen3_8b_prefill_2048_tc_bf16", lambda: extra_prefill(peaks, 1)),
             ("bert_base_attn_simt_fp32", lambda: extra_bert(peaks, 0)),
-            ("bert_base_attn_tc_bf16", lambda: extra_bert(peaks, 1))]
+            ("bert_base_attn_tc_bf16", lambda: extra_bert(peaks, 1)),
+            ("qwen3_8b_qkv_q8_0", lambda: extra_qkv(peaks, ("Q8_0", "Q8_0", "Q8_0"))),
+            ("qwen3_8b_qkv_q4_k_m", lambda: extra_qkv(peaks, ("Q4_K", "Q4_K", "Q6_K"))),
+            ("qwen3_8b_qkv_q4_k_m_prompt_2048", lambda: extra_qkv(peaks, ("Q4_K", "Q4_K", "Q6_K"), n_tok=2048))]
     for name, fn in jobs:
         try:
             extra[name] = fn()

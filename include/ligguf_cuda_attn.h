@@ -222,6 +222,49 @@ int ligguf_cuda_bert_attn_tc_noalloc(int n_heads, int head_dim, int batch, int m
  * bounded wait in one of them gave up since the last call began, else 0.  Allocates nothing. */
 int ligguf_cuda_bert_attn_tc_noalloc_status(void* stream);
 
+/* ---- quantized projections (the QKV step of the forward pass) ---------------------------- */
+/* Replaces quantize_q8_K + matmul3 at fast/ligguf_fast_qk.cpp:39-40 (fast/lil_math.cpp:352-385,
+ * 827-899), and matmul / matmul2 (fast/lil_math.cpp:757-825) with one or two matrices: out[r] =
+ * dot(row r of W, x) for weights in their GGUF block layout, with the activation quantized on the
+ * device exactly as the reference quantizes it (Q8_K for the K-quants, Q8_0 for Q8_0 / Q1_0 / Q1_G,
+ * fp32 for F32 / F16).  The integer block dot products and scale terms are exact; only the fp32 sum
+ * over blocks runs in another order than the reference's AVX2 loops.
+ * Weight types (gguf_type, fast/lil_gguf.h:26-44): 0 F32, 1 F16, 8 Q8_0, 10 Q2_K, 11 Q3_K, 12 Q4_K,
+ * 13 Q5_K, 14 Q6_K, 40 Q1_0, 41 Q1_G.  Widths: a multiple of 32 (256 for K-quants), at most 16384. */
+typedef struct ligguf_qmat ligguf_qmat;
+/* Bytes of one row of `n` elements of `type` (the reference's row_size), 0 if not a whole number of
+ * blocks or an unknown type. */
+size_t ligguf_cuda_qmat_row_bytes(int type, int n);
+/* Copies a d x n weight matrix (d rows of ligguf_cuda_qmat_row_bytes(type, n) bytes, the GGUF tensor
+ * as the engine mmaps it: wtensor::ptr / rsz, fast/lil_gguf.h:126-130) to HBM once. `rows` is host
+ * memory, or device memory when rows_on_device is set. */
+int ligguf_cuda_qmat_init(int type, int n, int d, const void* rows, int rows_on_device, int device,
+                          ligguf_qmat** out);
+int ligguf_cuda_qmat_free(ligguf_qmat* w);
+/* matmul3 (w1, w2 non-NULL), matmul2 (w2 NULL) or matmul (w1, w2 NULL): device pointers, x [n],
+ * out_i [d_i], enqueued on `stream` (a cudaStream_t; NULL = legacy default).  All matrices share n
+ * and the device. */
+int ligguf_cuda_matmul3_async(const ligguf_qmat* w0, const ligguf_qmat* w1, const ligguf_qmat* w2,
+                              const float* d_x, float* d_out0, float* d_out1, float* d_out2,
+                              void* stream);
+/* Same with host pointers; returns when the outputs are written. */
+int ligguf_cuda_matmul3(const ligguf_qmat* w0, const ligguf_qmat* w1, const ligguf_qmat* w2,
+                        const float* x, float* out0, float* out1, float* out2);
+/* Batched prompt projections: n_tok rows x [n_tok][n] -> out_i [n_tok][d_i], equal to n_tok calls of
+ * the single-token form (the prompt loop of feed_text runs matmul3 once per token,
+ * fast/ligguf_fast_qk.cpp:340-356); the weights stream from HBM once per group of up to 8 tokens. */
+int ligguf_cuda_matmul3_batch_async(const ligguf_qmat* w0, const ligguf_qmat* w1, const ligguf_qmat* w2,
+                                    const float* d_x, int n_tok, float* d_out0, float* d_out1,
+                                    float* d_out2, void* stream);
+int ligguf_cuda_matmul3_batch(const ligguf_qmat* w0, const ligguf_qmat* w1, const ligguf_qmat* w2,
+                              const float* x, int n_tok, float* out0, float* out1, float* out2);
+/* The activation quantizers on their own (device pointers), writing the reference's block layouts:
+ * quantize_q8_K -> n/256 blocks {float d; int8 qs[256]; int16 bsums[16]} (292 bytes each), and
+ * quantize_q8_0 -> n/32 blocks {fp16 d; int8 qs[32]} (34 bytes each); bit-identical to the
+ * reference's results. */
+int ligguf_cuda_quantize_q8_K_async(const float* d_x, int n, void* d_blocks, void* stream);
+int ligguf_cuda_quantize_q8_0_async(const float* d_x, int n, void* d_blocks, void* stream);
+
 /* ---- seeded synthetic inputs ------------------------------------------------------------- */
 /* Tensor ids of the synthetic generator's streams. */
 #define LIGGUF_SYNTH_K 1

@@ -75,6 +75,15 @@ _PROTOS = {
     "ligguf_cuda_bert_attn_async": [_vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _i, _vp],
     "ligguf_cuda_bert_attn_tc_noalloc": [_i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp],
     "ligguf_cuda_bert_attn_tc_noalloc_status": [_vp],
+    "ligguf_cuda_qmat_row_bytes": [_i, _i],
+    "ligguf_cuda_qmat_init": [_i, _i, _i, _vp, _i, _i, ctypes.POINTER(_vp)],
+    "ligguf_cuda_qmat_free": [_vp],
+    "ligguf_cuda_matmul3_async": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
+    "ligguf_cuda_matmul3": [_vp, _vp, _vp, _vp, _vp, _vp, _vp],
+    "ligguf_cuda_matmul3_batch_async": [_vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp],
+    "ligguf_cuda_matmul3_batch": [_vp, _vp, _vp, _vp, _i, _vp, _vp, _vp],
+    "ligguf_cuda_quantize_q8_K_async": [_vp, _i, _vp, _vp],
+    "ligguf_cuda_quantize_q8_0_async": [_vp, _i, _vp, _vp],
     "ligguf_cuda_synth_fill": [_vp, _i, _sz, _u64, _u64, _u64, _f, _f, _vp],
 }
 
@@ -93,7 +102,8 @@ def load(path: str = LIB_PATH):
     for name, argtypes in _PROTOS.items():
         fn = getattr(lib, name)
         fn.argtypes = argtypes
-        fn.restype = _cp if name in ("ligguf_cuda_attn_strerror", "ligguf_cuda_attn_last_error") else _i
+        fn.restype = (_cp if name in ("ligguf_cuda_attn_strerror", "ligguf_cuda_attn_last_error")
+                      else _sz if name == "ligguf_cuda_qmat_row_bytes" else _i)
     _lib = lib
     return lib
 

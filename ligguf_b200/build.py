@@ -15,7 +15,7 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 LIB_PATH = os.path.join(PKG, "libligguf_cuda_attn.so")
-SOURCES = [os.path.join(CSRC, "attn_api.cu")]
+SOURCES = [os.path.join(CSRC, "attn_api.cu"), os.path.join(CSRC, "qmat_api.cu")]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-lineinfo", "-O3", "-std=c++17",

@@ -14,15 +14,16 @@
 #include <vector>
 
 #include "ligguf_cuda_attn.h"
+#include "api_util.h"
 #include "common.cuh"
 #include "decode.cuh"
 #include "flash_simt.cuh"
 #include "flash_tc.cuh"
 
+namespace lgapi {
 namespace {
-
 thread_local std::string g_last_error;
-
+}
 int fail(int code, const char* fmt, ...) {
     char buf[512];
     va_list ap;
@@ -32,27 +33,12 @@ int fail(int code, const char* fmt, ...) {
     g_last_error = buf;
     return code;
 }
+const char* last_error() { return g_last_error.c_str(); }
+}  // namespace lgapi
 
-#define LG_CUDA(expr)                                                                          \
-    do {                                                                                       \
-        const cudaError_t e_ = (expr);                                                         \
-        if (e_ != cudaSuccess) {                                                               \
-            (void)cudaGetLastError(); /* do not leave it pending for unrelated calls */       \
-            return fail(LIGGUF_ATTN_ECUDA, "%s failed: %s (%s:%d)", #expr,                     \
-                        cudaGetErrorString(e_), __FILE__, __LINE__);                           \
-        }                                                                                      \
-    } while (0)
-
-struct DeviceGuard {
-    int prev = -1;
-    bool switched = false;
-    explicit DeviceGuard(int dev) {
-        if (cudaGetDevice(&prev) == cudaSuccess && prev != dev) switched = cudaSetDevice(dev) == cudaSuccess;
-    }
-    ~DeviceGuard() {
-        if (switched) cudaSetDevice(prev);
-    }
-};
+namespace {
+using lgapi::DeviceGuard;
+using lgapi::fail;
 
 inline int ceil_div(long long a, long long b) { return static_cast<int>((a + b - 1) / b); }
 
@@ -666,7 +652,7 @@ const char* ligguf_cuda_attn_strerror(int status) {
     }
 }
 
-const char* ligguf_cuda_attn_last_error(void) { return g_last_error.c_str(); }
+const char* ligguf_cuda_attn_last_error(void) { return lgapi::last_error(); }
 
 int ligguf_cuda_attn_free(ligguf_attn* h) {
     if (!h) return LIGGUF_ATTN_OK;

@@ -1,0 +1,311 @@
+// qmat_api.cu - the C ABI of the quantized projections (include/ligguf_cuda_attn.h, "quantized
+// projections"): device-resident GGUF weight matrices, matmul / matmul2 / matmul3 on them for one
+// token or a batch of prompt tokens, and the activation quantizers.  Nothing here falls back to the
+// CPU.
+#include <algorithm>
+#include <cstring>
+#include <numeric>
+
+#include "api_util.h"
+#include "common.cuh"
+#include "ligguf_cuda_attn.h"
+#include "qmatvec.cuh"
+
+using lgapi::DeviceGuard;
+using lgapi::fail;
+
+struct ligguf_qmat {
+    int type = 0, n = 0, d = 0, device = 0, rb = 0;
+    uint8_t* w = nullptr;      // d rows of rb bytes, allocation padded to a 16-byte multiple
+    int* h_err = nullptr;      // mapped pinned error word of the kernels that read this matrix
+    int* d_err = nullptr;
+    float* stage = nullptr;    // device staging of the host-pointer calls: x and the outputs
+    size_t stage_floats = 0;
+    cudaStream_t stream = nullptr;
+};
+
+namespace {
+
+constexpr int kSmemLimit = 226 * 1024;
+
+int row_bytes(int type, int n) {
+    const int be = lg::qt_block_elems(type), bb = lg::qt_block_bytes(type);
+    if (!be || n % be) return 0;
+    return n / be * bb;
+}
+
+// Rows per ring stage: as many as fit kQmvStageMax, a multiple of the consumer warps when that many
+// fit, and always a multiple of the rows that make the stage a whole number of 16-byte units (a
+// bulk copy must start on a 16-byte boundary and move 16-byte multiples).
+int tile_rows(int rb) {
+    const int align = 16 / std::gcd(rb, 16);
+    int r = lg::kQmvStageMax / rb;
+    if (r >= lg::kQmvWarps) {
+        const int step = std::lcm(align, lg::kQmvWarps);
+        r = r / step * step;
+        if (r == 0) r = lg::kQmvStageMax / rb / align * align;
+    } else {
+        r = r / align * align;
+    }
+    return r;
+}
+
+// Shared-memory layout of the activations of `tokens` tokens; returns the dynamic shared memory.
+int act_layout(lg::QmvArgs& a, int tokens) {
+    auto up = [](int v, int m) { return (v + m - 1) / m * m; };
+    int off = 0;
+    lg::QmvAct& t = a.act;
+    t = {};
+    if (a.need_k) {
+        t.off_qk = off;
+        off = up(off + a.n, 16);
+        t.off_dk = off;
+        off = up(off + a.n / 256 * 4, 16);
+        t.off_bs = off;
+        off = up(off + a.n / 16 * 4, 16);
+    }
+    if (a.need_0) {
+        t.off_q0 = off;
+        off = up(off + a.n, 16);
+        t.off_d0 = off;
+        off = up(off + a.n / 32 * 4, 16);
+    }
+    if (a.need_f) {
+        t.off_xf = off;
+        off = up(off + a.n * 4, 16);
+    }
+    t.tok_bytes = off;
+    t.bytes = up(off * tokens, 1024);
+    return t.bytes + lg::kQmvStages * lg::kQmvStageMax;
+}
+
+template <int T>
+int launch_qmv(lg::QmvArgs& a, int smem, int dev, cudaStream_t st) {
+    auto kern = lg::qmv_kernel<T>;
+    static int attr_bytes[64] = {};  // dynamic shared memory allowed so far on each device
+    if (dev < 0 || dev >= 64 || attr_bytes[dev] < smem) {
+        LG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        if (dev >= 0 && dev < 64) attr_bytes[dev] = smem;
+    }
+    int sms = 0;
+    LG_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(std::max(1, std::min(a.ntiles, sms)), 1, 1);
+    lc.blockDim = dim3(lg::kQmvThreads, 1, 1);
+    lc.dynamicSmemBytes = smem;
+    lc.stream = st;
+    // Programmatic dependent launch: the weights stream while the previous kernel finishes; the
+    // consumers wait for it (griddepcontrol.wait) before reading x.
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    LG_CUDA(cudaLaunchKernelEx(&lc, kern, a));
+    return LIGGUF_ATTN_OK;
+}
+
+// n_tok x rows of x (row stride x_stride) through up to three matrices; out_i row t at
+// outs[i] + t * out_strides[i].  One launch per group of up to kQmvMaxTokens tokens (fewer when
+// their activations would not fit shared memory next to the weight ring).
+int matmul_enqueue(const ligguf_qmat* const* ws, float* const* outs, const long long* out_strides, int nmat,
+                   const float* d_x, long long x_stride, int n_tok, cudaStream_t st) {
+    lg::QmvArgs a = {};
+    a.n = ws[0]->n;
+    a.err = ws[0]->d_err;
+    a.x_stride = x_stride;
+    int tiles = 0;
+    for (int i = 0; i < nmat; ++i) {
+        const ligguf_qmat* w = ws[i];
+        if (w->n != a.n) return fail(LIGGUF_ATTN_EINVAL, "matrices of one call have different input widths");
+        if (w->device != ws[0]->device) return fail(LIGGUF_ATTN_EINVAL, "matrices of one call are on different devices");
+        if (!outs[i]) return fail(LIGGUF_ATTN_EINVAL, "null output");
+        lg::QmvMat& m = a.m[a.nmat++];
+        m.w = w->w;
+        m.out = outs[i];
+        m.out_stride = out_strides[i];
+        m.type = w->type;
+        m.rows = w->d;
+        m.rb = w->rb;
+        m.tile_rows = tile_rows(w->rb);
+        m.tile0 = tiles;
+        m.ntiles = (w->d + m.tile_rows - 1) / m.tile_rows;
+        tiles += m.ntiles;
+        a.need_k |= lg::qt_uses_q8k(w->type);
+        a.need_0 |= lg::qt_uses_q80(w->type);
+        a.need_f |= lg::qt_uses_f32(w->type);
+    }
+    a.ntiles = tiles;
+    int T = lg::kQmvMaxTokens;
+    while (T > 1 && (T / 2 >= n_tok || act_layout(a, T) > kSmemLimit)) T /= 2;
+    const int smem = act_layout(a, T);
+    if (smem > kSmemLimit)
+        return fail(LIGGUF_ATTN_EUNSUPPORTED, "input width %d needs %d bytes of shared memory with these types",
+                    a.n, smem);
+    const int dev = ws[0]->device;
+    for (int t0 = 0; t0 < n_tok; t0 += T) {
+        a.x = d_x + t0 * x_stride;
+        a.n_tok = std::min(T, n_tok - t0);
+        for (int i = 0; i < nmat; ++i) a.m[i].out = outs[i] + t0 * out_strides[i];
+        int rc;
+        switch (T) {
+            case 8: rc = launch_qmv<8>(a, smem, dev, st); break;
+            case 4: rc = launch_qmv<4>(a, smem, dev, st); break;
+            case 2: rc = launch_qmv<2>(a, smem, dev, st); break;
+            default: rc = launch_qmv<1>(a, smem, dev, st); break;
+        }
+        if (rc) return rc;
+    }
+    return LIGGUF_ATTN_OK;
+}
+
+int check_qmat_err(const ligguf_qmat* w) {
+    if (w->h_err && *reinterpret_cast<volatile int*>(w->h_err)) {
+        const int code = *w->h_err;
+        *reinterpret_cast<volatile int*>(w->h_err) = 0;
+        return fail(LIGGUF_ATTN_ETIMEDOUT, "a bounded in-kernel wait of the projection gave up (code %d)", code);
+    }
+    return LIGGUF_ATTN_OK;
+}
+
+int batch_args(const ligguf_qmat* w0, const ligguf_qmat* w1, const ligguf_qmat* w2, int n_tok) {
+    if (!w0) return fail(LIGGUF_ATTN_EINVAL, "null w0");
+    if (!w1 && w2) return fail(LIGGUF_ATTN_EINVAL, "w2 without w1");
+    if (n_tok < 1) return fail(LIGGUF_ATTN_EINVAL, "n_tok %d", n_tok);
+    return LIGGUF_ATTN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t ligguf_cuda_qmat_row_bytes(int type, int n) { return n > 0 ? size_t(row_bytes(type, n)) : 0; }
+
+int ligguf_cuda_qmat_free(ligguf_qmat* w) {
+    if (!w) return LIGGUF_ATTN_OK;
+    DeviceGuard dg(w->device);
+    if (w->stream) cudaStreamSynchronize(w->stream);
+    if (w->w) cudaFree(w->w);
+    if (w->stage) cudaFree(w->stage);
+    if (w->h_err) cudaFreeHost(w->h_err);
+    if (w->stream) cudaStreamDestroy(w->stream);
+    delete w;
+    return LIGGUF_ATTN_OK;
+}
+
+int ligguf_cuda_qmat_init(int type, int n, int d, const void* rows, int rows_on_device, int device,
+                          ligguf_qmat** out) {
+    if (!out || !rows) return fail(LIGGUF_ATTN_EINVAL, "null argument");
+    *out = nullptr;
+    if (n < 1 || d < 1) return fail(LIGGUF_ATTN_EINVAL, "non-positive size %d x %d", d, n);
+    if (!lg::qt_block_bytes(type)) return fail(LIGGUF_ATTN_EUNSUPPORTED, "weight type %d has no kernel", type);
+    const int rb = row_bytes(type, n);
+    if (!rb || n % 32) return fail(LIGGUF_ATTN_EINVAL, "width %d is not a whole number of units of 32 of type %d", n, type);
+    if (lg::qt_uses_q8k(type) && n % 256) return fail(LIGGUF_ATTN_EINVAL, "K-quant width %d is not a multiple of 256", n);
+    if (n > lg::kQmvMaxN) return fail(LIGGUF_ATTN_EUNSUPPORTED, "width %d beyond %d", n, lg::kQmvMaxN);
+    const int tr = tile_rows(rb);
+    if (tr < 1 || size_t(tr) * rb > size_t(lg::kQmvStageMax))
+        return fail(LIGGUF_ATTN_EUNSUPPORTED, "rows of %d bytes do not fit a %d-byte stage", rb, lg::kQmvStageMax);
+    int ndev = 0;
+    LG_CUDA(cudaGetDeviceCount(&ndev));
+    if (device < 0 || device >= ndev) return fail(LIGGUF_ATTN_EINVAL, "device %d of %d", device, ndev);
+    DeviceGuard dg(device);
+    ligguf_qmat* w = new ligguf_qmat();
+    w->type = type;
+    w->n = n;
+    w->d = d;
+    w->rb = rb;
+    w->device = device;
+    const size_t bytes = size_t(d) * rb;
+    const size_t alloc = (bytes + 15) / 16 * 16 + 16;
+    if (cudaMalloc(&w->w, alloc) != cudaSuccess || cudaMemset(w->w, 0, alloc) != cudaSuccess ||
+        cudaMemcpy(w->w, rows, bytes, rows_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice) !=
+            cudaSuccess ||
+        cudaHostAlloc(&w->h_err, 64, cudaHostAllocMapped) != cudaSuccess ||
+        cudaHostGetDevicePointer(reinterpret_cast<void**>(&w->d_err), w->h_err, 0) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&w->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        (void)cudaGetLastError();
+        ligguf_cuda_qmat_free(w);
+        return fail(LIGGUF_ATTN_ENOMEM, "weight matrix of %zu bytes", bytes);
+    }
+    *w->h_err = 0;
+    *out = w;
+    return LIGGUF_ATTN_OK;
+}
+
+int ligguf_cuda_matmul3_batch_async(const ligguf_qmat* w0, const ligguf_qmat* w1, const ligguf_qmat* w2,
+                                    const float* d_x, int n_tok, float* d_out0, float* d_out1, float* d_out2,
+                                    void* stream) {
+    int rc = batch_args(w0, w1, w2, n_tok);
+    if (rc) return rc;
+    if (!d_x) return fail(LIGGUF_ATTN_EINVAL, "null x");
+    const ligguf_qmat* ws[3] = {w0, w1, w2};
+    float* outs[3] = {d_out0, d_out1, d_out2};
+    const long long strides[3] = {w0->d, w1 ? w1->d : 0, w2 ? w2->d : 0};
+    const int nmat = w2 ? 3 : (w1 ? 2 : 1);
+    DeviceGuard dg(w0->device);
+    return matmul_enqueue(ws, outs, strides, nmat, d_x, w0->n, n_tok, static_cast<cudaStream_t>(stream));
+}
+
+int ligguf_cuda_matmul3_async(const ligguf_qmat* w0, const ligguf_qmat* w1, const ligguf_qmat* w2, const float* d_x,
+                              float* d_out0, float* d_out1, float* d_out2, void* stream) {
+    return ligguf_cuda_matmul3_batch_async(w0, w1, w2, d_x, 1, d_out0, d_out1, d_out2, stream);
+}
+
+int ligguf_cuda_matmul3_batch(const ligguf_qmat* w0, const ligguf_qmat* w1, const ligguf_qmat* w2, const float* x,
+                              int n_tok, float* out0, float* out1, float* out2) {
+    int rc = batch_args(w0, w1, w2, n_tok);
+    if (rc) return rc;
+    if (!x || !out0 || (w1 && !out1) || (w2 && !out2)) return fail(LIGGUF_ATTN_EINVAL, "null argument");
+    ligguf_qmat* s = const_cast<ligguf_qmat*>(w0);
+    DeviceGuard dg(s->device);
+    const size_t d0 = w0->d, d1 = w1 ? w1->d : 0, d2 = w2 ? w2->d : 0;
+    const size_t need = size_t(n_tok) * (w0->n + d0 + d1 + d2);
+    if (s->stage_floats < need) {
+        if (s->stage) cudaFree(s->stage);
+        s->stage = nullptr;
+        s->stage_floats = 0;
+        if (cudaMalloc(&s->stage, need * sizeof(float)) != cudaSuccess)
+            return fail(LIGGUF_ATTN_ENOMEM, "staging of %zu floats", need);
+        s->stage_floats = need;
+    }
+    float* dx = s->stage;
+    float* o0 = dx + size_t(n_tok) * w0->n;
+    float* o1 = o0 + size_t(n_tok) * d0;
+    float* o2 = o1 + size_t(n_tok) * d1;
+    LG_CUDA(cudaMemcpyAsync(dx, x, size_t(n_tok) * w0->n * sizeof(float), cudaMemcpyHostToDevice, s->stream));
+    rc = ligguf_cuda_matmul3_batch_async(w0, w1, w2, dx, n_tok, o0, w1 ? o1 : nullptr, w2 ? o2 : nullptr, s->stream);
+    if (rc) return rc;
+    LG_CUDA(cudaMemcpyAsync(out0, o0, size_t(n_tok) * d0 * sizeof(float), cudaMemcpyDeviceToHost, s->stream));
+    if (w1) LG_CUDA(cudaMemcpyAsync(out1, o1, size_t(n_tok) * d1 * sizeof(float), cudaMemcpyDeviceToHost, s->stream));
+    if (w2) LG_CUDA(cudaMemcpyAsync(out2, o2, size_t(n_tok) * d2 * sizeof(float), cudaMemcpyDeviceToHost, s->stream));
+    LG_CUDA(cudaStreamSynchronize(s->stream));
+    return check_qmat_err(w0);
+}
+
+int ligguf_cuda_matmul3(const ligguf_qmat* w0, const ligguf_qmat* w1, const ligguf_qmat* w2, const float* x,
+                        float* out0, float* out1, float* out2) {
+    return ligguf_cuda_matmul3_batch(w0, w1, w2, x, 1, out0, out1, out2);
+}
+
+int ligguf_cuda_quantize_q8_K_async(const float* d_x, int n, void* d_blocks, void* stream) {
+    if (!d_x || !d_blocks) return fail(LIGGUF_ATTN_EINVAL, "null argument");
+    if (n < 256 || n % 256) return fail(LIGGUF_ATTN_EINVAL, "n = %d is not a positive multiple of 256", n);
+    const int nb = n / 256;
+    lg::quantize_q8k_kernel<<<(nb + 7) / 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        d_x, nb, static_cast<uint8_t*>(d_blocks));
+    LG_CUDA(cudaGetLastError());
+    return LIGGUF_ATTN_OK;
+}
+
+int ligguf_cuda_quantize_q8_0_async(const float* d_x, int n, void* d_blocks, void* stream) {
+    if (!d_x || !d_blocks) return fail(LIGGUF_ATTN_EINVAL, "null argument");
+    if (n < 32 || n % 32) return fail(LIGGUF_ATTN_EINVAL, "n = %d is not a positive multiple of 32", n);
+    const int nb = n / 32;
+    lg::quantize_q80_kernel<<<(nb + 7) / 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        d_x, nb, static_cast<uint8_t*>(d_blocks));
+    LG_CUDA(cudaGetLastError());
+    return LIGGUF_ATTN_OK;
+}
+
+}  // extern "C"

@@ -91,6 +91,9 @@ def port_lib():
         lib.lo_kv_synth.argtypes = [_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
                                     _c_u64, _c_float]
         lib.lo_set_threads.argtypes = [_c_int]
+        lib.lo_quantize_q8_K.argtypes = [_vp, _c_int, _vp]
+        lib.lo_quantize_q8_0.argtypes = [_vp, _c_int, _vp]
+        lib.lo_matmul.argtypes = [_vp, _vp, _c_int, _c_int, _vp, _c_int, _c_int, _vp, _vp]
         _port = lib
     return _port
 
@@ -242,3 +245,65 @@ class Checker:
         if rc:
             raise ValueError(f"{self.p}bert_attn failed ({rc})")
         return out.reshape(batch, max_len, n_heads * head_dim)
+
+
+# ------------------------------------------------------------------ quantized projections ---------
+Q8K_BYTES, Q80_BYTES = 292, 34
+
+
+def quantize_q8_K(x, which: str = "port"):
+    """quantize_q8_K (fast/lil_math.cpp:352-385) of x (n % 256 == 0): n/256 blocks as raw bytes."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.zeros(x.size // 256 * Q8K_BYTES, dtype=np.uint8)
+    if which == "port":
+        port_lib().lo_quantize_q8_K(_ptr(x), x.size, _ptr(out))
+    else:
+        lib = ref_lib()
+        lib.rf_quantize_q8_K.argtypes = [_vp, _c_int, _vp]
+        lib.rf_quantize_q8_K(_ptr(x), x.size, _ptr(out))
+    return out
+
+
+def quantize_q8_0(x, which: str = "port"):
+    """quantize_q8_0 (fast/lil_math.cpp:329-350) of x (n % 32 == 0): n/32 blocks as raw bytes."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.zeros(x.size // 32 * Q80_BYTES, dtype=np.uint8)
+    if which == "port":
+        port_lib().lo_quantize_q8_0(_ptr(x), x.size, _ptr(out))
+    else:
+        lib = ref_lib()
+        lib.rf_quantize_q8_0.argtypes = [_vp, _c_int, _vp]
+        lib.rf_quantize_q8_0(_ptr(x), x.size, _ptr(out))
+    return out
+
+
+def matmul(w_type: int, w_rows, n: int, x, which: str = "port"):
+    """matmul (fast/lil_math.cpp:757-778): out[r] = row r of the GGUF weight rows `w_rows` ([d][rb]
+    uint8) against x, with x quantized as the engine does (Q8_K for K-quants, Q8_0 for Q8_0/Q1_*)."""
+    w = np.ascontiguousarray(w_rows, dtype=np.uint8)
+    d, rb = w.shape
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.zeros(d, dtype=np.float32)
+    if which == "port":
+        sk = np.zeros(max(1, n // 256) * Q8K_BYTES, dtype=np.uint8)
+        s0 = np.zeros(max(1, n // 32) * Q80_BYTES, dtype=np.uint8)
+        port_lib().lo_matmul(_ptr(out), _ptr(x), n, w_type, _ptr(w), rb, d, _ptr(sk), _ptr(s0))
+    else:
+        lib = ref_lib()
+        lib.rf_matmul.argtypes = [_vp, _vp, _c_int, _c_int, _vp, _c_int, _c_int]
+        lib.rf_matmul(_ptr(out), _ptr(x), n, w_type, _ptr(w), rb, d)
+    return out
+
+
+def matmul3(ws, n: int, x):
+    """The engine's QKV step (fast/ligguf_fast_qk.cpp:39-40) through the reference build:
+    quantize_q8_K, then matmul3 over ws = [(type, rows), (type, rows), (type, rows)]."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    (t0, w0), (t1, w1), (t2, w2) = [(t, np.ascontiguousarray(w, dtype=np.uint8)) for t, w in ws]
+    outs = [np.zeros(w.shape[0], dtype=np.float32) for w in (w0, w1, w2)]
+    lib = ref_lib()
+    lib.rf_matmul3.argtypes = [_vp, _vp, _vp, _vp, _c_int] + [_c_int, _vp, _c_int, _c_int] * 3
+    lib.rf_matmul3(_ptr(outs[0]), _ptr(outs[1]), _ptr(outs[2]), _ptr(x), n,
+                   t0, _ptr(w0), w0.shape[1], w0.shape[0], t1, _ptr(w1), w1.shape[1], w1.shape[0],
+                   t2, _ptr(w2), w2.shape[1], w2.shape[0])
+    return outs

@@ -314,3 +314,23 @@ def test_errors_are_reported_not_fatal(gpu):
         h.decode(1, 3, c["q"], c["k"], c["v"])  # layer out of range
     h.decode(0, 3, c["q"], c["k"], c["v"])  # still usable
     h.close()
+
+
+@pytest.mark.parametrize("H,Hk,D,pos,kv_headn,scale", [
+    (32, 4, 64, 512, 0, 0.125),      # TinyLlama-shaped: one tile per CTA
+    (32, 8, 128, 4096, 0, 1.0),      # 4K: static chunks of a few tiles
+    (32, 8, 128, 32768, 1, 1.0),     # one KV head at 32K (the 8-GPU shard): two-level merge
+    (16, 4, 128, 2000, 0, 3.0),      # peaked softmax: one split's maximum dominates the merge
+])
+def test_decode_short_streams(gpu, H, Hk, D, pos, kv_headn, scale):
+    """Few tiles per CTA: static equal chunks (no grabs), every chunk requested before the previous
+    kernel completes, then the merge of the splits' partials."""
+    port = orc.Checker("port")
+    c = cases.decode_case(H=H, Hk=Hk, D=D, n_ctx=pos + 64, theta=1e6, qk_norm=int(D == 128), pos=pos, seed=pos + H,
+                          scale=scale, layer=0, kv_head0=0, kv_headn=kv_headn)
+    h = make_handle(c, kv_head0=0, kv_headn=kv_headn)
+    for _ in range(2):  # twice: the tickets and counters must be back at zero after each call
+        out, _, _, _ = gpu_decode(c, h)
+        ref, _, _ = cases.run_decode(port, c)
+        assert cases.rel_err(out, ref) <= TOL
+    h.close()
