@@ -134,7 +134,8 @@ def bench_config(w, world: int, gather: str) -> dict:
             "parallelism": (f"kv-head shards x{world} + per-layer all-gather of head outputs "
                             f"({'decode-kernel NVLink peer stores' if gather == 'p2p' else 'NCCL'})")
             if world > 1 else "single GPU",
-            "l2": "inputs larger than L2 (KV bytes per step >> 126 MB); no flush"}
+            "l2": "inputs larger than L2 (KV bytes per step >> 126 MB); no flush",
+            "step": "one token through all layers"}
 
 
 def cpu_step_runner(w):
@@ -370,8 +371,21 @@ def bench_decode(args, w, rank, world, local, pg, peaks):
                     pg.all_gather_into_tensor(full[l], out[l])
 
     def timed(n, gather):
-        for _ in range(args.warmup):
+        # One step (36 layers, decode plus gather at N > 1) captured in a CUDA graph and replayed: the
+        # kernels carry no per-call host state (the gather epoch lives on the device), and the host
+        # would otherwise have to issue two launches per ~18 us layer at N = 8.  The NCCL gather runs
+        # as a host loop.
+        run = lambda: step(gather=gather)  # noqa: E731
+        graph = None
+        if world == 1 or gather == "p2p":
             step(gather=gather)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                step(gather=gather)
+            run = graph.replay
+        for _ in range(args.warmup):
+            run()
         torch.cuda.synchronize()
         h.sync()
         if world > 1:
@@ -381,13 +395,14 @@ def bench_decode(args, w, rank, world, local, pg, peaks):
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record()
         for _ in range(n):
-            step(gather=gather)
+            run()
         t1.record()
         torch.cuda.synchronize()
         if world > 1:
             pg.barrier()
             torch.cuda.synchronize()
         h.sync()
+        del graph
         ms = t0.elapsed_time(t1)
         if world > 1:
             t = torch.tensor([ms], device=dev)
@@ -771,6 +786,8 @@ def main():
             "hbm_gbs": res["hbm_gbs_step"],
             "roofline": res["roofline"], "clocks": res["clocks"], "e2e": res["e2e"],
             "gpu_launches": res["gpu_launches"], "parity": res["parity"],
+            "timing": ("CUDA events around K replays of a CUDA graph of one step (36 decode launches"
+                       + (", 36 gather waits" if world > 1 else "") + "), max over ranks"),
         }
         if res.get("other_gather"):
             line["other_gather"] = res["other_gather"]

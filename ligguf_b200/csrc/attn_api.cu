@@ -98,27 +98,42 @@ float synth_mul(float scale) { return static_cast<float>(static_cast<double>(sca
 
 // ---------------------------------------------------------------------------- gather wait
 // Gather wait: one thread per element polls its 64-bit word in this rank's gather slot until the
-// word carries `epoch` (bounded), then writes the fp32 value to `out`.  Launched as a programmatic
+// word carries the call's epoch (bounded), then writes the fp32 value to `out`.  The epoch is
+// gstate[0] + 1 (gstate[0] = the last completed call's epoch, advanced here by the last block to
+// finish, gstate[1] counting the finished blocks), the slot is epoch & 1: nothing of a call is
+// decided on the host, so a captured CUDA graph replays correctly.  Launched as a programmatic
 // dependent of the decode kernel, it starts while the decode still runs; it reads nothing the decode
-// writes other than these self-validating words, so it never waits for the decode grid itself.
-__global__ void __launch_bounds__(256) gather_wait_kernel(const unsigned long long* words, int epoch, float* out,
-                                                          int n, int* err) {
+// writes other than these self-validating words, so it never waits for the decode grid itself (the
+// decode reads gstate[0] only after this kernel's predecessor completed, and the next decode only
+// after this one completed).
+__global__ void __launch_bounds__(256) gather_wait_kernel(const unsigned long long* words_base, int* gstate,
+                                                          float* out, int n, int* err) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int epoch = __ldcg(gstate) + 1;
+    const unsigned long long* words = words_base + size_t(epoch & 1) * n;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    const uint64_t deadline = lg::globaltimer_ns() + lg::kWaitLimitNs;
-    const uint32_t want = static_cast<uint32_t>(epoch);
-    unsigned long long w;
-    uint32_t spins = 0;
-    while (true) {
-        asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(words + i) : "memory");
-        if (static_cast<uint32_t>(w >> 32) == want) break;
-        if ((++spins & 63u) == 0u && lg::globaltimer_ns() > deadline) {
-            *reinterpret_cast<volatile int*>(err) = lg::KERR_TIMEOUT_PEER;
-            return;
+    if (i < n) {
+        const uint64_t deadline = lg::globaltimer_ns() + lg::kWaitLimitNs;
+        const uint32_t want = static_cast<uint32_t>(epoch);
+        unsigned long long w;
+        uint32_t spins = 0;
+        bool ok = true;
+        while (true) {
+            asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(words + i) : "memory");
+            if (static_cast<uint32_t>(w >> 32) == want) break;
+            if ((++spins & 63u) == 0u && lg::globaltimer_ns() > deadline) {
+                *reinterpret_cast<volatile int*>(err) = lg::KERR_TIMEOUT_PEER;
+                ok = false;
+                break;
+            }
         }
+        if (ok) out[i] = __uint_as_float(static_cast<uint32_t>(w));
     }
-    out[i] = __uint_as_float(static_cast<uint32_t>(w));
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(&gstate[1], 1) == static_cast<int>(gridDim.x) - 1) {
+        gstate[1] = 0;
+        gstate[0] = epoch;  // read by the next call's kernels, which start after this grid completes
+    }
 }
 
 }  // namespace
@@ -160,7 +175,9 @@ struct ligguf_attn {
     // SARA gather over CUDA IPC
     unsigned long long* gbuf = nullptr;  // [2][n_heads*D] gather words: (epoch << 32) | fp32 bits
     size_t gbuf_bytes = 0;
-    int g_nranks = 0, g_rank = -1, g_epoch = 0;
+    int g_nranks = 0, g_rank = -1;
+    bool g_pending = false;   // a gathered decode was enqueued and its wait not yet
+    int* d_gstate = nullptr;  // device: [0] last completed gather epoch, [1] finished wait blocks
     std::vector<void*> g_opened;
     unsigned long long** d_peer_ll = nullptr;  // [2][nranks]: slot s of every rank's gather buffer
 };
@@ -320,12 +337,11 @@ int decode_enqueue(ligguf_attn* h, int layer, int pos, const float* dq, const fl
     a.pre_rows = (layer >= h->wr_l0 && layer < h->wr_l1) ? std::min(pos, h->wr_row0) : pos;
     note_cache_write(h, layer, 1, pos);
     if (gather) {
-        const int slot = h->g_epoch & 1;
-        a.peer_ll = h->d_peer_ll + slot * h->g_nranks;
+        a.peer_ll = h->d_peer_ll;
         a.nranks = h->g_nranks;
         a.rank = h->g_rank;
         a.q_off = c.kv_head0 * h->nrep * D;
-        a.flag_value = h->g_epoch;
+        a.epoch = h->d_gstate;
     }
     switch (c.kv_type) {
         case LIGGUF_KV_F32: return launch_decode_k<float>(h, a, st);
@@ -661,7 +677,7 @@ int ligguf_cuda_attn_free(ligguf_attn* h) {
     for (void* p : h->g_opened)
         if (p) cudaIpcCloseMemHandle(p);
     void* dev_ptrs[] = {h->kc, h->vc, h->freq, h->qg, h->kg, h->part, h->gpart, h->counters, h->d_stage, h->qf, h->qb,
-                        h->kb, h->vb, h->gbuf, h->d_peer_ll};
+                        h->kb, h->vb, h->gbuf, h->d_peer_ll, h->d_gstate};
     for (void* p : dev_ptrs)
         if (p) cudaFree(p);
     if (h->h_err) cudaFreeHost(h->h_err);
@@ -1076,9 +1092,11 @@ int ligguf_cuda_attn_gather_open(ligguf_attn* h, int nranks, int rank, const voi
     }
     LG_CUDA(cudaMalloc(reinterpret_cast<void**>(&h->d_peer_ll), slots.size() * sizeof(unsigned long long*)));
     LG_CUDA(cudaMemcpy(h->d_peer_ll, slots.data(), slots.size() * sizeof(unsigned long long*), cudaMemcpyHostToDevice));
+    LG_CUDA(cudaMalloc(reinterpret_cast<void**>(&h->d_gstate), 2 * sizeof(int)));
+    LG_CUDA(cudaMemset(h->d_gstate, 0, 2 * sizeof(int)));
     h->g_nranks = nranks;
     h->g_rank = rank;
-    h->g_epoch = 0;
+    h->g_pending = false;
     return LIGGUF_ATTN_OK;
 }
 
@@ -1086,19 +1104,18 @@ int ligguf_cuda_attn_decode_gather_async(ligguf_attn* h, int layer, int pos, con
                                          const float* d_v, void* stream) {
     if (!h) return fail(LIGGUF_ATTN_EINVAL, "null handle");
     if (!h->g_nranks) return fail(LIGGUF_ATTN_ESTATE, "gather not open");
+    if (h->g_pending) return fail(LIGGUF_ATTN_ESTATE, "the previous gathered decode has no gather wait yet");
     DeviceGuard dg(h->cfg.device);
-    ++h->g_epoch;
     const int rc = decode_enqueue(h, layer, pos, d_q, d_k, d_v, nullptr, static_cast<cudaStream_t>(stream), true);
-    if (rc) --h->g_epoch;
+    if (!rc) h->g_pending = true;
     return rc;
 }
 
 int ligguf_cuda_attn_gather_wait_async(ligguf_attn* h, int layer, float* d_out, void* stream) {
     if (!h || !d_out) return fail(LIGGUF_ATTN_EINVAL, "null argument");
-    if (!h->g_nranks || h->g_epoch == 0) return fail(LIGGUF_ATTN_ESTATE, "no gathered decode in flight");
+    if (!h->g_nranks || !h->g_pending) return fail(LIGGUF_ATTN_ESTATE, "no gathered decode in flight");
     if (layer < 0 || layer >= h->cfg.n_layers) return fail(LIGGUF_ATTN_EINVAL, "layer %d out of range", layer);
     DeviceGuard dg(h->cfg.device);
-    const int slot = h->g_epoch & 1;
     const int vec = h->cfg.n_heads * h->cfg.head_dim;
     cudaLaunchConfig_t lc = {};
     lc.gridDim = dim3(ceil_div(vec, 256), 1, 1);
@@ -1109,9 +1126,10 @@ int ligguf_cuda_attn_gather_wait_async(ligguf_attn* h, int layer, float* d_out, 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     lc.attrs = attr;
     lc.numAttrs = 1;
-    LG_CUDA(cudaLaunchKernelEx(&lc, gather_wait_kernel, static_cast<const unsigned long long*>(h->gbuf + size_t(slot) * vec),
-                               h->g_epoch, d_out, vec, h->d_err));
+    LG_CUDA(cudaLaunchKernelEx(&lc, gather_wait_kernel, static_cast<const unsigned long long*>(h->gbuf), h->d_gstate,
+                               d_out, vec, h->d_err));
     LG_CUDA(cudaGetLastError());
+    h->g_pending = false;
     return LIGGUF_ATTN_OK;
 }
 

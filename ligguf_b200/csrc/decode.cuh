@@ -65,12 +65,13 @@ struct DecodeArgs {
     int* counters;      // [kv_headn] head tickets, then [kv_headn] grab counters, then
                         // [kv_headn][kDecodeMaxGroups] group tickets; zero between launches
     int* err;           // error word (mapped host memory)
-    unsigned long long* const* peer_ll;  // multi-GPU gather: [nranks] gather slots of [n_heads*D] words (or null)
+    unsigned long long* const* peer_ll;  // multi-GPU gather (or null): [2][nranks] gather slots of
+                                         // [n_heads*D] words, slot = call epoch & 1
     int nranks;
     int rank;
     int q_off;          // element offset of this shard's heads in the gathered vector
     int kv_head0;       // global index of this shard's first KV head (gather flag slot)
-    int flag_value;     // epoch carried in the high half of every gather word
+    const int* epoch;   // gather: the last completed call's epoch (device); this call's is one more
     int pre_rows;       // cache rows [0, pre_rows) of this layer are final before the previous grid ends
     int row0;           // tensor-map row of (this layer, position 0) = layer * n_context
     int pos;
@@ -460,8 +461,13 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
     // completed - except the producer's first copies of cache rows below a.pre_rows, which no
     // kernel still in flight can be writing (see the producer).  The next kernel may then launch:
     // its CTAs take SM slots as this grid's retire.
-    if (warp != kDecodeConsumerWarps) asm volatile("griddepcontrol.wait;" ::: "memory");
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // The producer warp waits later (after its early copies) and never triggers: the dependent grid
+    // may launch only once every CTA's consumers have seen the previous grid complete (the gather
+    // wait that follows a gathered decode reads the epoch its own predecessor wrote).
+    if (warp != kDecodeConsumerWarps) {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    }
 
     // Consumer warps start loading their first prologue job (q head, and k / v of the current token
     // on the owner CTA) right away; the norm and rotation happen after the set-up barrier.
@@ -830,15 +836,27 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
         if (tid == 0) a.chunk_ctr[g] = 0;
     }
     if (a.peer_ll) {
+        // The next layer's decode may start once the gathered words have arrived, before this grid
+        // has completed: the counter resets above go out before any word does.
+        if (a.n_split > 1) {
+            __threadfence();
+            named_bar_sync(1, kDecodeConsumers);
+        }
         // Multi-GPU gather: every output element goes to every rank's gather slot as one 64-bit word,
         // (epoch << 32) | fp32 bits, stored with a single relaxed system-scope store.  A reader that
         // sees the current epoch in a word has that word's value: no fence, no flags.
-        const unsigned long long tag = static_cast<unsigned long long>(static_cast<uint32_t>(a.flag_value)) << 32;
-        for (int idx = tid; idx < NREP * D; idx += kDecodeConsumers) {
-            const unsigned long long w = tag | __float_as_uint(o_s[idx] / l_s[idx / D]);
+        // The epoch lives in device memory (the gather wait of the previous call advanced it), so a
+        // captured CUDA graph replays correctly.  Two consecutive elements per 16-byte store.
+        const int epoch = __ldcg(a.epoch) + 1;
+        unsigned long long* const* peers = a.peer_ll + (epoch & 1) * a.nranks;
+        const unsigned long long tag = static_cast<unsigned long long>(static_cast<uint32_t>(epoch)) << 32;
+        for (int idx = 2 * tid; idx < NREP * D; idx += 2 * kDecodeConsumers) {
+            const unsigned long long w0 = tag | __float_as_uint(o_s[idx] / l_s[idx / D]);
+            const unsigned long long w1 = tag | __float_as_uint(o_s[idx + 1] / l_s[(idx + 1) / D]);
             const size_t e = static_cast<size_t>(a.q_off) + static_cast<size_t>(head0) * D + idx;
             for (int rr = 0; rr < a.nranks; ++rr)
-                asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(a.peer_ll[rr] + e), "l"(w) : "memory");
+                asm volatile("st.relaxed.sys.global.v2.b64 [%0], {%1, %2};" ::"l"(peers[rr] + e), "l"(w0), "l"(w1)
+                             : "memory");
         }
         return;
     }

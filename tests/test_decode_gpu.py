@@ -334,3 +334,50 @@ def test_decode_short_streams(gpu, H, Hk, D, pos, kv_headn, scale):
         ref, _, _ = cases.run_decode(port, c)
         assert cases.rel_err(out, ref) <= TOL
     h.close()
+
+
+def test_self_gather_epochs_advance_on_device_and_replay(gpu):
+    """A one-rank gather (the whole model on one GPU, the rank storing into its own buffer): calls
+    issued directly, then the same calls captured in a CUDA graph and replayed several times.  The
+    gather epoch and slot are decided on the device, so every replay tags its words with a new epoch
+    and the waits never take a stale word: each output equals the reference's."""
+    import torch
+    port = orc.Checker("port")
+    H, Hk, D, L, pos = 16, 4, 128, 3, 700
+    cs = [cases.decode_case(H=H, Hk=Hk, D=D, n_ctx=768, theta=1e6, qk_norm=1, pos=pos, seed=60 + l, layer=l)
+          for l in range(L)]
+    h = make_handle(cs[0], n_layers=L, layer=0)
+    for l, c in enumerate(cs):
+        h.set_qk_norm(l, c["qg"], c["kg"])
+        h.kv_synth(l, 1, 0, pos, c["seed"], c["scale"])
+    h.gather_open(0, [h.gather_ipc_handle()])
+    dev = torch.device("cuda", 0)
+    ins = [tuple(torch.from_numpy(c[x]).to(dev) for x in ("q", "k", "v")) for c in cs]
+    outs = torch.full((L, H * D), float("nan"), device=dev)
+    refs = [cases.run_decode(port, c)[0] for c in cs]
+
+    def step():
+        for l in range(L):
+            h.decode_gather_async(l, pos, *ins[l])
+            h.gather_wait_async(l, outs[l])
+
+    def check():
+        torch.cuda.synchronize()
+        h.sync()
+        for l in range(L):
+            assert cases.rel_err(outs[l].cpu().numpy(), refs[l]) <= TOL, l
+        outs.fill_(float("nan"))
+
+    for _ in range(3):
+        step()
+        check()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    for _ in range(4):
+        g.replay()
+        check()
+    step()  # direct calls after the replays continue the device's epoch sequence
+    check()
+    del g
+    h.close()
