@@ -240,6 +240,11 @@ size_t ligguf_cuda_qmat_row_bytes(int type, int n);
  * memory, or device memory when rows_on_device is set. */
 int ligguf_cuda_qmat_init(int type, int n, int d, const void* rows, int rows_on_device, int device,
                           ligguf_qmat** out);
+/* Columns [col0, col0+ncols) of every row of such a matrix (whole blocks of the type): the SARA
+ * shard's slice of attn_output, whose rank multiplies only its heads' columns
+ * (matmul_partial_cols, cpp/ligguf_distrib.cpp:587-605,750).  The result is a d x ncols matrix. */
+int ligguf_cuda_qmat_init_cols(int type, int n, int d, const void* rows, int col0, int ncols,
+                               int rows_on_device, int device, ligguf_qmat** out);
 int ligguf_cuda_qmat_free(ligguf_qmat* w);
 /* matmul3 (w1, w2 non-NULL), matmul2 (w2 NULL) or matmul (w1, w2 NULL): device pointers, x [n],
  * out_i [d_i], enqueued on `stream` (a cudaStream_t; NULL = legacy default).  All matrices share n
@@ -264,6 +269,31 @@ int ligguf_cuda_matmul3_batch(const ligguf_qmat* w0, const ligguf_qmat* w1, cons
  * reference's results. */
 int ligguf_cuda_quantize_q8_K_async(const float* d_x, int n, void* d_blocks, void* stream);
 int ligguf_cuda_quantize_q8_0_async(const float* d_x, int n, void* d_blocks, void* stream);
+
+/* ---- SARA attn_output projection + reduce over NVLink ------------------------------------- */
+/* Replaces the tail of att_partial and the master's sum (cpp/ligguf_distrib.cpp:749-750,1025-1047):
+ * every rank projects its heads' attention output through its columns of attn_output (a column slice,
+ * ligguf_cuda_qmat_init_cols) and the partial rows are summed over the ranks.  Here the projection's
+ * epilogue stores each partial row straight into every rank's reduce buffer over NVLink (CUDA IPC,
+ * one 64-bit word (epoch << 32) | fp32 bits per row and rank, no fence, no flag), and a wait kernel on
+ * every rank sums the ranks' rows in rank order (rank 0's, then += rank 1's, ... as the master does)
+ * and adds the sum to the residual.  The reference sends the workers' partials over TCP quantized to
+ * Q8_0 (:892-902); here they cross as fp32, so the sum does not carry that wire error.
+ * Set-up: ligguf_cuda_reduce_init on every rank (rows = n_embed), exchange the 64-byte handles of
+ * ligguf_cuda_reduce_ipc_handle (any side channel), ligguf_cuda_reduce_open with all of them in rank
+ * order.  Per use: ligguf_cuda_matmul_reduce_async, then ligguf_cuda_reduce_wait_async on the same
+ * stream (x_inout += sum, out = sum; either may be NULL).  Epochs live on the device, so the pair can
+ * be captured in a CUDA graph.  Waits are bounded: ligguf_cuda_reduce_status reports a timeout. */
+typedef struct ligguf_reduce ligguf_reduce;
+int ligguf_cuda_reduce_init(int rows, int nranks, int rank, int device, ligguf_reduce** out);
+int ligguf_cuda_reduce_free(ligguf_reduce* r);
+int ligguf_cuda_reduce_ipc_handle(ligguf_reduce* r, void* handle_out /* 64 bytes */, size_t handle_size);
+int ligguf_cuda_reduce_open(ligguf_reduce* r, const void* handles /* nranks * 64 bytes */,
+                            size_t handle_size);
+int ligguf_cuda_matmul_reduce_async(const ligguf_qmat* w, ligguf_reduce* r, const float* d_x,
+                                    void* stream);
+int ligguf_cuda_reduce_wait_async(ligguf_reduce* r, float* d_x_inout, float* d_out, void* stream);
+int ligguf_cuda_reduce_status(ligguf_reduce* r, void* stream);
 
 /* ---- seeded synthetic inputs ------------------------------------------------------------- */
 /* Tensor ids of the synthetic generator's streams. */

@@ -77,7 +77,15 @@ _PROTOS = {
     "ligguf_cuda_bert_attn_tc_noalloc_status": [_vp],
     "ligguf_cuda_qmat_row_bytes": [_i, _i],
     "ligguf_cuda_qmat_init": [_i, _i, _i, _vp, _i, _i, ctypes.POINTER(_vp)],
+    "ligguf_cuda_qmat_init_cols": [_i, _i, _i, _vp, _i, _i, _i, _i, ctypes.POINTER(_vp)],
     "ligguf_cuda_qmat_free": [_vp],
+    "ligguf_cuda_reduce_init": [_i, _i, _i, _i, ctypes.POINTER(_vp)],
+    "ligguf_cuda_reduce_free": [_vp],
+    "ligguf_cuda_reduce_ipc_handle": [_vp, _vp, _sz],
+    "ligguf_cuda_reduce_open": [_vp, _vp, _sz],
+    "ligguf_cuda_matmul_reduce_async": [_vp, _vp, _vp, _vp],
+    "ligguf_cuda_reduce_wait_async": [_vp, _vp, _vp, _vp],
+    "ligguf_cuda_reduce_status": [_vp, _vp],
     "ligguf_cuda_matmul3_async": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
     "ligguf_cuda_matmul3": [_vp, _vp, _vp, _vp, _vp, _vp, _vp],
     "ligguf_cuda_matmul3_batch_async": [_vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp],

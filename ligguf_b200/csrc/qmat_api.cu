@@ -5,6 +5,7 @@
 #include <algorithm>
 #include <cstring>
 #include <numeric>
+#include <vector>
 
 #include "api_util.h"
 #include "common.cuh"
@@ -22,6 +23,19 @@ struct ligguf_qmat {
     float* stage = nullptr;    // device staging of the host-pointer calls: x and the outputs
     size_t stage_floats = 0;
     cudaStream_t stream = nullptr;
+};
+
+// A SARA reduce group member: this rank's buffer [2][nranks][rows] of 64-bit words, shared with the
+// other ranks through CUDA IPC, and the device state of its epochs.
+struct ligguf_reduce {
+    int rows = 0, nranks = 0, rank = 0, device = 0;
+    unsigned long long* buf = nullptr;
+    unsigned long long** d_peers = nullptr;  // [nranks] buffer bases (own buffer for this rank)
+    std::vector<void*> opened;
+    int* d_state = nullptr;                  // [0] last completed epoch, [1] finished wait blocks
+    int* h_err = nullptr;
+    int* d_err = nullptr;
+    bool open = false, pending = false;
 };
 
 namespace {
@@ -109,8 +123,15 @@ int launch_qmv(lg::QmvArgs& a, int smem, int dev, cudaStream_t st) {
 // outs[i] + t * out_strides[i].  One launch per group of up to kQmvMaxTokens tokens (fewer when
 // their activations would not fit shared memory next to the weight ring).
 int matmul_enqueue(const ligguf_qmat* const* ws, float* const* outs, const long long* out_strides, int nmat,
-                   const float* d_x, long long x_stride, int n_tok, cudaStream_t st) {
+                   const float* d_x, long long x_stride, int n_tok, cudaStream_t st,
+                   const ligguf_reduce* red = nullptr) {
     lg::QmvArgs a = {};
+    if (red) {
+        a.red.peers = red->d_peers;
+        a.red.state = red->d_state;
+        a.red.nranks = red->nranks;
+        a.red.rank = red->rank;
+    }
     a.n = ws[0]->n;
     a.err = ws[0]->d_err;
     a.x_stride = x_stride;
@@ -119,7 +140,7 @@ int matmul_enqueue(const ligguf_qmat* const* ws, float* const* outs, const long 
         const ligguf_qmat* w = ws[i];
         if (w->n != a.n) return fail(LIGGUF_ATTN_EINVAL, "matrices of one call have different input widths");
         if (w->device != ws[0]->device) return fail(LIGGUF_ATTN_EINVAL, "matrices of one call are on different devices");
-        if (!outs[i]) return fail(LIGGUF_ATTN_EINVAL, "null output");
+        if (!outs[i] && !red) return fail(LIGGUF_ATTN_EINVAL, "null output");
         lg::QmvMat& m = a.m[a.nmat++];
         m.w = w->w;
         m.out = outs[i];
@@ -146,7 +167,7 @@ int matmul_enqueue(const ligguf_qmat* const* ws, float* const* outs, const long 
     for (int t0 = 0; t0 < n_tok; t0 += T) {
         a.x = d_x + t0 * x_stride;
         a.n_tok = std::min(T, n_tok - t0);
-        for (int i = 0; i < nmat; ++i) a.m[i].out = outs[i] + t0 * out_strides[i];
+        for (int i = 0; i < nmat; ++i) a.m[i].out = outs[i] ? outs[i] + t0 * out_strides[i] : nullptr;
         int rc;
         switch (T) {
             case 8: rc = launch_qmv<8>(a, smem, dev, st); break;
@@ -195,7 +216,20 @@ int ligguf_cuda_qmat_free(ligguf_qmat* w) {
 
 int ligguf_cuda_qmat_init(int type, int n, int d, const void* rows, int rows_on_device, int device,
                           ligguf_qmat** out) {
+    return ligguf_cuda_qmat_init_cols(type, n, d, rows, 0, n, rows_on_device, device, out);
+}
+
+int ligguf_cuda_qmat_init_cols(int type, int n, int d, const void* rows, int col0, int ncols, int rows_on_device,
+                               int device, ligguf_qmat** out) {
     if (!out || !rows) return fail(LIGGUF_ATTN_EINVAL, "null argument");
+    const int be = lg::qt_block_elems(type);
+    if (!be) return fail(LIGGUF_ATTN_EUNSUPPORTED, "weight type %d has no kernel", type);
+    if (col0 < 0 || ncols < 1 || col0 + ncols > n || col0 % be || ncols % be)
+        return fail(LIGGUF_ATTN_EINVAL, "columns [%d, %d) of %d are not whole blocks of %d", col0, col0 + ncols, n, be);
+    const int src_rb = row_bytes(type, n);
+    if (!src_rb) return fail(LIGGUF_ATTN_EINVAL, "width %d is not a whole number of blocks", n);
+    const size_t src_off = size_t(col0 / be) * lg::qt_block_bytes(type);
+    n = ncols;
     *out = nullptr;
     if (n < 1 || d < 1) return fail(LIGGUF_ATTN_EINVAL, "non-positive size %d x %d", d, n);
     if (!lg::qt_block_bytes(type)) return fail(LIGGUF_ATTN_EUNSUPPORTED, "weight type %d has no kernel", type);
@@ -218,9 +252,10 @@ int ligguf_cuda_qmat_init(int type, int n, int d, const void* rows, int rows_on_
     w->device = device;
     const size_t bytes = size_t(d) * rb;
     const size_t alloc = (bytes + 15) / 16 * 16 + 16;
+    // rows of the source are src_rb bytes apart; the kept columns start src_off bytes into each
     if (cudaMalloc(&w->w, alloc) != cudaSuccess || cudaMemset(w->w, 0, alloc) != cudaSuccess ||
-        cudaMemcpy(w->w, rows, bytes, rows_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice) !=
-            cudaSuccess ||
+        cudaMemcpy2D(w->w, rb, static_cast<const uint8_t*>(rows) + src_off, src_rb, rb, d,
+                     rows_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaHostAlloc(&w->h_err, 64, cudaHostAllocMapped) != cudaSuccess ||
         cudaHostGetDevicePointer(reinterpret_cast<void**>(&w->d_err), w->h_err, 0) != cudaSuccess ||
         cudaStreamCreateWithFlags(&w->stream, cudaStreamNonBlocking) != cudaSuccess) {
@@ -286,6 +321,131 @@ int ligguf_cuda_matmul3_batch(const ligguf_qmat* w0, const ligguf_qmat* w1, cons
 int ligguf_cuda_matmul3(const ligguf_qmat* w0, const ligguf_qmat* w1, const ligguf_qmat* w2, const float* x,
                         float* out0, float* out1, float* out2) {
     return ligguf_cuda_matmul3_batch(w0, w1, w2, x, 1, out0, out1, out2);
+}
+
+// ---------------------------------------------------------------------------- SARA reduce
+int ligguf_cuda_reduce_free(ligguf_reduce* r) {
+    if (!r) return LIGGUF_ATTN_OK;
+    DeviceGuard dg(r->device);
+    cudaDeviceSynchronize();
+    for (void* p : r->opened)
+        if (p) cudaIpcCloseMemHandle(p);
+    if (r->buf) cudaFree(r->buf);
+    if (r->d_peers) cudaFree(r->d_peers);
+    if (r->d_state) cudaFree(r->d_state);
+    if (r->h_err) cudaFreeHost(r->h_err);
+    delete r;
+    return LIGGUF_ATTN_OK;
+}
+
+int ligguf_cuda_reduce_init(int rows, int nranks, int rank, int device, ligguf_reduce** out) {
+    if (!out) return fail(LIGGUF_ATTN_EINVAL, "null out");
+    *out = nullptr;
+    if (rows < 1 || nranks < 1 || rank < 0 || rank >= nranks)
+        return fail(LIGGUF_ATTN_EINVAL, "rows %d, rank %d of %d", rows, rank, nranks);
+    int ndev = 0;
+    LG_CUDA(cudaGetDeviceCount(&ndev));
+    if (device < 0 || device >= ndev) return fail(LIGGUF_ATTN_EINVAL, "device %d of %d", device, ndev);
+    DeviceGuard dg(device);
+    ligguf_reduce* r = new ligguf_reduce();
+    r->rows = rows;
+    r->nranks = nranks;
+    r->rank = rank;
+    r->device = device;
+    const size_t words = 2 * size_t(nranks) * rows;
+    if (cudaMalloc(&r->buf, words * 8) != cudaSuccess || cudaMemset(r->buf, 0, words * 8) != cudaSuccess ||
+        cudaMalloc(&r->d_peers, nranks * sizeof(void*)) != cudaSuccess ||
+        cudaMalloc(&r->d_state, 2 * sizeof(int)) != cudaSuccess ||
+        cudaMemset(r->d_state, 0, 2 * sizeof(int)) != cudaSuccess ||
+        cudaHostAlloc(&r->h_err, 64, cudaHostAllocMapped) != cudaSuccess ||
+        cudaHostGetDevicePointer(reinterpret_cast<void**>(&r->d_err), r->h_err, 0) != cudaSuccess) {
+        (void)cudaGetLastError();
+        ligguf_cuda_reduce_free(r);
+        return fail(LIGGUF_ATTN_ENOMEM, "reduce buffers");
+    }
+    *r->h_err = 0;
+    *out = r;
+    return LIGGUF_ATTN_OK;
+}
+
+int ligguf_cuda_reduce_ipc_handle(ligguf_reduce* r, void* handle_out, size_t handle_size) {
+    if (!r || !handle_out) return fail(LIGGUF_ATTN_EINVAL, "null argument");
+    if (handle_size < sizeof(cudaIpcMemHandle_t)) return fail(LIGGUF_ATTN_EINVAL, "handle buffer of %zu bytes", handle_size);
+    DeviceGuard dg(r->device);
+    cudaIpcMemHandle_t hd;
+    LG_CUDA(cudaIpcGetMemHandle(&hd, r->buf));
+    memcpy(handle_out, &hd, sizeof(hd));
+    return LIGGUF_ATTN_OK;
+}
+
+int ligguf_cuda_reduce_open(ligguf_reduce* r, const void* handles, size_t handle_size) {
+    if (!r || !handles) return fail(LIGGUF_ATTN_EINVAL, "null argument");
+    if (handle_size < sizeof(cudaIpcMemHandle_t)) return fail(LIGGUF_ATTN_EINVAL, "handle stride %zu", handle_size);
+    if (r->open) return fail(LIGGUF_ATTN_ESTATE, "reduce already open");
+    DeviceGuard dg(r->device);
+    std::vector<unsigned long long*> bases(r->nranks);
+    r->opened.assign(r->nranks, nullptr);
+    for (int p = 0; p < r->nranks; ++p) {
+        if (p == r->rank) {
+            bases[p] = r->buf;
+            continue;
+        }
+        cudaIpcMemHandle_t hd;
+        memcpy(&hd, static_cast<const char*>(handles) + size_t(p) * handle_size, sizeof(hd));
+        void* ptr = nullptr;
+        LG_CUDA(cudaIpcOpenMemHandle(&ptr, hd, cudaIpcMemLazyEnablePeerAccess));
+        r->opened[p] = ptr;
+        bases[p] = static_cast<unsigned long long*>(ptr);
+    }
+    LG_CUDA(cudaMemcpy(r->d_peers, bases.data(), bases.size() * sizeof(void*), cudaMemcpyHostToDevice));
+    r->open = true;
+    return LIGGUF_ATTN_OK;
+}
+
+int ligguf_cuda_matmul_reduce_async(const ligguf_qmat* w, ligguf_reduce* r, const float* d_x, void* stream) {
+    if (!w || !r || !d_x) return fail(LIGGUF_ATTN_EINVAL, "null argument");
+    if (!r->open) return fail(LIGGUF_ATTN_ESTATE, "reduce not open");
+    if (r->pending) return fail(LIGGUF_ATTN_ESTATE, "the previous reduced projection has no reduce wait yet");
+    if (w->d != r->rows) return fail(LIGGUF_ATTN_EINVAL, "matrix of %d rows into a reduce of %d", w->d, r->rows);
+    if (w->device != r->device) return fail(LIGGUF_ATTN_EINVAL, "matrix and reduce on different devices");
+    DeviceGuard dg(w->device);
+    const ligguf_qmat* ws[1] = {w};
+    float* outs[1] = {nullptr};
+    const long long strides[1] = {0};
+    const int rc = matmul_enqueue(ws, outs, strides, 1, d_x, w->n, 1, static_cast<cudaStream_t>(stream), r);
+    if (!rc) r->pending = true;
+    return rc;
+}
+
+int ligguf_cuda_reduce_wait_async(ligguf_reduce* r, float* d_x_inout, float* d_out, void* stream) {
+    if (!r) return fail(LIGGUF_ATTN_EINVAL, "null argument");
+    if (!r->open || !r->pending) return fail(LIGGUF_ATTN_ESTATE, "no reduced projection in flight");
+    DeviceGuard dg(r->device);
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3((r->rows + 255) / 256, 1, 1);
+    lc.blockDim = dim3(256, 1, 1);
+    lc.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    LG_CUDA(cudaLaunchKernelEx(&lc, lg::reduce_wait_kernel, static_cast<const unsigned long long*>(r->buf), r->d_state,
+                               r->nranks, r->rows, d_x_inout, d_out, r->d_err));
+    r->pending = false;
+    return LIGGUF_ATTN_OK;
+}
+
+int ligguf_cuda_reduce_status(ligguf_reduce* r, void* stream) {
+    if (!r) return fail(LIGGUF_ATTN_EINVAL, "null argument");
+    DeviceGuard dg(r->device);
+    LG_CUDA(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+    if (*reinterpret_cast<volatile int*>(r->h_err)) {
+        const int code = *r->h_err;
+        *reinterpret_cast<volatile int*>(r->h_err) = 0;
+        return fail(LIGGUF_ATTN_ETIMEDOUT, "a bounded wait of the reduce gave up (code %d)", code);
+    }
+    return LIGGUF_ATTN_OK;
 }
 
 int ligguf_cuda_quantize_q8_K_async(const float* d_x, int n, void* d_blocks, void* stream) {

@@ -75,7 +75,18 @@ struct QmvAct {
     int bytes;                   // all tokens, a multiple of 1024 (the ring starts after it)
 };
 
+// Reduce mode (the SARA attn_output partial, cpp/ligguf_distrib.cpp:749-750): instead of out[r], row
+// r's value goes to every rank's reduce buffer [2][nranks][rows] as one 64-bit word (epoch << 32) |
+// fp32 bits, at [epoch & 1][rank][r]; the epoch is state[0] + 1 (state[0] is advanced by the reduce
+// wait kernel).  One token, one matrix.
+struct QmvRed {
+    unsigned long long* const* peers;  // [nranks] reduce buffer bases (null: plain outputs)
+    const int* state;
+    int nranks, rank;
+};
+
 struct QmvArgs {
+    QmvRed red;
     QmvMat m[kQmvMaxMats];
     int nmat;
     const float* x;  // x[t * x_stride + i], t < n_tok
@@ -510,7 +521,7 @@ struct WUnit<QT_Q6_K> {
 template <int TY, int T>
 __device__ __forceinline__ void qmv_tile(const uint8_t* tile, int nrows, int rb, int units, const uint8_t* act,
                                          const QmvAct& L, int n_tok, float* out, long long out_stride, int warp,
-                                         int lane) {
+                                         int lane, const QmvRed& red, int epoch, int r0, int rows) {
     for (int r = warp; r < nrows; r += kQmvWarps) {
         const uint8_t* row = tile + size_t(r) * rb;
         float acc[T];
@@ -527,7 +538,15 @@ __device__ __forceinline__ void qmv_tile(const uint8_t* tile, int nrows, int rb,
         for (int t = 0; t < T; ++t) {
             if (t < n_tok) {
                 const float v = warp_sum(acc[t]);
-                if (lane == 0) out[t * out_stride + r] = v;
+                if (red.peers) {  // lane p stores to rank p's buffer
+                    const unsigned long long w =
+                        (static_cast<unsigned long long>(static_cast<uint32_t>(epoch)) << 32) | __float_as_uint(v);
+                    const size_t e = (size_t(epoch & 1) * red.nranks + red.rank) * size_t(rows) + r0 + r;
+                    for (int p = lane; p < red.nranks; p += 32)
+                        asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(red.peers[p] + e), "l"(w) : "memory");
+                } else if (lane == 0) {
+                    out[t * out_stride + r] = v;
+                }
             }
         }
     }
@@ -617,6 +636,7 @@ __global__ void __launch_bounds__(kQmvThreads, 1) qmv_kernel(const __grid_consta
                 reinterpret_cast<float*>(tb + a.act.off_xf)[i] = x[i];
     }
     named_bar_sync(1, kQmvWarps * 32);
+    const int epoch = a.red.peers ? __ldcg(a.red.state) + 1 : 0;
 
     const int units = a.n / 32;
     for (int t = t_begin, it = 0; t < t_end; ++t, ++it) {
@@ -634,8 +654,11 @@ __global__ void __launch_bounds__(kQmvThreads, 1) qmv_kernel(const __grid_consta
         const int nrows = min(m.tile_rows, m.rows - r0);
         const uint8_t* tile = ring + s * kQmvStageMax;
         float* out = m.out + r0;
-#define LG_QMV_CASE(TY) \
-    case TY: qmv_tile<TY, T>(tile, nrows, m.rb, units, smem, a.act, a.n_tok, out, m.out_stride, warp, lane); break;
+#define LG_QMV_CASE(TY)                                                                                    \
+    case TY:                                                                                               \
+        qmv_tile<TY, T>(tile, nrows, m.rb, units, smem, a.act, a.n_tok, out, m.out_stride, warp, lane, a.red, \
+                        epoch, r0, m.rows);                                                                \
+        break;
         switch (m.type) {
             LG_QMV_CASE(QT_F32)
             LG_QMV_CASE(QT_F16)
@@ -646,11 +669,58 @@ __global__ void __launch_bounds__(kQmvThreads, 1) qmv_kernel(const __grid_consta
             LG_QMV_CASE(QT_Q3_K)
             LG_QMV_CASE(QT_Q4_K)
             LG_QMV_CASE(QT_Q5_K)
-            default: qmv_tile<QT_Q6_K, T>(tile, nrows, m.rb, units, smem, a.act, a.n_tok, out, m.out_stride, warp, lane);
+            default:
+                qmv_tile<QT_Q6_K, T>(tile, nrows, m.rb, units, smem, a.act, a.n_tok, out, m.out_stride, warp, lane,
+                                     a.red, epoch, r0, m.rows);
         }
 #undef LG_QMV_CASE
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
+    }
+}
+
+// Reduce wait (the SARA master's sum, cpp/ligguf_distrib.cpp:1040-1045, for every rank at once): one
+// thread per row polls the row's word of every rank in this rank's buffer until each carries the
+// call's epoch (bounded), sums them in rank order (rank 0's partial, then += rank 1's, ...), and adds
+// the sum to the residual x (fast/ligguf_fast_qk.cpp:111: x += attention output) and/or writes it to
+// `out`.  Epoch = state[0] + 1; the last block to finish advances state[0] (state[1] counts blocks).
+// Launched after the projection; it starts while the projection runs (its only inputs from it are
+// the self-validating words).
+__global__ void __launch_bounds__(256) reduce_wait_kernel(const unsigned long long* buf, int* state, int nranks,
+                                                          int rows, float* x_inout, float* out, int* err) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int epoch = __ldcg(state) + 1;
+    const unsigned long long* slot = buf + size_t(epoch & 1) * nranks * rows;
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r < rows) {
+        const uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
+        const uint32_t want = static_cast<uint32_t>(epoch);
+        float sum = 0.f;
+        bool ok = true;
+        for (int p = 0; p < nranks && ok; ++p) {
+            unsigned long long w;
+            uint32_t spins = 0;
+            while (true) {
+                asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(slot + size_t(p) * rows + r) : "memory");
+                if (static_cast<uint32_t>(w >> 32) == want) break;
+                if ((++spins & 63u) == 0u && globaltimer_ns() > deadline) {
+                    *reinterpret_cast<volatile int*>(err) = KERR_TIMEOUT_PEER;
+                    ok = false;
+                    break;
+                }
+            }
+            const float v = __uint_as_float(static_cast<uint32_t>(w));
+            sum = p == 0 ? v : __fadd_rn(sum, v);
+        }
+        if (ok) {
+            if (out) out[r] = sum;
+            if (x_inout) x_inout[r] = __fadd_rn(x_inout[r], sum);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(&state[1], 1) == static_cast<int>(gridDim.x) - 1) {
+        state[1] = 0;
+        state[0] = epoch;
     }
 }
 

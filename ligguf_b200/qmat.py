@@ -18,7 +18,7 @@ from . import _lib
 from ._lib import check
 
 __all__ = ["QT", "BLOCK", "row_bytes", "synthetic_rows", "QuantMatrix", "matmul3_async", "matmul3",
-           "matmul3_batch_async", "matmul3_batch"]
+           "matmul3_batch_async", "matmul3_batch", "NvlReduce"]
 
 # gguf_type numbers (fast/lil_gguf.h:26-44) of the supported weight types
 QT = {"F32": 0, "F16": 1, "Q8_0": 8, "Q2_K": 10, "Q3_K": 11, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14, "Q1_0": 40,
@@ -76,11 +76,17 @@ def _stream(stream):
 class QuantMatrix:
     """A d x n weight matrix of GGUF type ``t`` copied to HBM once (ligguf_cuda_qmat_init)."""
 
-    def __init__(self, t: int, n: int, rows, device: int = 0):
+    def __init__(self, t: int, n: int, rows, device: int = 0, cols=None):
+        """cols = (col0, ncols): keep only those columns of every row (ligguf_cuda_qmat_init_cols)."""
         self.lib = _lib.load()
         self.type, self.n = t, n
         self._h = ctypes.c_void_p()
-        if isinstance(rows, np.ndarray):
+        if cols is not None:
+            rows = np.ascontiguousarray(rows, dtype=np.uint8)
+            self.d, self.n = rows.shape[0], cols[1]
+            check(self.lib.ligguf_cuda_qmat_init_cols(t, n, self.d, rows.ctypes.data, cols[0], cols[1], 0, device,
+                                                      ctypes.byref(self._h)), "ligguf_cuda_qmat_init_cols")
+        elif isinstance(rows, np.ndarray):
             rows = np.ascontiguousarray(rows, dtype=np.uint8)
             self.d = rows.shape[0]
             check(self.lib.ligguf_cuda_qmat_init(t, n, self.d, rows.ctypes.data, 0, device, ctypes.byref(self._h)),
@@ -140,3 +146,47 @@ def matmul3(w0: QuantMatrix, w1, w2, x):
     check(_lib.load().ligguf_cuda_matmul3(_h(w0), _h(w1), _h(w2), x.ctypes.data, _ptr(outs[0]), _ptr(outs[1]),
                                           _ptr(outs[2])), "ligguf_cuda_matmul3")
     return [o for o in outs if o is not None]
+
+
+class NvlReduce:
+    """One rank of a SARA reduce group (ligguf_cuda_reduce_*): the attn_output partial projection of
+    this rank's heads stored into every rank's buffer over NVLink, summed in rank order on every rank
+    (cpp/ligguf_distrib.cpp:749-750,1025-1047)."""
+
+    def __init__(self, rows: int, nranks: int, rank: int, device: int = 0):
+        self.lib = _lib.load()
+        self.rows, self.nranks, self.rank = rows, nranks, rank
+        self._h = ctypes.c_void_p()
+        check(self.lib.ligguf_cuda_reduce_init(rows, nranks, rank, device, ctypes.byref(self._h)),
+              "ligguf_cuda_reduce_init")
+
+    def ipc_handle(self) -> bytes:
+        buf = ctypes.create_string_buffer(64)
+        check(self.lib.ligguf_cuda_reduce_ipc_handle(self._h, buf, 64), "ligguf_cuda_reduce_ipc_handle")
+        return buf.raw
+
+    def open(self, handles):
+        blob = b"".join(handles)
+        check(self.lib.ligguf_cuda_reduce_open(self._h, blob, 64), "ligguf_cuda_reduce_open")
+
+    def project_async(self, w: QuantMatrix, x, stream=None):
+        check(self.lib.ligguf_cuda_matmul_reduce_async(w.handle, self._h, _ptr(x), _stream(stream)),
+              "ligguf_cuda_matmul_reduce_async")
+
+    def wait_async(self, x_inout=None, out=None, stream=None):
+        check(self.lib.ligguf_cuda_reduce_wait_async(self._h, _ptr(x_inout), _ptr(out), _stream(stream)),
+              "ligguf_cuda_reduce_wait_async")
+
+    def status(self, stream=None):
+        check(self.lib.ligguf_cuda_reduce_status(self._h, _stream(stream)), "ligguf_cuda_reduce_status")
+
+    def close(self):
+        if self._h:
+            self.lib.ligguf_cuda_reduce_free(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -67,3 +67,17 @@ def test_qmat_argument_checks_without_gpu():
     assert lib.ligguf_cuda_matmul3_batch_async(None, None, None, None, 4, None, None, None, None) == _lib.EINVAL
     assert lib.ligguf_cuda_quantize_q8_K_async(None, 256, None, None) == _lib.EINVAL
     assert lib.ligguf_cuda_qmat_free(None) == _lib.OK
+
+
+def test_column_slice_and_reduce_argument_checks_without_gpu():
+    from ligguf_b200 import _lib
+    lib = _lib.load()
+    out = ctypes.c_void_p()
+    row = (ctypes.c_uint8 * 64)()
+    # columns must be whole blocks of the type (32 for Q8_0)
+    assert lib.ligguf_cuda_qmat_init_cols(8, 256, 1, row, 16, 64, 0, 0, ctypes.byref(out)) == _lib.EINVAL
+    assert lib.ligguf_cuda_qmat_init_cols(8, 256, 1, row, 224, 64, 0, 0, ctypes.byref(out)) == _lib.EINVAL
+    assert lib.ligguf_cuda_reduce_init(0, 2, 0, 0, ctypes.byref(out)) == _lib.EINVAL
+    assert lib.ligguf_cuda_reduce_init(16, 2, 2, 0, ctypes.byref(out)) == _lib.EINVAL
+    assert lib.ligguf_cuda_matmul_reduce_async(None, None, None, None) == _lib.EINVAL
+    assert lib.ligguf_cuda_reduce_free(None) == _lib.OK
