@@ -427,6 +427,8 @@ def bench_decode(args, w, rank, world, local, pg, peaks):
         alt = "nccl" if args.gather == "p2p" else "p2p"
         other = {"gather": alt, "tokens_s": 1e3 / timed(max(3, args.steps // 2), alt)}
 
+    sara = bench_sara_layer(args, w, h, s, q, k, v, rank, world, local, pg)
+
     # end to end through the public API (pinned host buffers, copies inside the timed region)
     e2e = bench_decode_e2e(args, w, h, s, q, k, v, world, local, pg)
     h.close()
@@ -441,7 +443,74 @@ def bench_decode(args, w, rank, world, local, pg, peaks):
                      "peak_source": f"{peaks['source']} hbm_gbs (copy)"},
         "hbm_gbs_step": w.kv_bytes_per_token() * tok_s / 1e9,
         "e2e": e2e, "gpu_launches": args.steps * L * per_layer, "other_gather": other, "parity": parity,
+        "sara_layer": sara,
     }
+
+
+def bench_sara_layer(args, w, h, s, q, k, v, rank, world, local, pg):
+    """The SARA attention step with its output projection (cpp/ligguf_distrib.cpp:709-750,1025-1047):
+    per layer, the rank's shard decodes (no gather), projects its heads' output through its columns of
+    a Q8_0 attn_output (synthetic, 4096 x 4096) and the partial rows are reduced over NVLink into
+    every rank's residual.  36 layers in a CUDA graph; the same timing rules as the headline."""
+    import numpy as np
+    import torch
+    from ligguf_b200.qmat import NvlReduce, QuantMatrix, synthetic_rows
+    D, L = w.head_dim, w.n_layers
+    n_embed = w.n_heads * D
+    dev = torch.device("cuda", local)
+    col0, ncols = s["q_head0"] * D, s["q_headn"] * D
+    rows = synthetic_rows(8, n_embed, n_embed, seed=1234)
+    n_distinct = 6  # distinct attn_output matrices used in turn (the whole set exceeds L2 at N = 1)
+    mats = [QuantMatrix(8, n_embed, synthetic_rows(8, n_embed, n_embed, seed=1234 + i), local, cols=(col0, ncols))
+            for i in range(n_distinct)]
+    del rows
+    red = NvlReduce(n_embed, world, rank, local)
+    if world > 1:
+        handles = [None] * world
+        pg.all_gather_object(handles, red.ipc_handle())
+    else:
+        handles = [red.ipc_handle()]
+    red.open(handles)
+    xb = torch.empty(L, ncols, device=dev)
+    x = torch.zeros(n_embed, device=dev)
+
+    def step():
+        for l in range(L):
+            h.decode_async(l, w.pos, q[l], k[l], v[l], xb[l])
+            red.project_async(mats[l % n_distinct], xb[l])
+            red.wait_async(x_inout=x)
+    step()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    for _ in range(args.warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        pg.barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = max(3, args.steps // 2)
+    t0.record()
+    for _ in range(n):
+        g.replay()
+    t1.record()
+    torch.cuda.synchronize()
+    red.status()
+    ms = t0.elapsed_time(t1) / n
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms = float(t.item())
+        pg.barrier()
+    del g
+    red.close()
+    for m in mats:
+        m.close()
+    return {"tokens_s": 1e3 / ms, "ms_per_step": ms, "us_per_layer": ms * 1e3 / L,
+            "note": "per layer: sharded decode + Q8_0 attn_output column-slice projection with its partial rows "
+                    "stored into every rank's buffer over NVLink + reduce wait adding the rank-ordered sum to the "
+                    f"residual; CUDA-graph replay, {n} steps, max over ranks"}
 
 
 def bench_decode_e2e(args, w, h, s, q, k, v, world, local, pg):
@@ -791,6 +860,8 @@ def main():
         }
         if res.get("other_gather"):
             line["other_gather"] = res["other_gather"]
+        if res.get("sara_layer"):
+            line["sara_layer"] = res["sara_layer"]
         if cb is not None:
             line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
         if extra:
