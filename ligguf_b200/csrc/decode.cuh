@@ -214,33 +214,39 @@ __device__ __forceinline__ void norm_rope_head_tab(const float* __restrict__ src
     for (int u = 0; u < kPairs; ++u) reinterpret_cast<float2*>(dst)[lane + 32 * u] = x[u];
 }
 
-// Prologue inputs of one head, loaded early so their latency overlaps the kernel's set-up.
+// Prologue inputs of one head.  The norm weights and the rotation (sin, cos of pos * freq) do not
+// depend on the previous kernel, so they are loaded and computed before the kernel waits for it; only
+// the head's raw values are loaded after.
 template <int D>
 struct HeadIn {
     float2 x[D / 64];
     float2 gm[D / 64];
-    float fr[D / 64];  // inverse frequency of each pair (0 where no rotation)
+    float cs[D / 64], sn[D / 64];  // rotation of each pair (identity where there is none)
 };
 
 template <int D>
-__device__ __forceinline__ void head_prefetch(HeadIn<D>& in, const float* __restrict__ src,
-                                              const float* __restrict__ gamma, int norm,
-                                              const float* __restrict__ freq, int rope_pairs, int pos,
-                                              int lane) {
+__device__ __forceinline__ void head_consts(HeadIn<D>& in, const float* __restrict__ gamma, int norm,
+                                            const float* __restrict__ freq, int rope_pairs, int pos, int lane) {
 #pragma unroll
     for (int u = 0; u < D / 64; ++u) {
         const int m = lane + 32 * u;
-        in.x[u] = reinterpret_cast<const float2*>(src)[m];
         in.gm[u] = norm ? reinterpret_cast<const float2*>(gamma)[m] : make_float2(1.f, 1.f);
-        in.fr[u] = m < rope_pairs ? freq[m] : 0.f;
+        in.cs[u] = 1.f;
+        in.sn[u] = 0.f;
+        if (m < rope_pairs) sincosf(static_cast<float>(pos) * freq[m], &in.sn[u], &in.cs[u]);
     }
-    (void)pos;
+}
+
+template <int D>
+__device__ __forceinline__ void head_load(HeadIn<D>& in, const float* __restrict__ src, int lane) {
+#pragma unroll
+    for (int u = 0; u < D / 64; ++u) in.x[u] = reinterpret_cast<const float2*>(src)[lane + 32 * u];
 }
 
 // The arithmetic of norm_rope_head on prefetched inputs.
 template <int D>
-__device__ __forceinline__ void head_finish(const HeadIn<D>& in, int norm, float eps, int rope_pairs, int pos,
-                                            float* dst, int lane) {
+__device__ __forceinline__ void head_finish(const HeadIn<D>& in, int norm, float eps, int rope_pairs, float* dst,
+                                            int lane) {
     constexpr int kPairs = D / 64;
     float2 x[kPairs];
 #pragma unroll
@@ -263,11 +269,9 @@ __device__ __forceinline__ void head_finish(const HeadIn<D>& in, int norm, float
 #pragma unroll
     for (int u = 0; u < kPairs; ++u) {
         if (lane + 32 * u < rope_pairs) {
-            float sn, cs;
-            sincosf(static_cast<float>(pos) * in.fr[u], &sn, &cs);
             const float x0 = x[u].x, x1 = x[u].y;
-            x[u].x = x0 * cs - x1 * sn;
-            x[u].y = x0 * sn + x1 * cs;
+            x[u].x = x0 * in.cs[u] - x1 * in.sn[u];
+            x[u].y = x0 * in.sn[u] + x1 * in.cs[u];
         }
     }
 #pragma unroll
@@ -464,25 +468,22 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
     // The producer warp waits later (after its early copies) and never triggers: the dependent grid
     // may launch only once every CTA's consumers have seen the previous grid complete (the gather
     // wait that follows a gathered decode reads the epoch its own predecessor wrote).
+    // Consumer warps take the first prologue job (a q head, and k / v of the current token on the
+    // owner CTA): its constants before the wait, its raw values right after; the norm and rotation
+    // happen after the set-up barrier.
+    const int njobs = NREP + (owner ? 2 : 0);
+    const bool first_job = warp < kDecodeConsumerWarps && warp < njobs;
+    HeadIn<D> pin;
+    if (first_job)
+        head_consts<D>(pin, warp < NREP ? a.qg : a.kg, warp <= NREP ? a.qk_norm : 0, a.freq,
+                       warp <= NREP ? a.rope_pairs : 0, a.pos, lane);
     if (warp != kDecodeConsumerWarps) {
         asm volatile("griddepcontrol.wait;" ::: "memory");
         asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     }
-
-    // Consumer warps start loading their first prologue job (q head, and k / v of the current token
-    // on the owner CTA) right away; the norm and rotation happen after the set-up barrier.
-    const int njobs = NREP + (owner ? 2 : 0);
-    HeadIn<D> pin;
-    if (warp < kDecodeConsumerWarps && warp < njobs) {
-        if (warp < NREP)
-            head_prefetch<D>(pin, a.q + static_cast<size_t>(g * NREP + warp) * D, a.qg, a.qk_norm, a.freq,
-                             a.rope_pairs, a.pos, lane);
-        else if (warp == NREP)
-            head_prefetch<D>(pin, a.k + static_cast<size_t>(g) * D, a.kg, a.qk_norm, a.freq, a.rope_pairs,
-                             a.pos, lane);
-        else
-            head_prefetch<D>(pin, a.v + static_cast<size_t>(g) * D, nullptr, 0, a.freq, 0, a.pos, lane);
-    }
+    if (first_job)
+        head_load<D>(pin, warp < NREP ? a.q + static_cast<size_t>(g * NREP + warp) * D
+                                      : (warp == NREP ? a.k : a.v) + static_cast<size_t>(g) * D, lane);
     __syncthreads();
 
     // ------------------------------------------------------------------ producer warp
@@ -573,8 +574,7 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
         for (int job = warp; job < njobs; job += kDecodeConsumerWarps) {
             if (job == warp) {  // first round: inputs already in registers
                 float* dst = job < NREP ? q_s + job * D : (job == NREP ? kn_s : vn_s);
-                head_finish<D>(pin, job <= NREP ? a.qk_norm : 0, a.eps, job <= NREP ? a.rope_pairs : 0, a.pos,
-                               dst, lane);
+                head_finish<D>(pin, job <= NREP ? a.qk_norm : 0, a.eps, job <= NREP ? a.rope_pairs : 0, dst, lane);
             } else if (job < NREP) {
                 const int hq = g * NREP + job;
                 norm_rope_head<D>(a.q + static_cast<size_t>(hq) * D, a.qg, a.qk_norm, a.eps, a.freq,
