@@ -168,8 +168,12 @@ struct ligguf_attn {
     size_t qf_floats = 0;
     __nv_bfloat16* qb = nullptr;  // prefill bf16 q rows
     size_t qb_elems = 0;
-    __nv_bfloat16* kb = nullptr;  // bf16 shadows of one layer's K/V [n_context][kv_dim]
-    __nv_bfloat16* vb = nullptr;
+    // bf16 shadows of the K/V cache for the tensor-core prefill, per layer [n_context][kv_dim],
+    // allocated at a layer's first tensor-core prefill; d_wm[layer]: shadow rows [0, d_wm[layer])
+    // match the cache (the decode kernel, the SIMT prefill and the host writes lower it; the
+    // tensor-core prefill converts only the rows between it and pos0, then raises it).
+    std::vector<__nv_bfloat16*> kb, vb;
+    int* d_wm = nullptr;
     alignas(64) CUtensorMap tm_k;
     alignas(64) CUtensorMap tm_v;
     // SARA gather over CUDA IPC
@@ -273,6 +277,15 @@ void note_cache_write(ligguf_attn* h, int layer0, int n_layers, int row0) {
     h->wr_row0 = row0;
 }
 
+// A host-side write of cache rows from row0 up in layers [layer0, +n_layers): the bf16 shadows of
+// those rows are stale.  On the handle's stream, then waited for (the callers are synchronous).
+int lower_shadow_marks(ligguf_attn* h, int layer0, int n_layers, int row0) {
+    lg::shadow_lower_kernel<<<1, 256, 0, h->stream>>>(h->d_wm + layer0, n_layers, row0);
+    LG_CUDA(cudaGetLastError());
+    LG_CUDA(cudaStreamSynchronize(h->stream));
+    return LIGGUF_ATTN_OK;
+}
+
 int decode_enqueue(ligguf_attn* h, int layer, int pos, const float* dq, const float* dk, const float* dv,
                    float* dout, cudaStream_t st, bool gather) {
     const ligguf_attn_cfg& c = h->cfg;
@@ -297,6 +310,7 @@ int decode_enqueue(ligguf_attn* h, int layer, int pos, const float* dq, const fl
     a.gpart = h->gpart;
     a.counters = h->counters;
     a.err = h->d_err;
+    a.shadow_wm = h->d_wm + layer;
     a.row0 = layer * c.n_context;
     a.pos = pos;
     const int tp = decode_tile_rows(c.kv_type, D);
@@ -494,6 +508,7 @@ int prefill_enqueue(ligguf_attn* h, int layer, int pos0, int n, const float* dq,
     p.rope_pairs = h->rope_pairs;
     p.qk_norm = c.qk_norm;
     p.eps = c.rms_epsilon;
+    p.wm = h->d_wm + layer;
     const bool div = c.scale_mode == LIGGUF_SCALE_DIV;
     const float scale = div ? sqrtf(static_cast<float>(D)) : 1.0f / sqrtf(static_cast<float>(D));
 
@@ -530,34 +545,34 @@ int prefill_enqueue(ligguf_attn* h, int layer, int pos0, int n, const float* dq,
         }
     }
 
-    // Tensor-core path: bf16 q rows, bf16 K/V shadow rows [0, pos0+n) of this layer.
+    // Tensor-core path: bf16 q rows, this layer's bf16 K/V shadow rows [0, pos0+n).
     int rc = grow(&h->qb, &h->qb_elems, qn);
     if (rc) return rc;
-    if (!h->kb) {
+    if (!h->kb[layer]) {
         const size_t bytes = size_t(c.n_context) * h->kv_dim * sizeof(__nv_bfloat16);
-        if (cudaMalloc(&h->kb, bytes) != cudaSuccess || cudaMalloc(&h->vb, bytes) != cudaSuccess)
+        if (cudaMalloc(&h->kb[layer], bytes) != cudaSuccess || cudaMalloc(&h->vb[layer], bytes) != cudaSuccess)
             return fail(LIGGUF_ATTN_ENOMEM, "bf16 K/V shadow allocation failed");
     }
     p.qb = h->qb;
-    p.kb = h->kb;
-    p.vb = h->vb;
-    if (pos0 > 0) {  // earlier positions of the cache -> bf16 shadow
-        const size_t cnt = size_t(pos0) * h->kv_dim;
-        const int blocks = std::min(4 * h->num_sms, std::max(1, ceil_div(cnt, 256)));
+    p.kb = h->kb[layer];
+    p.vb = h->vb[layer];
+    if (pos0 > 0) {  // cache rows written since the shadows last matched -> bf16
+        const int blocks = std::min(4 * h->num_sms, std::max(1, ceil_div(size_t(pos0) * h->kv_dim, 256)));
         switch (c.kv_type) {
             case LIGGUF_KV_F32:
-                lg::cache_to_bf16_kernel<float><<<blocks, 256, 0, st>>>(static_cast<const float*>(p.kc), h->kb, cnt);
-                lg::cache_to_bf16_kernel<float><<<blocks, 256, 0, st>>>(static_cast<const float*>(p.vc), h->vb, cnt);
+                lg::shadow_sync_kernel<float><<<blocks, 256, 0, st>>>(static_cast<const float*>(p.kc),
+                                                                      static_cast<const float*>(p.vc), p.kb, p.vb,
+                                                                      h->kv_dim, p.wm, pos0);
                 break;
             case LIGGUF_KV_F16:
-                lg::cache_to_bf16_kernel<__half><<<blocks, 256, 0, st>>>(static_cast<const __half*>(p.kc), h->kb, cnt);
-                lg::cache_to_bf16_kernel<__half><<<blocks, 256, 0, st>>>(static_cast<const __half*>(p.vc), h->vb, cnt);
+                lg::shadow_sync_kernel<__half><<<blocks, 256, 0, st>>>(static_cast<const __half*>(p.kc),
+                                                                       static_cast<const __half*>(p.vc), p.kb, p.vb,
+                                                                       h->kv_dim, p.wm, pos0);
                 break;
             default:
-                lg::cache_to_bf16_kernel<__nv_bfloat16>
-                    <<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(p.kc), h->kb, cnt);
-                lg::cache_to_bf16_kernel<__nv_bfloat16>
-                    <<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(p.vc), h->vb, cnt);
+                lg::shadow_sync_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
+                    static_cast<const __nv_bfloat16*>(p.kc), static_cast<const __nv_bfloat16*>(p.vc), p.kb, p.vb,
+                    h->kv_dim, p.wm, pos0);
                 break;
         }
         LG_CUDA(cudaGetLastError());
@@ -570,8 +585,8 @@ int prefill_enqueue(ligguf_attn* h, int layer, int pos0, int n, const float* dq,
     if (rc) return rc;
     lg::TcArgs t = {};
     t.q = h->qb;
-    t.k = h->kb;
-    t.v = h->vb;
+    t.k = p.kb;
+    t.v = p.vb;
     t.out = dout;
     t.q_rows = n;
     t.q_heads = h->q_headn;
@@ -677,9 +692,12 @@ int ligguf_cuda_attn_free(ligguf_attn* h) {
     for (void* p : h->g_opened)
         if (p) cudaIpcCloseMemHandle(p);
     void* dev_ptrs[] = {h->kc, h->vc, h->freq, h->qg, h->kg, h->part, h->gpart, h->counters, h->d_stage, h->qf, h->qb,
-                        h->kb, h->vb, h->gbuf, h->d_peer_ll, h->d_gstate};
+                        h->d_wm, h->gbuf, h->d_peer_ll, h->d_gstate};
     for (void* p : dev_ptrs)
         if (p) cudaFree(p);
+    for (auto* v : {&h->kb, &h->vb})
+        for (__nv_bfloat16* p : *v)
+            if (p) cudaFree(p);
     if (h->h_err) cudaFreeHost(h->h_err);
     if (h->h_stage) cudaFreeHost(h->h_stage);
     if (h->stream) cudaStreamDestroy(h->stream);
@@ -758,10 +776,14 @@ int ligguf_cuda_attn_init(const ligguf_attn_cfg* cfg, ligguf_attn** out) {
     if (cudaMalloc(&h->freq, nfreq * 4) != cudaSuccess || cudaMalloc(&h->qg, pd * 4) != cudaSuccess ||
         cudaMalloc(&h->kg, pd * 4) != cudaSuccess || cudaMalloc(&h->part, part_floats * 4) != cudaSuccess ||
         cudaMalloc(&h->gpart, gpart_floats * 4) != cudaSuccess ||
-        cudaMalloc(&h->counters, n_counters * sizeof(int)) != cudaSuccess)
+        cudaMalloc(&h->counters, n_counters * sizeof(int)) != cudaSuccess ||
+        cudaMalloc(&h->d_wm, size_t(c.n_layers) * sizeof(int)) != cudaSuccess)
         return bail(fail(LIGGUF_ATTN_ENOMEM, "handle buffers"));
+    h->kb.assign(c.n_layers, nullptr);
+    h->vb.assign(c.n_layers, nullptr);
     if (cudaMemcpy(h->freq, freq.data(), nfreq * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemset(h->counters, 0, n_counters * sizeof(int)) != cudaSuccess)
+        cudaMemset(h->counters, 0, n_counters * sizeof(int)) != cudaSuccess ||
+        cudaMemset(h->d_wm, 0, size_t(c.n_layers) * sizeof(int)) != cudaSuccess)
         return bail(fail(LIGGUF_ATTN_ECUDA, "handle initialisation copies"));
     if (cudaHostAlloc(&h->h_err, 64, cudaHostAllocMapped) != cudaSuccess ||
         cudaHostGetDevicePointer(reinterpret_cast<void**>(&h->d_err), h->h_err, 0) != cudaSuccess)
@@ -890,6 +912,7 @@ int ligguf_cuda_attn_kv_upload(ligguf_attn* h, int layer, int pos0, int n, const
     const size_t bytes = size_t(n) * h->kv_dim * h->es;
     LG_CUDA(cudaStreamSynchronize(h->stream));
     note_cache_write(h, layer, 1, pos0);
+    if (int rc = lower_shadow_marks(h, layer, 1, pos0)) return rc;
     LG_CUDA(cudaMemcpy(static_cast<char*>(h->kc) + off, host_k, bytes, cudaMemcpyHostToDevice));
     LG_CUDA(cudaMemcpy(static_cast<char*>(h->vc) + off, host_v, bytes, cudaMemcpyHostToDevice));
     return LIGGUF_ATTN_OK;
@@ -997,6 +1020,7 @@ int ligguf_cuda_attn_state_load(ligguf_attn* h, const char* path, int* pos_out, 
     if (fread(lg.data(), n_logits * sizeof(float), 1, f) != 1) return bad("short read of the logits");
     fclose(f);
     note_cache_write(h, 0, h->cfg.n_layers, 0);
+    if (int rc = lower_shadow_marks(h, 0, h->cfg.n_layers, 0)) return rc;
     std::memcpy(logits, lg.data(), n_logits * sizeof(float));
     if (pos_out) *pos_out = hdr.pos;
     if (n_context_out) *n_context_out = hdr.n_context;
@@ -1013,6 +1037,7 @@ int ligguf_cuda_attn_kv_synth(ligguf_attn* h, int layer0, int n_layers, int pos0
     const float mul = synth_mul(scale);
     const int kv_off = h->cfg.kv_head0 * h->cfg.head_dim;
     note_cache_write(h, layer0, n_layers, pos0);
+    if (int rc = lower_shadow_marks(h, layer0, n_layers, pos0)) return rc;
     const size_t total = size_t(n) * h->kv_dim;
     const int blocks = std::min(8 * h->num_sms, std::max(1, ceil_div(total, 256)));
     for (int l = layer0; l < layer0 + n_layers && n > 0; ++l) {

@@ -65,6 +65,7 @@ struct DecodeArgs {
     int* counters;      // [kv_headn] head tickets, then [kv_headn] grab counters, then
                         // [kv_headn][kDecodeMaxGroups] group tickets; zero between launches
     int* err;           // error word (mapped host memory)
+    int* shadow_wm;     // the layer's bf16-shadow watermark (tensor-core prefill): lowered to pos
     unsigned long long* const* peer_ll;  // multi-GPU gather (or null): [2][nranks] gather slots of
                                          // [n_heads*D] words, slot = call epoch & 1
     int nranks;
@@ -595,6 +596,7 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
             krow[d] = KvTraits<KV>::from_float(kn_s[d]);
             vrow[d] = KvTraits<KV>::from_float(vn_s[d]);
         }
+        if (tid == 0 && a.shadow_wm) atomicMin(a.shadow_wm, a.pos);
     }
 
     const int r = lane / LPR, j = lane % LPR;

@@ -239,6 +239,7 @@ struct PrepArgs {
     __nv_bfloat16* qb;  // [n][q_headn*D] bf16 out (or null)
     __nv_bfloat16* kb;  // [n_context][kv_dim] bf16 key shadow, rows by absolute position (or null)
     __nv_bfloat16* vb;
+    int* wm;            // the layer's shadow watermark: shadow rows [0, *wm) equal the cache rows
     int n, pos0, q_headn, kv_headn, kv_dim, rope_pairs, qk_norm;
     float eps;
 };
@@ -342,6 +343,10 @@ __global__ void __launch_bounds__(kPrepWarps * 32) prefill_prep_kernel(const Pre
     }
     for (int m = threadIdx.x; m < a.rope_pairs; m += blockDim.x)
         sincosf(static_cast<float>(pos) * a.freq[m], &sn[m], &cs[m]);
+    // Watermark: with shadows, rows [0, pos0) were brought up to date by shadow_sync_kernel and this
+    // grid writes [pos0, pos0 + n) to both; without, the cache rows from pos0 up change under them.
+    if (a.wm && i == 0 && blockIdx.y == 0 && threadIdx.x == 0)
+        *a.wm = a.kb ? max(*a.wm, a.pos0 + a.n) : min(*a.wm, a.pos0);
     __syncthreads();
     if (!active) return;
     if (is_q) {
@@ -358,12 +363,23 @@ __global__ void __launch_bounds__(kPrepWarps * 32) prefill_prep_kernel(const Pre
     if (shadow) store_vec16<__nv_bfloat16, E>(shadow + o, x);
 }
 
-// Cache rows [0, n_rows) of one layer -> bf16 shadow (tensor-core prefill over earlier positions).
+// Before a tensor-core prefill at pos0: the layer's cache rows [min(*wm, pos0), pos0) -> its bf16
+// shadows, i.e. only the rows written since the shadows last matched the cache (none when a prompt
+// is prefilled chunk after chunk with nothing else writing the cache in between).
 template <typename KV>
-__global__ void cache_to_bf16_kernel(const KV* __restrict__ src, __nv_bfloat16* __restrict__ dst,
-                                     size_t n) {
-    for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x)
-        dst[i] = __float2bfloat16_rn(KvTraits<KV>::to_float(src[i]));
+__global__ void shadow_sync_kernel(const KV* __restrict__ kc, const KV* __restrict__ vc, __nv_bfloat16* __restrict__ kb,
+                                   __nv_bfloat16* __restrict__ vb, int kv_dim, const int* __restrict__ wm, int pos0) {
+    const size_t end = size_t(pos0) * kv_dim;
+    for (size_t i = size_t(min(*wm, pos0)) * kv_dim + blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < end;
+         i += size_t(gridDim.x) * blockDim.x) {
+        kb[i] = __float2bfloat16_rn(KvTraits<KV>::to_float(kc[i]));
+        vb[i] = __float2bfloat16_rn(KvTraits<KV>::to_float(vc[i]));
+    }
+}
+
+// Cache rows from row0 up of layers [0, n) changed outside the shadows' writers: lower their marks.
+__global__ void shadow_lower_kernel(int* wm, int n, int row0) {
+    for (int l = threadIdx.x; l < n; l += blockDim.x) wm[l] = min(wm[l], row0);
 }
 
 }  // namespace lg

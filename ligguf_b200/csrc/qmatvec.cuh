@@ -50,10 +50,13 @@ __host__ __device__ constexpr bool qt_uses_q8k(int t) { return t >= QT_Q2_K && t
 __host__ __device__ constexpr bool qt_uses_q80(int t) { return t == QT_Q8_0 || t == QT_Q1_0 || t == QT_Q1_G; }
 __host__ __device__ constexpr bool qt_uses_f32(int t) { return t == QT_F32 || t == QT_F16; }
 
-constexpr int kQmvWarps = 8;                        // consumer warps
+// 7 consumer warps + 1 producer warp, two CTAs per SM (14 consumer warps per SM; the consumers are
+// latency-bound, so resident warps are what sets the pace).  The ring depth (2..4 stages of up to
+// 32 KB) is chosen per launch so that two CTAs fit an SM's shared memory.
+constexpr int kQmvWarps = 7;                        // consumer warps
 constexpr int kQmvThreads = (kQmvWarps + 1) * 32;   // + the producer warp
-constexpr int kQmvStages = 4;
-constexpr int kQmvStageMax = 40 * 1024;              // bytes of one ring stage (a tile of rows)
+constexpr int kQmvMaxStages = 4;
+constexpr int kQmvStageMax = 32 * 1024;              // bytes of one ring stage (a tile of rows)
 constexpr int kQmvMaxN = 16384;                      // input width limit (activation in shared memory)
 constexpr int kQmvMaxMats = 3;
 constexpr int kQmvMaxTokens = 8;                     // x rows per launch
@@ -95,6 +98,7 @@ struct QmvArgs {
     int n;
     int need_k, need_0, need_f;
     int ntiles;      // over all matrices
+    int stages;      // ring depth, 2..kQmvMaxStages
     QmvAct act;
     int* err;
 };
@@ -111,12 +115,8 @@ __device__ __forceinline__ int nearest_int_ref(float f) {
 // division); q = min(127, nearest_int(iscale*x)); d = max * (-1/127), the form the reference's
 // -Ofast build computes 1/iscale in (checked against the compiled reference).  Writes q, d and the
 // 16 sums of 16 to the given destinations (q and sums indexed within the block).
-__device__ __forceinline__ void q8k_block_warp(const float* __restrict__ x, int8_t* q, float* d, int* bs_int,
-                                               int16_t* bs_i16, int lane) {
-    float v[8];
-    const float4 a = reinterpret_cast<const float4*>(x)[2 * lane];
-    const float4 b = reinterpret_cast<const float4*>(x)[2 * lane + 1];
-    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+__device__ __forceinline__ void q8k_block_vals(const float (&v)[8], int8_t* q, float* d, int* bs_int, int16_t* bs_i16,
+                                               int lane) {
     float amax = 0.f, mx = 0.f;
     int idx = 1 << 30;
 #pragma unroll
@@ -165,6 +165,13 @@ __device__ __forceinline__ void q8k_block_warp(const float* __restrict__ x, int8
         if (bs_i16) bs_i16[lane >> 1] = static_cast<int16_t>(s16);
     }
     if (lane == 0) *d = amax == 0.f ? 0.f : __fmul_rn(mx, -1.0f / 127.0f);
+}
+__device__ __forceinline__ void q8k_block_warp(const float* __restrict__ x, int8_t* q, float* d, int* bs_int,
+                                               int16_t* bs_i16, int lane) {
+    const float4 a = reinterpret_cast<const float4*>(x)[2 * lane];
+    const float4 b = reinterpret_cast<const float4*>(x)[2 * lane + 1];
+    const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    q8k_block_vals(v, q, d, bs_int, bs_i16, lane);
 }
 
 // One 32-element block of quantize_q8_0 (fast/lil_math.cpp:329-350) by one warp, lane = element:
@@ -566,17 +573,18 @@ __device__ __forceinline__ int qmv_find_mat(const QmvArgs& a, int t) {
 }
 
 template <int T>
-__global__ void __launch_bounds__(kQmvThreads, 1) qmv_kernel(const __grid_constant__ QmvArgs a) {
+__global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const __grid_constant__ QmvArgs a) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t* ring = smem + a.act.bytes;
-    __shared__ uint64_t full[kQmvStages], empty[kQmvStages];
+    __shared__ uint64_t full[kQmvMaxStages], empty[kQmvMaxStages];
+    const int S = a.stages;
     __shared__ int abort_s;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int t_begin = int((long long)blockIdx.x * a.ntiles / gridDim.x);
     const int t_end = int((long long)(blockIdx.x + 1) * a.ntiles / gridDim.x);
     const uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
     if (tid == 0) {
-        for (int s = 0; s < kQmvStages; ++s) {
+        for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kQmvWarps);
         }
@@ -589,9 +597,9 @@ __global__ void __launch_bounds__(kQmvThreads, 1) qmv_kernel(const __grid_consta
         if (lane == 0) {
             int issued = 0;
             for (int t = t_begin, it = 0; t < t_end; ++t, ++it) {
-                const int s = it % kQmvStages;
-                if (it >= kQmvStages &&
-                    !mbar_wait_bounded(&empty[s], ((it / kQmvStages) - 1) & 1, deadline, &abort_s)) {
+                const int s = it % S;
+                if (it >= S &&
+                    !mbar_wait_bounded(&empty[s], ((it / S) - 1) & 1, deadline, &abort_s)) {
                     abort_s = 1;
                     *reinterpret_cast<volatile int*>(a.err) = KERR_TIMEOUT_EMPTY;
                     break;
@@ -606,8 +614,8 @@ __global__ void __launch_bounds__(kQmvThreads, 1) qmv_kernel(const __grid_consta
             }
             // the copies must land before the CTA exits (bounded, past the consumers' deadline)
             const uint64_t dd = deadline + kWaitLimitNs / 2;
-            for (int u = max(0, issued - kQmvStages); u < issued; ++u)
-                while (!mbar_try_wait(&full[u % kQmvStages], (u / kQmvStages) & 1) && globaltimer_ns() < dd) {
+            for (int u = max(0, issued - S); u < issued; ++u)
+                while (!mbar_try_wait(&full[u % S], (u / S) & 1) && globaltimer_ns() < dd) {
                 }
         }
         return;
@@ -616,32 +624,77 @@ __global__ void __launch_bounds__(kQmvThreads, 1) qmv_kernel(const __grid_consta
     // ------------------------------------------------------------------------- consumers
     asm volatile("griddepcontrol.wait;" ::: "memory");  // x comes from the previous kernel
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    for (int t = 0; t < a.n_tok; ++t) {
-        const float* x = a.x + t * a.x_stride;
-        uint8_t* tb = smem + size_t(t) * a.act.tok_bytes;
-        if (a.need_k)
-            for (int b = warp; b < a.n / 256; b += kQmvWarps)
-                q8k_block_warp(x + 256 * b, reinterpret_cast<int8_t*>(tb + a.act.off_qk) + 256 * b,
-                               reinterpret_cast<float*>(tb + a.act.off_dk) + b,
-                               reinterpret_cast<int*>(tb + a.act.off_bs) + 16 * b, nullptr, lane);
-        if (a.need_0)
-            for (int b = warp; b < a.n / 32; b += kQmvWarps) {
-                uint16_t dh;
-                const int q = q80_block_warp(x[32 * b + lane], &dh, lane);
-                reinterpret_cast<int8_t*>(tb + a.act.off_q0)[32 * b + lane] = static_cast<int8_t>(q);
-                if (lane == 0) reinterpret_cast<float*>(tb + a.act.off_d0)[b] = h2f(dh);
+    // Quantize every token's x.  Work items are (token, block) pairs dealt round-robin to the warps;
+    // each warp first issues the loads of a batch of its items (x is read from L2 once), then
+    // quantizes them, so the load latency is paid once per batch rather than once per block.
+    if (a.need_k) {
+        constexpr int kB = 4;  // Q8_K blocks per batch: 8 loads of 16 bytes per lane in flight
+        const int nb = a.n / 256, items = nb * a.n_tok;
+        for (int i0 = warp; i0 < items; i0 += kQmvWarps * kB) {
+            float v[kB][8];
+#pragma unroll
+            for (int j = 0; j < kB; ++j) {
+                const int it = i0 + j * kQmvWarps;
+                if (it < items) {
+                    const float4* src = reinterpret_cast<const float4*>(a.x + (it / nb) * a.x_stride + 256 * (it % nb));
+                    const float4 p = src[2 * lane], q = src[2 * lane + 1];
+                    v[j][0] = p.x; v[j][1] = p.y; v[j][2] = p.z; v[j][3] = p.w;
+                    v[j][4] = q.x; v[j][5] = q.y; v[j][6] = q.z; v[j][7] = q.w;
+                }
             }
-        if (a.need_f)
-            for (int i = warp * 32 + lane; i < a.n; i += kQmvWarps * 32)
-                reinterpret_cast<float*>(tb + a.act.off_xf)[i] = x[i];
+#pragma unroll
+            for (int j = 0; j < kB; ++j) {
+                const int it = i0 + j * kQmvWarps;
+                if (it < items) {
+                    const int t = it / nb, b = it % nb;
+                    uint8_t* tb = smem + size_t(t) * a.act.tok_bytes;
+                    q8k_block_vals(v[j], reinterpret_cast<int8_t*>(tb + a.act.off_qk) + 256 * b,
+                                   reinterpret_cast<float*>(tb + a.act.off_dk) + b,
+                                   reinterpret_cast<int*>(tb + a.act.off_bs) + 16 * b, nullptr, lane);
+                }
+            }
+        }
+    }
+    if (a.need_0) {
+        constexpr int kB = 16;  // Q8_0 blocks per batch: one 4-byte load per lane each
+        const int nb = a.n / 32, items = nb * a.n_tok;
+        for (int i0 = warp; i0 < items; i0 += kQmvWarps * kB) {
+            float v[kB];
+#pragma unroll
+            for (int j = 0; j < kB; ++j) {
+                const int it = i0 + j * kQmvWarps;
+                v[j] = it < items ? a.x[(it / nb) * a.x_stride + 32 * (it % nb) + lane] : 0.f;
+            }
+#pragma unroll
+            for (int j = 0; j < kB; ++j) {
+                const int it = i0 + j * kQmvWarps;
+                if (it < items) {
+                    const int t = it / nb, b = it % nb;
+                    uint8_t* tb = smem + size_t(t) * a.act.tok_bytes;
+                    uint16_t dh;
+                    const int q = q80_block_warp(v[j], &dh, lane);
+                    reinterpret_cast<int8_t*>(tb + a.act.off_q0)[32 * b + lane] = static_cast<int8_t>(q);
+                    if (lane == 0) reinterpret_cast<float*>(tb + a.act.off_d0)[b] = h2f(dh);
+                }
+            }
+        }
+    }
+    if (a.need_f) {
+        const int n4 = a.n / 4;
+        for (int t = 0; t < a.n_tok; ++t) {
+            const float4* x = reinterpret_cast<const float4*>(a.x + t * a.x_stride);
+            float4* dst = reinterpret_cast<float4*>(smem + size_t(t) * a.act.tok_bytes + a.act.off_xf);
+#pragma unroll 4
+            for (int i = warp * 32 + lane; i < n4; i += kQmvWarps * 32) dst[i] = x[i];
+        }
     }
     named_bar_sync(1, kQmvWarps * 32);
     const int epoch = a.red.peers ? __ldcg(a.red.state) + 1 : 0;
 
     const int units = a.n / 32;
     for (int t = t_begin, it = 0; t < t_end; ++t, ++it) {
-        const int s = it % kQmvStages;
-        const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (it / kQmvStages) & 1, deadline, &abort_s));
+        const int s = it % S;
+        const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (it / S) & 1, deadline, &abort_s));
         if (!ok) {
             if (lane == 0) {
                 abort_s = 1;

@@ -107,3 +107,48 @@ def test_prefill_full_size_vs_reference(gpu):
             assert cases.rel_err(o, ref[i]) <= TOL_SIMT, i
     d.close()
     h.close()
+
+
+def test_prefill_tc_chunks_reuse_and_refresh_the_bf16_shadow(gpu):
+    """The tensor-core path keeps a bf16 copy of each layer's cache and converts only the rows written
+    since it last matched: a prompt prefilled in chunks equals the one-call result, and every other
+    writer of the cache (a decode at an earlier position, a host upload, a SIMT prefill) makes the next
+    tensor-core call see the new rows.  The SIMT path on the same handle reads the cache itself and is
+    the yardstick."""
+    from ligguf_b200 import AttnConfig, CudaAttention
+    H, Hk, D, n_ctx = 16, 4, 128, 512
+    c = cases.prefill_case(H=H, Hk=Hk, D=D, n_ctx=n_ctx, theta=1e6, qk_norm=1, pos0=0, n=300, seed=91)
+    ref, _, _ = cases.run_prefill(orc.Checker("port"), c)
+    cfg = AttnConfig(n_layers=1, n_heads=H, n_kv_heads=Hk, head_dim=D, n_context=n_ctx, rope_dim=D,
+                     rope_base=c["theta"], rms_epsilon=c["eps"], qk_norm=True)
+    h = CudaAttention(cfg)
+    h.set_qk_norm(0, c["qg"], c["kg"])
+    outs = [h.prefill(0, p, c["q"][p:p + 100], c["k"][p:p + 100], c["v"][p:p + 100], 1) for p in (0, 100, 200)]
+    assert cases.rel_err(np.concatenate(outs), ref) <= TOL_TC
+
+    rng = np.random.default_rng(3)
+    kv_dim = Hk * D
+
+    def tc_vs_simt(p, n):
+        q = rng.standard_normal((n, H * D)).astype(np.float32)
+        k = rng.standard_normal((n, kv_dim)).astype(np.float32)
+        v = rng.standard_normal((n, kv_dim)).astype(np.float32)
+        tc = h.prefill(0, p, q, k, v, 1)
+        simt = h.prefill(0, p, q, k, v, 0)  # rewrites the same rows with the same values
+        return cases.rel_err(tc, simt)
+
+    # a decode at an earlier position (a backtrack) with a value row that dominates the sums
+    q1 = rng.standard_normal(H * D).astype(np.float32)
+    k1 = rng.standard_normal(kv_dim).astype(np.float32)
+    h.decode(0, 120, q1, k1, 1e3 * rng.standard_normal(kv_dim).astype(np.float32))
+    assert tc_vs_simt(300, 40) <= TOL_TC
+    # a host upload of earlier rows
+    kk, vv = h.kv_download(0, 10, 50)
+    h.kv_upload(0, 10, kk * 3, vv * 50)
+    assert tc_vs_simt(340, 40) <= TOL_TC
+    # a SIMT prefill over earlier rows, then a tensor-core call behind it
+    q2 = rng.standard_normal((30, H * D)).astype(np.float32)
+    k2 = rng.standard_normal((30, kv_dim)).astype(np.float32)
+    h.prefill(0, 200, q2, k2, 30 * rng.standard_normal((30, kv_dim)).astype(np.float32), 0)
+    assert tc_vs_simt(380, 40) <= TOL_TC
+    h.close()
