@@ -41,7 +41,8 @@ def parse_args():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--gather", choices=["p2p", "nccl"], default="p2p",
                     help="N>1: all-gather of head outputs by the decode kernel's peer stores (p2p, default) or NCCL")
-    ap.add_argument("--case", choices=["decode-layer", "prefill-layer", "bert-layer"], default=None,
+    ap.add_argument("--case", choices=["decode-layer", "decode-4k-layer", "prefill-layer", "bert-layer", "qkv-layer"],
+                    default=None,
                     help="run one small case a few times and exit (the command the ncu summaries use)")
     return ap.parse_args()
 
@@ -778,7 +779,7 @@ def run_case(case: str, reps: int = 3):
     import numpy as np
     import torch
     from ligguf_b200 import AttnConfig, CudaAttention, CudaBertAttention, synth_fill
-    from ligguf_b200.workloads import BERT_BASE, QWEN3_DECODE_32K, QWEN3_PREFILL
+    from ligguf_b200.workloads import BERT_BASE, QWEN3_DECODE_4K, QWEN3_DECODE_32K, QWEN3_PREFILL
     dev = torch.device("cuda", 0)
     g = np.ones(128, dtype=np.float32)
     if case == "decode-layer":  # qwen3_8b_decode_32k shapes, 2 layers of cache (537 MB), layer 0
@@ -794,6 +795,43 @@ def run_case(case: str, reps: int = 3):
             synth_fill(x, x.numel(), w.seed, t << 32, 0, w.scale)
         for _ in range(reps):
             h.decode_async(0, w.pos, q, k, v, out)
+    elif case == "decode-4k-layer":
+        # qwen3_8b_decode_4k shapes, 8 layers of cache (268 MB, more than L2), two passes over the
+        # layers: a launch of the second pass reads a layer that 7 others have since evicted.
+        w = QWEN3_DECODE_4K
+        L = 8
+        h = CudaAttention(AttnConfig(n_layers=L, n_heads=w.n_heads, n_kv_heads=w.n_kv_heads, head_dim=w.head_dim,
+                                     n_context=w.n_context, rope_dim=w.rope_dim, rope_base=w.rope_base,
+                                     rms_epsilon=w.eps, qk_norm=True))
+        for l in range(L):
+            h.set_qk_norm(l, g, g)
+        h.kv_synth(0, L, 0, w.pos, w.seed, w.scale)
+        q, k, v = torch.empty(w.q_dim, device=dev), torch.empty(w.kv_dim, device=dev), torch.empty(w.kv_dim, device=dev)
+        out = torch.empty(w.q_dim, device=dev)
+        for t, x in ((3, q), (4, k), (5, v)):
+            synth_fill(x, x.numel(), w.seed, t << 32, 0, w.scale)
+        for _ in range(2):
+            for l in range(L):
+                h.decode_async(l, w.pos, q, k, v, out)
+    elif case == "qkv-layer":
+        # the Qwen3-8B Q8_0 QKV projection of one decode token over 12 distinct weight sets (321 MB,
+        # more than L2), two passes: a launch of the second pass reads weights that 11 others have
+        # since evicted
+        from ligguf_b200.qmat import QT, QuantMatrix, matmul3_async, synthetic_rows
+        n, dims = 4096, (4096, 1024, 1024)
+        mats = [[QuantMatrix(QT["Q8_0"], n, synthetic_rows(QT["Q8_0"], n, d, seed=97 * i + j), 0)
+                 for j, d in enumerate(dims)] for i in range(12)]
+        x = torch.randn(n, device=dev)
+        outs = [torch.empty(d, device=dev) for d in dims]
+        for _ in range(2):
+            for m in mats:
+                matmul3_async(m[0], m[1], m[2], x, *outs)
+        torch.cuda.synchronize()
+        for m in mats:
+            for w_ in m:
+                w_.close()
+        print(f"case {case}: ok")
+        return 0
     elif case == "prefill-layer":  # qwen3_8b_prefill_2048, one layer, tensor-core path
         w = QWEN3_PREFILL
         h = CudaAttention(AttnConfig(n_layers=1, n_heads=w.n_heads, n_kv_heads=w.n_kv_heads, head_dim=w.head_dim,
