@@ -384,7 +384,7 @@ int launch_flash_simt(const lg::FlashArgs& f, int D, dim3 grid, cudaStream_t st,
 
 template <typename KV, int D>
 int launch_prep_t(const lg::PrepArgs& p, cudaStream_t st) {
-    const dim3 grid(p.n, ceil_div(p.q_headn + 2 * p.kv_headn, lg::kPrepWarps));
+    const dim3 grid(p.n, ceil_div(p.q_headn + 2 * p.kv_headn, lg::kPrepWarps * lg::kPrepJobs));
     lg::prefill_prep_kernel<KV, D><<<grid, lg::kPrepWarps * 32, 0, st>>>(p);
     LG_CUDA(cudaGetLastError());
     return LIGGUF_ATTN_OK;

@@ -316,11 +316,15 @@ __device__ __forceinline__ void norm_rope_vec(float (&x)[D / 32], const float* _
 }
 
 // Prompt rows before attention: per token, the q heads (norm + RoPE; fp32 and/or bf16 out), the k
-// heads (norm + RoPE) and the v heads into this layer's cache rows (and their bf16 shadow).  One warp
-// per head: block (token, group of kPrepWarps heads), each lane holding E = D/32 consecutive elements
-// (one 16- or 8-byte load).  The row is loaded before the token's cos/sin table is computed into
-// shared memory, so the load's latency overlaps that computation and the block barrier.
+// heads (norm + RoPE) and the v heads into this layer's cache rows (and their bf16 shadow).  Three
+// heads per warp: block (token, group of 3 * kPrepWarps heads: all 48 of a Qwen3-8B token), warp w
+// taking heads w, w + kPrepWarps and w + 2 * kPrepWarps of the group, each lane holding E = D/32
+// consecutive elements of each (one 16- or 8-byte load per head).  All the rows are loaded before
+// the token's cos/sin table is computed into shared memory, so their latency overlaps that
+// computation and the block barrier; three loads per lane in flight instead of one (the kernel is
+// bound by the bytes each SM keeps in flight).
 constexpr int kPrepWarps = 16;
+constexpr int kPrepJobs = 3;  // heads per warp
 template <typename KV, int D>
 __global__ void __launch_bounds__(kPrepWarps * 32) prefill_prep_kernel(const PrepArgs a) {
     // Launched in stream order (its predecessor has completed); the tensor-core kernel that follows
@@ -331,15 +335,18 @@ __global__ void __launch_bounds__(kPrepWarps * 32) prefill_prep_kernel(const Pre
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int i = blockIdx.x;
     const int pos = a.pos0 + i;
-    const int job = blockIdx.y * kPrepWarps + warp;
-    const bool active = job < a.q_headn + 2 * a.kv_headn;
-    const bool is_q = job < a.q_headn, is_k = !is_q && job < a.q_headn + a.kv_headn;
-    const int gi = is_q ? job : (is_k ? job - a.q_headn : job - a.q_headn - a.kv_headn);
-    float x[E];
-    if (active) {
-        const float* src = is_q ? a.q + (static_cast<size_t>(i) * a.q_headn + gi) * D
-                                : (is_k ? a.k : a.v) + (static_cast<size_t>(i) * a.kv_headn + gi) * D;
-        load_vec<E>(src + lane * E, x);
+    const int n_jobs = a.q_headn + 2 * a.kv_headn;
+    float x[kPrepJobs][E];
+#pragma unroll
+    for (int jj = 0; jj < kPrepJobs; ++jj) {
+        const int job = blockIdx.y * kPrepWarps * kPrepJobs + jj * kPrepWarps + warp;
+        if (job < n_jobs) {
+            const bool is_q = job < a.q_headn, is_k = !is_q && job < a.q_headn + a.kv_headn;
+            const int gi = is_q ? job : (is_k ? job - a.q_headn : job - a.q_headn - a.kv_headn);
+            const float* src = is_q ? a.q + (static_cast<size_t>(i) * a.q_headn + gi) * D
+                                    : (is_k ? a.k : a.v) + (static_cast<size_t>(i) * a.kv_headn + gi) * D;
+            load_vec<E>(src + lane * E, x[jj]);
+        }
     }
     for (int m = threadIdx.x; m < a.rope_pairs; m += blockDim.x)
         sincosf(static_cast<float>(pos) * a.freq[m], &sn[m], &cs[m]);
@@ -348,19 +355,25 @@ __global__ void __launch_bounds__(kPrepWarps * 32) prefill_prep_kernel(const Pre
     if (a.wm && i == 0 && blockIdx.y == 0 && threadIdx.x == 0)
         *a.wm = a.kb ? max(*a.wm, a.pos0 + a.n) : min(*a.wm, a.pos0);
     __syncthreads();
-    if (!active) return;
-    if (is_q) {
-        norm_rope_vec<D>(x, a.qg, a.qk_norm, a.eps, cs, sn, a.rope_pairs, lane);
-        const size_t o = (static_cast<size_t>(i) * a.q_headn + gi) * D + lane * E;
-        if (a.qf) store_vec_f32<E>(a.qf + o, x);
-        if (a.qb) store_vec16<__nv_bfloat16, E>(a.qb + o, x);
-        return;
+#pragma unroll
+    for (int jj = 0; jj < kPrepJobs; ++jj) {
+        const int job = blockIdx.y * kPrepWarps * kPrepJobs + jj * kPrepWarps + warp;
+        if (job >= n_jobs) continue;
+        const bool is_q = job < a.q_headn, is_k = !is_q && job < a.q_headn + a.kv_headn;
+        const int gi = is_q ? job : (is_k ? job - a.q_headn : job - a.q_headn - a.kv_headn);
+        if (is_q) {
+            norm_rope_vec<D>(x[jj], a.qg, a.qk_norm, a.eps, cs, sn, a.rope_pairs, lane);
+            const size_t o = (static_cast<size_t>(i) * a.q_headn + gi) * D + lane * E;
+            if (a.qf) store_vec_f32<E>(a.qf + o, x[jj]);
+            if (a.qb) store_vec16<__nv_bfloat16, E>(a.qb + o, x[jj]);
+            continue;
+        }
+        if (is_k) norm_rope_vec<D>(x[jj], a.kg, a.qk_norm, a.eps, cs, sn, a.rope_pairs, lane);
+        const size_t o = static_cast<size_t>(pos) * a.kv_dim + static_cast<size_t>(gi) * D + lane * E;
+        store_vec_kv<KV, E>(reinterpret_cast<KV*>(is_k ? a.kc : a.vc) + o, x[jj]);
+        __nv_bfloat16* shadow = is_k ? a.kb : a.vb;
+        if (shadow) store_vec16<__nv_bfloat16, E>(shadow + o, x[jj]);
     }
-    if (is_k) norm_rope_vec<D>(x, a.kg, a.qk_norm, a.eps, cs, sn, a.rope_pairs, lane);
-    const size_t o = static_cast<size_t>(pos) * a.kv_dim + static_cast<size_t>(gi) * D + lane * E;
-    store_vec_kv<KV, E>(reinterpret_cast<KV*>(is_k ? a.kc : a.vc) + o, x);
-    __nv_bfloat16* shadow = is_k ? a.kb : a.vb;
-    if (shadow) store_vec16<__nv_bfloat16, E>(shadow + o, x);
 }
 
 // Before a tensor-core prefill at pos0: the layer's cache rows [min(*wm, pos0), pos0) -> its bf16
