@@ -22,6 +22,8 @@ struct ligguf_qmat {
     int* d_err = nullptr;
     float* stage = nullptr;    // device staging of the host-pointer calls: x and the outputs
     size_t stage_floats = 0;
+    uint8_t* act = nullptr;    // the activation forms of a call's token group (qmv_act_kernel)
+    size_t act_bytes = 0;
     cudaStream_t stream = nullptr;
 };
 
@@ -105,6 +107,20 @@ int ring_stages(int act) {
     return 0;
 }
 
+int launch_act(const lg::QmvActArgs& qa, cudaStream_t st) {
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(std::max(1, (lg::qmv_act_items(qa) + 7) / 8), 1, 1);
+    lc.blockDim = dim3(256, 1, 1);
+    lc.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    LG_CUDA(cudaLaunchKernelEx(&lc, lg::qmv_act_kernel, qa));
+    return LIGGUF_ATTN_OK;
+}
+
 template <int T>
 int launch_qmv(lg::QmvArgs& a, int smem, int dev, cudaStream_t st) {
     auto kern = lg::qmv_kernel<T>;
@@ -148,7 +164,6 @@ int matmul_enqueue(const ligguf_qmat* const* ws, float* const* outs, const long 
     }
     a.n = ws[0]->n;
     a.err = ws[0]->d_err;
-    a.x_stride = x_stride;
     int tiles = 0;
     for (int i = 0; i < nmat; ++i) {
         const ligguf_qmat* w = ws[i];
@@ -179,10 +194,27 @@ int matmul_enqueue(const ligguf_qmat* const* ws, float* const* outs, const long 
         return fail(LIGGUF_ATTN_EUNSUPPORTED, "input width %d needs %d bytes of shared memory with these types",
                     a.n, act + 2 * lg::kQmvStageMax);
     const int smem = act + a.stages * lg::kQmvStageMax;
+    if (size_t(a.act.tok_bytes) * T > ws[0]->act_bytes)
+        return fail(LIGGUF_ATTN_EUNSUPPORTED, "activation forms of %d tokens exceed the matrix's scratch", T);
+    lg::QmvActArgs qa = {};
+    qa.n = a.n;
+    qa.need_k = a.need_k;
+    qa.need_0 = a.need_0;
+    qa.need_f = a.need_f;
+    qa.act = a.act;
+    qa.out = ws[0]->act;
+    qa.x_stride = x_stride;
+    a.act_g = ws[0]->act;
     const int dev = ws[0]->device;
     for (int t0 = 0; t0 < n_tok; t0 += T) {
-        a.x = d_x + t0 * x_stride;
+        // The group's activation forms, then the projection (each a programmatic dependent of the
+        // kernel before it: the activation kernel waits for x, the projection streams its weights
+        // before waiting for the forms; the next group's activation kernel waits for this
+        // projection, so the scratch is free).
         a.n_tok = std::min(T, n_tok - t0);
+        qa.x = d_x + t0 * x_stride;
+        qa.n_tok = a.n_tok;
+        if (int rc = launch_act(qa, st)) return rc;
         for (int i = 0; i < nmat; ++i) a.m[i].out = outs[i] ? outs[i] + t0 * out_strides[i] : nullptr;
         int rc;
         switch (T) {
@@ -224,6 +256,7 @@ int ligguf_cuda_qmat_free(ligguf_qmat* w) {
     if (w->stream) cudaStreamSynchronize(w->stream);
     if (w->w) cudaFree(w->w);
     if (w->stage) cudaFree(w->stage);
+    if (w->act) cudaFree(w->act);
     if (w->h_err) cudaFreeHost(w->h_err);
     if (w->stream) cudaStreamDestroy(w->stream);
     delete w;
@@ -268,12 +301,16 @@ int ligguf_cuda_qmat_init_cols(int type, int n, int d, const void* rows, int col
     w->device = device;
     const size_t bytes = size_t(d) * rb;
     const size_t alloc = (bytes + 15) / 16 * 16 + 16;
+    // Scratch for the activation forms of a token group: room for every form at once (Q8_K, Q8_0 and
+    // the fp32 copy, each padded to 16 bytes), whichever types the matrices of a call have.
+    w->act_bytes = size_t(lg::kQmvMaxTokens) * ((n + n / 64 + n / 4 + 48) + (n + n / 8 + 32) + (4 * n + 16));
     // rows of the source are src_rb bytes apart; the kept columns start src_off bytes into each
     if (cudaMalloc(&w->w, alloc) != cudaSuccess || cudaMemset(w->w, 0, alloc) != cudaSuccess ||
         cudaMemcpy2D(w->w, rb, static_cast<const uint8_t*>(rows) + src_off, src_rb, rb, d,
                      rows_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaHostAlloc(&w->h_err, 64, cudaHostAllocMapped) != cudaSuccess ||
         cudaHostGetDevicePointer(reinterpret_cast<void**>(&w->d_err), w->h_err, 0) != cudaSuccess ||
+        cudaMalloc(&w->act, w->act_bytes) != cudaSuccess ||
         cudaStreamCreateWithFlags(&w->stream, cudaStreamNonBlocking) != cudaSuccess) {
         (void)cudaGetLastError();
         ligguf_cuda_qmat_free(w);

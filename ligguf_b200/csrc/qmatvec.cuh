@@ -92,9 +92,8 @@ struct QmvArgs {
     QmvRed red;
     QmvMat m[kQmvMaxMats];
     int nmat;
-    const float* x;  // x[t * x_stride + i], t < n_tok
-    long long x_stride;
-    int n_tok;       // tokens in this launch (<= the kernel's T)
+    const uint8_t* act_g;  // the tokens' activation forms (layout `act`), written by qmv_act_kernel
+    int n_tok;             // tokens in this launch (<= the kernel's T)
     int n;
     int need_k, need_0, need_f;
     int ntiles;      // over all matrices
@@ -624,69 +623,12 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const __grid_consta
     // ------------------------------------------------------------------------- consumers
     asm volatile("griddepcontrol.wait;" ::: "memory");  // x comes from the previous kernel
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    // Quantize every token's x.  Work items are (token, block) pairs dealt round-robin to the warps;
-    // each warp first issues the loads of a batch of its items (x is read from L2 once), then
-    // quantizes them, so the load latency is paid once per batch rather than once per block.
-    if (a.need_k) {
-        constexpr int kB = 4;  // Q8_K blocks per batch: 8 loads of 16 bytes per lane in flight
-        const int nb = a.n / 256, items = nb * a.n_tok;
-        for (int i0 = warp; i0 < items; i0 += kQmvWarps * kB) {
-            float v[kB][8];
-#pragma unroll
-            for (int j = 0; j < kB; ++j) {
-                const int it = i0 + j * kQmvWarps;
-                if (it < items) {
-                    const float4* src = reinterpret_cast<const float4*>(a.x + (it / nb) * a.x_stride + 256 * (it % nb));
-                    const float4 p = src[2 * lane], q = src[2 * lane + 1];
-                    v[j][0] = p.x; v[j][1] = p.y; v[j][2] = p.z; v[j][3] = p.w;
-                    v[j][4] = q.x; v[j][5] = q.y; v[j][6] = q.z; v[j][7] = q.w;
-                }
-            }
-#pragma unroll
-            for (int j = 0; j < kB; ++j) {
-                const int it = i0 + j * kQmvWarps;
-                if (it < items) {
-                    const int t = it / nb, b = it % nb;
-                    uint8_t* tb = smem + size_t(t) * a.act.tok_bytes;
-                    q8k_block_vals(v[j], reinterpret_cast<int8_t*>(tb + a.act.off_qk) + 256 * b,
-                                   reinterpret_cast<float*>(tb + a.act.off_dk) + b,
-                                   reinterpret_cast<int*>(tb + a.act.off_bs) + 16 * b, nullptr, lane);
-                }
-            }
-        }
-    }
-    if (a.need_0) {
-        constexpr int kB = 16;  // Q8_0 blocks per batch: one 4-byte load per lane each
-        const int nb = a.n / 32, items = nb * a.n_tok;
-        for (int i0 = warp; i0 < items; i0 += kQmvWarps * kB) {
-            float v[kB];
-#pragma unroll
-            for (int j = 0; j < kB; ++j) {
-                const int it = i0 + j * kQmvWarps;
-                v[j] = it < items ? a.x[(it / nb) * a.x_stride + 32 * (it % nb) + lane] : 0.f;
-            }
-#pragma unroll
-            for (int j = 0; j < kB; ++j) {
-                const int it = i0 + j * kQmvWarps;
-                if (it < items) {
-                    const int t = it / nb, b = it % nb;
-                    uint8_t* tb = smem + size_t(t) * a.act.tok_bytes;
-                    uint16_t dh;
-                    const int q = q80_block_warp(v[j], &dh, lane);
-                    reinterpret_cast<int8_t*>(tb + a.act.off_q0)[32 * b + lane] = static_cast<int8_t>(q);
-                    if (lane == 0) reinterpret_cast<float*>(tb + a.act.off_d0)[b] = h2f(dh);
-                }
-            }
-        }
-    }
-    if (a.need_f) {
-        const int n4 = a.n / 4;
-        for (int t = 0; t < a.n_tok; ++t) {
-            const float4* x = reinterpret_cast<const float4*>(a.x + t * a.x_stride);
-            float4* dst = reinterpret_cast<float4*>(smem + size_t(t) * a.act.tok_bytes + a.act.off_xf);
-#pragma unroll 4
-            for (int i = warp * 32 + lane; i < n4; i += kQmvWarps * 32) dst[i] = x[i];
-        }
+    // The tokens' activation forms, quantized once for the call by qmv_act_kernel (from L2).
+    {
+        const uint4* src = reinterpret_cast<const uint4*>(a.act_g);
+        uint4* dst = reinterpret_cast<uint4*>(smem);
+        const int n16 = a.n_tok * a.act.tok_bytes / 16;
+        for (int i = tid; i < n16; i += kQmvWarps * 32) dst[i] = __ldcg(src + i);
     }
     named_bar_sync(1, kQmvWarps * 32);
     const int epoch = a.red.peers ? __ldcg(a.red.state) + 1 : 0;
@@ -780,6 +722,54 @@ __global__ void __launch_bounds__(256) reduce_wait_kernel(const unsigned long lo
 // Activation quantizers on their own, writing the reference's block layouts: block_q8_K
 // {float d; int8 qs[256]; int16 bsums[16]} (292 bytes) and block_q8_0 {fp16 d; int8 qs[32]}
 // (34 bytes).  One warp per block.
+// The activation forms of n_tok tokens, once per call (the reference quantizes x once and then
+// runs the matmuls, fast/lil_math.cpp:827-899): Q8_K blocks, Q8_0 blocks and/or the fp32 copy,
+// in the QmvAct layout of the projection kernel's shared memory, into `out` (tok_bytes per token).
+// One warp per work item: a Q8_K block, a Q8_0 block or 256 floats of the copy.  A programmatic
+// dependent of the kernel that wrote x; the projection kernel that follows is one of this kernel
+// and starts streaming its weights while this one runs.
+struct QmvActArgs {
+    const float* x;  // x[t * x_stride + i], t < n_tok
+    long long x_stride;
+    int n_tok, n;
+    int need_k, need_0, need_f;
+    QmvAct act;
+    uint8_t* out;
+};
+__host__ __device__ inline int qmv_act_items(const QmvActArgs& a) {
+    return a.n_tok * ((a.need_k ? a.n / 256 : 0) + (a.need_0 ? a.n / 32 : 0) + (a.need_f ? (a.n + 255) / 256 : 0));
+}
+__global__ void __launch_bounds__(256) qmv_act_kernel(const __grid_constant__ QmvActArgs a) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // x comes from the previous kernel
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int item = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    const int nk = a.need_k ? a.n / 256 : 0, n0 = a.need_0 ? a.n / 32 : 0, nf = a.need_f ? (a.n + 255) / 256 : 0;
+    const int per_tok = nk + n0 + nf;
+    if (item >= a.n_tok * per_tok) return;
+    const int t = item / per_tok;
+    int r = item - t * per_tok;
+    const float* x = a.x + t * a.x_stride;
+    uint8_t* tb = a.out + size_t(t) * a.act.tok_bytes;
+    if (r < nk) {
+        q8k_block_warp(x + 256 * r, reinterpret_cast<int8_t*>(tb + a.act.off_qk) + 256 * r,
+                       reinterpret_cast<float*>(tb + a.act.off_dk) + r, reinterpret_cast<int*>(tb + a.act.off_bs) + 16 * r,
+                       nullptr, lane);
+        return;
+    }
+    r -= nk;
+    if (r < n0) {
+        uint16_t dh;
+        const int q = q80_block_warp(x[32 * r + lane], &dh, lane);
+        reinterpret_cast<int8_t*>(tb + a.act.off_q0)[32 * r + lane] = static_cast<int8_t>(q);
+        if (lane == 0) reinterpret_cast<float*>(tb + a.act.off_d0)[r] = h2f(dh);
+        return;
+    }
+    r -= n0;  // floats [256 r, 256 r + 256) of the copy (n is a multiple of 4)
+    const float4* src = reinterpret_cast<const float4*>(x);
+    float4* dst = reinterpret_cast<float4*>(tb + a.act.off_xf);
+    for (int i = 64 * r + lane; i < min(64 * r + 64, a.n / 4); i += 32) dst[i] = src[i];
+}
+
 __global__ void __launch_bounds__(256) quantize_q8k_kernel(const float* __restrict__ x, int nblocks, uint8_t* out) {
     const int b = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (b >= nblocks) return;
