@@ -248,7 +248,8 @@ int ligguf_cuda_qmat_init_cols(int type, int n, int d, const void* rows, int col
 int ligguf_cuda_qmat_free(ligguf_qmat* w);
 /* matmul3 (w1, w2 non-NULL), matmul2 (w2 NULL) or matmul (w1, w2 NULL): device pointers, x [n],
  * out_i [d_i], enqueued on `stream` (a cudaStream_t; NULL = legacy default).  All matrices share n
- * and the device. */
+ * and the device.  x is quantized once per call into a scratch owned by w0, so calls that share a
+ * first matrix must be issued on one stream. */
 int ligguf_cuda_matmul3_async(const ligguf_qmat* w0, const ligguf_qmat* w1, const ligguf_qmat* w2,
                               const float* d_x, float* d_out0, float* d_out1, float* d_out2,
                               void* stream);
