@@ -212,9 +212,14 @@ int matmul_enqueue(const ligguf_qmat* const* ws, float* const* outs, const long 
         // before waiting for the forms; the next group's activation kernel waits for this
         // projection, so the scratch is free).
         a.n_tok = std::min(T, n_tok - t0);
-        qa.x = d_x + t0 * x_stride;
-        qa.n_tok = a.n_tok;
-        if (int rc = launch_act(qa, st)) return rc;
+        if (T == 1) {  // one token: the projection kernel quantizes it itself
+            a.act_g = nullptr;
+            a.x = d_x + t0 * x_stride;
+        } else {
+            qa.x = d_x + t0 * x_stride;
+            qa.n_tok = a.n_tok;
+            if (int rc = launch_act(qa, st)) return rc;
+        }
         for (int i = 0; i < nmat; ++i) a.m[i].out = outs[i] ? outs[i] + t0 * out_strides[i] : nullptr;
         int rc;
         switch (T) {

@@ -92,7 +92,8 @@ struct QmvArgs {
     QmvRed red;
     QmvMat m[kQmvMaxMats];
     int nmat;
-    const uint8_t* act_g;  // the tokens' activation forms (layout `act`), written by qmv_act_kernel
+    const uint8_t* act_g;  // the tokens' activation forms (layout `act`), written by qmv_act_kernel, or
+    const float* x;        // null: one token's x, quantized by this kernel (T = 1)
     int n_tok;             // tokens in this launch (<= the kernel's T)
     int n;
     int need_k, need_0, need_f;
@@ -184,6 +185,33 @@ __device__ __forceinline__ int q80_block_warp(float xv, uint16_t* d_bits, int la
     const float id = d != 0.f ? __fdiv_rn(127.0f, amax) : 0.f;
     if (lane == 0) *d_bits = __half_as_ushort(__float2half_rn(d));
     return static_cast<int>(roundf(__fmul_rn(xv, id)));
+}
+
+// The same block by one thread: the 32 values in registers, amax over them (the order of a max does
+// not matter), then the same d, 1/d and rounding; writes the 32 q values and d (as its fp32 value).
+__device__ __forceinline__ void q80_block_lane(const float* __restrict__ x, int8_t* q, float* d_out) {
+    float v[32];
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 f = x4[i];
+        v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    const float d = __fmul_rn(amax, 1.0f / 127.0f);
+    const float id = d != 0.f ? __fdiv_rn(127.0f, amax) : 0.f;
+    uint32_t* qw = reinterpret_cast<uint32_t*>(q);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        uint32_t w = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            w |= uint32_t(uint8_t(static_cast<int8_t>(static_cast<int>(roundf(__fmul_rn(v[4 * i + j], id)))))) << (8 * j);
+        qw[i] = w;
+    }
+    *d_out = __half2float(__float2half_rn(d));
 }
 
 // ------------------------------------------------------------------------------ unit dots
@@ -623,12 +651,30 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const __grid_consta
     // ------------------------------------------------------------------------- consumers
     asm volatile("griddepcontrol.wait;" ::: "memory");  // x comes from the previous kernel
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    // The tokens' activation forms, quantized once for the call by qmv_act_kernel (from L2).
-    {
+    if (a.act_g) {
+        // The tokens' activation forms, quantized once for the call by qmv_act_kernel (from L2).
         const uint4* src = reinterpret_cast<const uint4*>(a.act_g);
         uint4* dst = reinterpret_cast<uint4*>(smem);
         const int n16 = a.n_tok * a.act.tok_bytes / 16;
         for (int i = tid; i < n16; i += kQmvWarps * 32) dst[i] = __ldcg(src + i);
+    } else {
+        // One token: its forms here, in each CTA, which costs less than another launch.  Q8_K: a
+        // warp per 256-element block; Q8_0: a lane per 32-element block (no shuffles: 128 blocks of a
+        // 4096-wide x are one pass of 4 warps); the fp32 copy for F32/F16 weights.
+        if (a.need_k)
+            for (int b = warp; b < a.n / 256; b += kQmvWarps)
+                q8k_block_warp(a.x + 256 * b, reinterpret_cast<int8_t*>(smem + a.act.off_qk) + 256 * b,
+                               reinterpret_cast<float*>(smem + a.act.off_dk) + b,
+                               reinterpret_cast<int*>(smem + a.act.off_bs) + 16 * b, nullptr, lane);
+        if (a.need_0)
+            for (int b = tid; b < a.n / 32; b += kQmvWarps * 32)
+                q80_block_lane(a.x + 32 * b, reinterpret_cast<int8_t*>(smem + a.act.off_q0) + 32 * b,
+                               reinterpret_cast<float*>(smem + a.act.off_d0) + b);
+        if (a.need_f) {
+            const float4* x4 = reinterpret_cast<const float4*>(a.x);
+            float4* dst = reinterpret_cast<float4*>(smem + a.act.off_xf);
+            for (int i = tid; i < a.n / 4; i += kQmvWarps * 32) dst[i] = x4[i];
+        }
     }
     named_bar_sync(1, kQmvWarps * 32);
     const int epoch = a.red.peers ? __ldcg(a.red.state) + 1 : 0;
