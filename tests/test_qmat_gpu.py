@@ -102,6 +102,25 @@ def test_matmul3_batch_equals_token_loop(gpu, n_tok, types):
         m.close()
 
 
+@pytest.mark.parametrize("types", [("Q8_0", "Q8_0", "Q8_0"), ("Q4_K", "Q4_K", "Q6_K"), ("F32", "Q1_0", "Q3_K")])
+def test_one_token_and_batch_quantize_alike(gpu, types):
+    """A token alone (quantized inside the projection kernel, a lane per Q8_0 block) and the same
+    token inside a batch (quantized once per call by the activation kernel, a warp per block) give
+    bit-identical outputs: both are the reference's quantizer, and the dots run in the same order."""
+    import torch
+    n, dims = 4096, (1024, 512, 256)
+    ws = [(QT[nm], synthetic_rows(QT[nm], n, d, seed=31 + i)) for i, (nm, d) in enumerate(zip(types, dims))]
+    mats = [QuantMatrix(t, n, w) for t, w in ws]
+    xs = np.stack([_x(n, 200 + i, mag=[1e-3, 1.0, 40.0][i]) for i in range(3)])
+    batch = matmul3_batch(*mats, xs)
+    for i in range(3):
+        one = matmul3(*mats, xs[i])
+        for j in range(3):
+            assert np.array_equal(one[j], batch[j][i]), (types, i, j)
+    for m in mats:
+        m.close()
+
+
 def test_matmul3_shapes_and_errors(gpu):
     from ligguf_b200 import _lib
     from ligguf_b200._lib import LigGufAttnError
