@@ -230,7 +230,9 @@ int ligguf_cuda_bert_attn_tc_noalloc_status(void* stream);
  * fp32 for F32 / F16).  The integer block dot products and scale terms are exact; only the fp32 sum
  * over blocks runs in another order than the reference's AVX2 loops.
  * Weight types (gguf_type, fast/lil_gguf.h:26-44): 0 F32, 1 F16, 8 Q8_0, 10 Q2_K, 11 Q3_K, 12 Q4_K,
- * 13 Q5_K, 14 Q6_K, 40 Q1_0, 41 Q1_G.  Widths: a multiple of 32 (256 for K-quants), at most 16384. */
+ * 13 Q5_K, 14 Q6_K, 40 Q1_0, 41 Q1_G.  Widths: a multiple of 32 (256 for K-quants), at most 16384,
+ * and one row must fit a 32 KB stream stage (F32: at most 8192; init fails with
+ * LIGGUF_ATTN_EUNSUPPORTED otherwise). */
 typedef struct ligguf_qmat ligguf_qmat;
 /* Bytes of one row of `n` elements of `type` (the reference's row_size), 0 if not a whole number of
  * blocks or an unknown type. */

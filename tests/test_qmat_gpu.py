@@ -77,6 +77,28 @@ def test_matmul3_qwen3_8b_shapes(gpu, types):
         m.close()
 
 
+@pytest.mark.parametrize("name", ["F32", "F16", "Q8_0", "Q1_0"])
+@pytest.mark.parametrize("n,d", [(96, 7), (864, 131), (16384, 40)])
+def test_matmul_ragged_widths(gpu, name, n, d):
+    """Widths that are a multiple of the 32-element block but not of 256 or 1024 (the tail of the
+    Q8_0 quantizer's lane-per-block pass and of the fp32 copy), row counts that leave a partial
+    tile, and the widest input the kernel takes (16384; for F32, whose row must fit a 32 KB stream
+    stage, 8192), one token and a batch of 5."""
+    if name == "F32" and n > 8192:
+        n = 8192
+    t = QT[name]
+    w = synthetic_rows(t, n, d, seed=t * 13 + n)
+    m = QuantMatrix(t, n, w)
+    xs = np.stack([_x(n, n + t + i, mag=0.5 + i) for i in range(5)])
+    (one,) = matmul3(m, None, None, xs[0])
+    (batch,) = matmul3_batch(m, None, None, xs)
+    m.close()
+    for i in range(5):
+        ref = orc.matmul(t, w, n, xs[i], "ref")
+        assert _rel(batch[i], ref) <= TOL, (name, i)
+    assert np.array_equal(one, batch[0])
+
+
 @pytest.mark.parametrize("n_tok", [1, 3, 8, 21])
 @pytest.mark.parametrize("types", [("Q4_K", "Q4_K", "Q6_K"), ("Q8_0", "Q8_0", "Q8_0"), ("F16", "Q2_K", "Q1_G")])
 def test_matmul3_batch_equals_token_loop(gpu, n_tok, types):
