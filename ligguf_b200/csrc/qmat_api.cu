@@ -155,6 +155,9 @@ int launch_qmv(lg::QmvArgs& a, int smem, int dev, cudaStream_t st) {
 int matmul_enqueue(const ligguf_qmat* const* ws, float* const* outs, const long long* out_strides, int nmat,
                    const float* d_x, long long x_stride, int n_tok, cudaStream_t st,
                    const ligguf_reduce* red = nullptr) {
+    // x is read in 16-byte vectors: rows must start on 16-byte boundaries.
+    if (!d_x || (reinterpret_cast<uintptr_t>(d_x) & 15) || (n_tok > 1 && (x_stride & 3)))
+        return fail(LIGGUF_ATTN_EINVAL, "x must be non-null, 16-byte aligned, with a row stride of a multiple of 4 floats");
     lg::QmvArgs a = {};
     if (red) {
         a.red.peers = red->d_peers;

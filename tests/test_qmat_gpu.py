@@ -155,5 +155,11 @@ def test_matmul3_shapes_and_errors(gpu):
     with pytest.raises(LigGufAttnError) as e:  # different input widths in one call
         matmul3(a, b, None, x)
     assert e.value.status == _lib.EINVAL
+    import torch
+    dx = torch.zeros(2048 + 4, device="cuda")
+    out = torch.empty(7, device="cuda")
+    with pytest.raises(LigGufAttnError) as e:  # x not on a 16-byte boundary (read in 16-byte vectors)
+        matmul3_async(a, None, None, dx.data_ptr() + 4, out)
+    assert e.value.status == _lib.EINVAL
     a.close()
     b.close()
