@@ -443,9 +443,10 @@ int launch_flash_tc_t(const lg::TcArgs& t, cudaStream_t st, int device) {
         // with; a smaller launch count would leave the softmax warpgroup's increase waiting forever.
         cudaFuncAttributes fa{};
         LG_CUDA(cudaFuncGetAttributes(&fa, kern));
-        if (fa.numRegs * 3 < lg::kTcRegsIssue + lg::kTcRegsSoftmax + lg::kTcRegsEpilogue)
+        constexpr int need = lg::kTcRegsIssue + 2 * lg::kTcRegsSoftmax + lg::kTcRegsEpilogue;
+        if (fa.numRegs * 4 < need)
             return fail(LIGGUF_ATTN_ECUDA, "tensor-core attention kernel built with %d registers per thread, %d needed",
-                        fa.numRegs, (lg::kTcRegsIssue + lg::kTcRegsSoftmax + lg::kTcRegsEpilogue + 2) / 3);
+                        fa.numRegs, (need + 3) / 4);
         int sms = 0, per_sm = 0;
         LG_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
         LG_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, lg::kTcThreads, lg::TcSmem<D>::kTotal));

@@ -7,7 +7,7 @@
 // Work item = 128 query rows (one tile) of one q head of one batch entry.  A kernel that uses
 // tcgen05 runs one CTA per SM, so the grid is persistent: one CTA per SM walks a fixed share of the
 // items, keeping its barriers and all 512 TMEM columns across them, and the overlap of tensor-core
-// work with softmax work comes from inside the CTA (384 threads, three warpgroups whose register
+// work with softmax work comes from inside the CTA (512 threads, four warpgroups whose register
 // budgets are rebalanced with setmaxnreg):
 //   warp 0      TMA producer: per item the Q tile (double-buffered), then K and V tiles of 128 keys
 //               into 2-stage rings (3 for D = 64)
@@ -16,11 +16,12 @@
 //   warp 2      lane 0 issues O += P.V: 8 MMAs of M128 N=D K16 per tile, P from TMEM, V from shared
 //               memory (MN-major, SWIZZLE_128B)
 //   warp 3      idle (completes the first warpgroup)
-//   warps 4..7  softmax: thread = query row = TMEM lane; reads the 128 columns of its S row from
-//               TMEM once into registers (row max, then exp2), writes P as bf16 pairs back into the
-//               same TMEM columns, rescales O in TMEM when the running max moves (rare); row sums
-//               to shared memory
-//   warps 8..11 epilogue: O / l from TMEM to global memory through a padded staging block (whole
+//   warps 4..11 softmax, two threads per query row (= TMEM lane): warps 4-7 take S columns
+//               [0, 64), warps 8-11 columns [64, 128) of the same lanes; each reads its half of the
+//               row from TMEM once into registers, the two exchange their half maxima through
+//               shared memory, then each writes its P half as bf16 pairs back into TMEM, rescales
+//               its half of O when the running max moves (rare), and keeps its half of the row sum
+//   warps 12..15 epilogue: O / l from TMEM to global memory through a padded staging block (whole
 //               128-byte row segments per store), so the softmax warps never wait for it
 // Items are walked heaviest first: causal prefill by their numbering, BERT through a work order
 // sorted by key-tile count that the operand conversion kernel writes (bert_item_order).
@@ -147,19 +148,21 @@ __global__ void __launch_bounds__(256) bert_to_bf16_kernel(const float* __restri
     }
 }
 
-// Three warpgroups: 0 = TMA producer (warp 0), S issuer (warp 1), P.V issuer (warp 2), warp 3 idle;
-// 1 = softmax (warps 4-7); 2 = epilogue (warps 8-11).  A warp reaches only TMEM lanes
-// [32 * (warp % 4), +32), so each of the softmax and epilogue warpgroups covers all 128 lanes.
-constexpr int kTcThreads = 384;
+// Four warpgroups: 0 = TMA producer (warp 0), S issuer (warp 1), P.V issuer (warp 2), warp 3 idle;
+// 1 and 2 = softmax, column halves of every row (warps 4-7, 8-11); 3 = epilogue (warps 12-15).  A
+// warp reaches only TMEM lanes [32 * (warp % 4), +32), so each of the last three warpgroups covers
+// all 128 lanes.
+constexpr int kTcThreads = 512;
 constexpr int kTcPvWarp = 2;  // the warp that issues the P.V MMAs
-// Register split (setmaxnreg) from the 168 per thread that 384 threads at one CTA per SM launch with:
-// the softmax holds a whole 128-column S row in registers.  The sum of the three shares must not
-// exceed 3 x 168, or the increase waits forever; the launcher checks the kernel's register count.
-constexpr int kTcRegsLaunch = 168;
-constexpr int kTcRegsIssue = 96;
-constexpr int kTcRegsSoftmax = 240;
-constexpr int kTcRegsEpilogue = 152;
-static_assert(kTcRegsIssue + kTcRegsSoftmax + kTcRegsEpilogue <= 3 * kTcRegsLaunch, "register split too large");
+// Register split (setmaxnreg) from the 128 per thread that 512 threads at one CTA per SM launch with:
+// a softmax thread holds half of a 128-column S row in registers, an epilogue thread a 32-column
+// block of O.  The sum of the four shares must not exceed 4 x 128, or an increase waits forever; the
+// launcher checks the kernel's register count.  (This split compiles without spills.)
+constexpr int kTcRegsLaunch = 128;
+constexpr int kTcRegsIssue = 56;
+constexpr int kTcRegsSoftmax = 160;
+constexpr int kTcRegsEpilogue = 136;
+static_assert(kTcRegsIssue + 2 * kTcRegsSoftmax + kTcRegsEpilogue <= 4 * kTcRegsLaunch, "register split too large");
 static_assert(kTcThreads * kTcRegsLaunch <= 65536, "launch register count does not fit an SM");
 // A kernel that uses tcgen05 runs one CTA per SM, which then owns all 512 TMEM columns:
 // S double buffer [0, 256) (P of a tile is packed over the first 64 columns of its S buffer),
@@ -185,15 +188,16 @@ struct TcSmem {
     static constexpr size_t kQ = 0;                      // Q double buffer (by item)
     static constexpr size_t kK = kQ + 2 * size_t(kQBytes);
     static constexpr size_t kV = kK + size_t(kStages) * kKvBytes;
-    static constexpr size_t kL = kV + size_t(kStages) * kKvBytes;  // row sums l, [kLRing][128] fp32
+    static constexpr size_t kL = kV + size_t(kStages) * kKvBytes;  // row sums l, [kLRing][2 halves][128] fp32
     // Epilogue staging: per epilogue warp a 32 x 32 fp32 block, rows padded to 36 floats (16-byte
     // aligned, conflict-free float4 accesses both ways).
     static constexpr int kStageRow = 36;
-    static constexpr size_t kE = kL + size_t(kLRing) * kTcRows * 4;
+    static constexpr size_t kX = kL + size_t(kLRing) * 2 * kTcRows * 4;  // half-row maxima [2 tiles][2][128]
+    static constexpr size_t kE = kX + size_t(2) * 2 * kTcRows * 4;
     static constexpr size_t kBar = kE + 4 * 32 * kStageRow * 4;
     // k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2], pv_done[2], drain, q_full[2],
     // q_empty[2], o_final[2], o_free[2], l_full[kLRing]
-    static constexpr int kNumBars = 4 * kStages + 2 + 2 + 2 + 1 + 8 + kLRing;
+    static constexpr int kNumBars = 4 * kStages + 2 + 2 + 2 + 1 + 8 + kLRing + 8;  // + xchg[2][4]
     static constexpr size_t kMisc = kBar + size_t(kNumBars) * 8;  // tmem base, abort flag
     static constexpr size_t kTotal = kMisc + 16 + 1024;           // + slack to align the base to 1 KB
 };
@@ -344,6 +348,16 @@ template <int R>
 __device__ __forceinline__ void reg_inc() {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(R));
 }
+// A warpgroup's share R set from the launch count: an increase or a decrease, chosen at compile time
+// (.dec to a count above the current one, or .inc below it, is an illegal instruction).
+template <int R>
+__device__ __forceinline__ void reg_set() {
+    static_assert(R % 8 == 0 && R >= 24 && R <= 256, "setmaxnreg takes a multiple of 8 in [24, 256]");
+    if constexpr (R > kTcRegsLaunch)
+        reg_inc<R>();
+    else if constexpr (R < kTcRegsLaunch)
+        reg_dec<R>();
+}
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
     float d;
     asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
@@ -439,7 +453,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint64_t* q_empty = q_full + 2;   // [2] the item's last S MMA completed: its Q buffer is free
     uint64_t* o_final = q_empty + 2;  // [2] the item's last P.V completed: O is final
     uint64_t* o_free = o_final + 2;   // [2] the epilogue has read O
-    uint64_t* l_full = o_free + 2;    // [LR] the item's row sums are in shared memory
+    uint64_t* l_full = o_free + 2;
+    uint64_t* xchg = l_full + LR;     // [tile parity][quarter] both halves of the rows wrote their maxima    // [LR] the item's row sums are in shared memory
     float* lsum = reinterpret_cast<float*>(sm + Sm::kL);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Sm::kMisc);
     volatile int* abort = reinterpret_cast<volatile int*>(sm + Sm::kMisc + 4);
@@ -466,9 +481,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mbar_init(&o_final[i], 1);
             mbar_init(&o_free[i], 4);
         }
-        for (int i = 0; i < LR; ++i) mbar_init(&l_full[i], 4);
-        mbar_init(&p_full[0], 4);
-        mbar_init(&p_full[1], 4);
+        for (int i = 0; i < LR; ++i) mbar_init(&l_full[i], 8);  // both halves of every row
+        for (int i = 0; i < 8; ++i) mbar_init(&xchg[i], 2);       // the two warps of a quarter
+        mbar_init(&p_full[0], 8);
+        mbar_init(&p_full[1], 8);
         mbar_init(&pv_done[0], 1);
         mbar_init(&pv_done[1], 1);
         mbar_init(drain, 2);
@@ -487,7 +503,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     asm volatile("griddepcontrol.wait;" ::: "memory");
 
     if (warp < 4) {
-        reg_dec<kTcRegsIssue>();
+        reg_set<kTcRegsIssue>();
         if (warp == 0) {
             // ------------------------------------------------------------------ TMA producer
             if (lane == 0) {
@@ -633,12 +649,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
             }
         }
-    } else if (warp < 8) {
-        reg_inc<kTcRegsSoftmax>();
-        // ------------------------------------------------------------------ softmax warpgroup
+    } else if (warp < 12) {
+        reg_set<kTcRegsSoftmax>();
+        // ------------------------------------------------------------------ softmax warpgroups
+        // Two warpgroups split every S row: warps 4-7 take columns [0, 64), warps 8-11 columns
+        // [64, 128) of the same TMEM lanes (warps w and w + 4 reach the same 32 lanes).  Per tile the
+        // two threads of a row exchange their half-row maxima through shared memory (a named barrier
+        // per warp pair, the buffer alternating by tile), so both use the same running max; each
+        // exponentiates and packs its own 64 columns, rescales its half of O, and keeps its half of
+        // the row sum, which the epilogue adds.  Two softmax warps per sub-partition instead of one
+        // halve each thread's dependent chain.
+        const int half = (warp - 4) >> 2;
         const int quarter = warp & 3;         // TMEM lanes [32*quarter, 32*quarter+32)
         const int row = quarter * 32 + lane;  // query row within the tile
         const uint32_t lane_off = uint32_t(quarter * 32) << 16;
+        float* xmax = reinterpret_cast<float*>(sm + Sm::kX);  // [tile parity][half][128]
+        constexpr int HK = kTcKeys / 2;                        // columns per half
         const float c2 = a.scale_log2;
         bool ok = true;
         int t = 0, z = 0;
@@ -655,6 +681,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int j = 0; j < n_kv; ++j, ++t) {
                 const int bf = t & 1;
                 const uint32_t s_tmem = tmem + Tm::kS + bf * kTcKeys + lane_off;
+                const uint32_t s_half = s_tmem + half * HK;  // this half's S columns
                 ok = __all_sync(0xffffffffu, ok && tc_wait(&s_full[bf], (t >> 1) & 1, deadline, abort, a.err,
                                                          KERR_TIMEOUT_MMA));
                 if (!ok) break;
@@ -666,24 +693,36 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const int lim = min(kv_len - k0, a.causal ? a.q_pos0 + qr - k0 + 1 : kTcKeys);
                 // The tile's row in registers (one read of TMEM; the softmax warpgroup's register
                 // share holds it), then the row max over 8 independent chains of three-input max.
-                uint32_t r[kTcKeys];
+                uint32_t r[HK];
 #pragma unroll
-                for (int c = 0; c < kTcKeys; c += 32) tmem_ld32p(s_tmem + c, r + c);
+                for (int c = 0; c < HK; c += 32) tmem_ld32p(s_half + c, r + c);
                 tmem_wait_ld();
                 if (edge)
 #pragma unroll
-                    for (int c = 0; c < kTcKeys; ++c)
-                        if (c >= lim) r[c] = __float_as_uint(-INFINITY);
+                    for (int c = 0; c < HK; ++c)
+                        if (half * HK + c >= lim) r[c] = __float_as_uint(-INFINITY);
                 float mx8[8];
 #pragma unroll
                 for (int u = 0; u < 8; ++u) mx8[u] = fmaxf(__uint_as_float(r[u]), __uint_as_float(r[8 + u]));
 #pragma unroll
-                for (int c = 16; c < kTcKeys; c += 16)
+                for (int c = 16; c < HK; c += 16)
 #pragma unroll
                     for (int u = 0; u < 8; ++u)
                         mx8[u] = fmax3(mx8[u], __uint_as_float(r[c + u]), __uint_as_float(r[c + 8 + u]));
-                const float mx =
+                const float mxh =
                     fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
+                // The row max from both halves, exchanged through shared memory and an mbarrier per
+                // warp pair (a bounded wait, so a partner that gave up cannot hang this warp).  The
+                // buffer and barrier alternate by tile: this warp writes the slot of tile t + 2 only
+                // after its partner's arrival for tile t + 1, which follows the partner's read of t.
+                float* xm = xmax + (t & 1) * 2 * kTcRows;
+                xm[half * kTcRows + row] = mxh;
+                __syncwarp();
+                uint64_t* xb = &xchg[(t & 1) * 4 + quarter];
+                if (lane == 0) mbar_arrive(xb);
+                ok = __all_sync(0xffffffffu, ok && tc_wait(xb, (t >> 1) & 1, deadline, abort, a.err, KERR_TIMEOUT_MMA));
+                if (!ok) break;
+                const float mx = fmaxf(mxh, xm[(1 - half) * kTcRows + row]);
                 // The running max (log2 units) only moves when the tile max exceeds it by more than 8:
                 // p = 2^(s*c2 - m) then stays <= 256 and O/l are rescaled rarely; the normalisation at
                 // the end uses the same m, so the result is unchanged.
@@ -703,7 +742,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     tc_fence_after();
                     uint32_t y[32];
 #pragma unroll 1
-                    for (int ch = 0; ch < D / 32; ++ch) {
+                    for (int ch = half * (D / 64); ch < (half + 1) * (D / 64); ++ch) {  // this half's columns of O
                         tmem_ld32(o_tmem + ch * 32, y);
                         tmem_wait_ld();
 #pragma unroll
@@ -719,12 +758,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 float2 rs4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                                  make_float2(0.f, 0.f)};
                 const float2 cc = make_float2(c2, c2), nm = make_float2(-ms, -ms);
-#pragma unroll
-                for (int hc = 0; hc < kTcKeys / 64; ++hc) {
+                {
                     uint32_t pk[32];
 #pragma unroll
                     for (int c = 0; c < 32; ++c) {
-                        const int i = hc * 64 + 2 * c;
+                        const int i = 2 * c;
                         float2 e = ffma2(make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), cc, nm);
                         if ((kTcPolyPairs >> (c & 7)) & 1u) {
                             e = exp2_poly2(e);
@@ -735,7 +773,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         pk[c] = pack_bf16(e.x, e.y);
                         rs4[c & 3] = fadd2(rs4[c & 3], e);
                     }
-                    tmem_st32(s_tmem + hc * 32, pk);
+                    tmem_st32(s_tmem + half * 32, pk);  // P of columns [64h, 64h+64) into [32h, 32h+32)
                 }
                 const float2 rs2 = fadd2(fadd2(rs4[0], rs4[1]), fadd2(rs4[2], rs4[3]));
                 l = l * corr + (rs2.x + rs2.y);
@@ -745,15 +783,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (lane == 0) mbar_arrive(&p_full[bf]);
             }
             if (!ok) break;
-            // The row sums go to the epilogue warps through shared memory.
-            lsum[(z % LR) * kTcRows + row] = l;
+            // The half-row sums go to the epilogue warps through shared memory.
+            lsum[((z % LR) * 2 + half) * kTcRows + row] = l;
             __syncwarp();
             if (lane == 0) mbar_arrive(&l_full[z % LR]);
             ++z;
         }
         tc_fence_before();
     } else {
-        reg_dec<kTcRegsEpilogue>();
+        reg_set<kTcRegsEpilogue>();
         // ------------------------------------------------------------------ epilogue warpgroup
         // Per item z: row sums from shared memory, O buffer z & 1 from TMEM once the last P.V has
         // completed, O / l to the output rows, then O buffer z & 1 is handed back to the MMA issuer.
@@ -791,7 +829,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                                  KERR_TIMEOUT_MMA));
             if (!ok) break;
             // Padded rows (past the valid ones) are written as zeros.
-            const float inv = it.r0 + row < it.nq_valid ? 1.0f / lsum[(z % LR) * kTcRows + row] : 0.f;
+            const float inv = it.r0 + row < it.nq_valid
+                                  ? 1.0f / (lsum[(z % LR) * 2 * kTcRows + row] + lsum[((z % LR) * 2 + 1) * kTcRows + row])
+                                  : 0.f;
             ok = __all_sync(0xffffffffu, tc_wait(&o_final[ob], (z >> 1) & 1, deadline, abort, a.err,
                                                  KERR_TIMEOUT_MMA));
             if (!ok) break;
