@@ -384,8 +384,11 @@ int launch_flash_simt(const lg::FlashArgs& f, int D, dim3 grid, cudaStream_t st,
 
 template <typename KV, int D>
 int launch_prep_t(const lg::PrepArgs& p, cudaStream_t st) {
-    const dim3 grid(p.n, ceil_div(p.q_headn + 2 * p.kv_headn, lg::kPrepWarps * lg::kPrepJobs));
-    lg::prefill_prep_kernel<KV, D><<<grid, lg::kPrepWarps * 32, 0, st>>>(p);
+    // One block per token; the token's q, k, v rows in dynamic shared memory.
+    const int smem = (p.q_headn + 2 * p.kv_headn) * D * 4;
+    auto kern = lg::prefill_prep_kernel<KV, D>;
+    if (smem > 48 * 1024) LG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    kern<<<p.n, lg::kPrepWarps * 32, smem, st>>>(p);
     LG_CUDA(cudaGetLastError());
     return LIGGUF_ATTN_OK;
 }
@@ -486,6 +489,8 @@ int prefill_enqueue(ligguf_attn* h, int layer, int pos0, int n, const float* dq,
     if (n < 1 || pos0 < 0 || pos0 + n > c.n_context)
         return fail(LIGGUF_ATTN_EINVAL, "positions [%d, %d) outside [0, %d)", pos0, pos0 + n, c.n_context);
     if (!dq || !dk || !dv || !dout) return fail(LIGGUF_ATTN_EINVAL, "null tensor pointer");
+    if ((reinterpret_cast<uintptr_t>(dq) | reinterpret_cast<uintptr_t>(dk) | reinterpret_cast<uintptr_t>(dv)) & 15)
+        return fail(LIGGUF_ATTN_EINVAL, "q, k and v must be 16-byte aligned");
     if (mode != LIGGUF_MODE_SIMT && mode != LIGGUF_MODE_TC) return fail(LIGGUF_ATTN_EINVAL, "mode %d", mode);
     if (c.qk_norm && !h->norm_set[layer])
         return fail(LIGGUF_ATTN_ESTATE, "QK-norm weights of layer %d were not set", layer);
@@ -510,6 +515,7 @@ int prefill_enqueue(ligguf_attn* h, int layer, int pos0, int n, const float* dq,
     p.qk_norm = c.qk_norm;
     p.eps = c.rms_epsilon;
     p.wm = h->d_wm + layer;
+    p.err = h->d_err;
     const bool div = c.scale_mode == LIGGUF_SCALE_DIV;
     const float scale = div ? sqrtf(static_cast<float>(D)) : 1.0f / sqrtf(static_cast<float>(D));
 

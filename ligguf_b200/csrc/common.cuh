@@ -74,6 +74,15 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     return true;
 }
 
+// 1-D bulk copy global -> this CTA's shared memory (no multicast), completion counted on `bar`.
+// Both addresses 16-byte aligned, `bytes` a multiple of 16.
+__device__ __forceinline__ void bulk_copy_g2s(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
+                 "l"(src), "r"(bytes), "r"(static_cast<uint32_t>(__cvta_generic_to_shared(bar)))
+                 : "memory");
+}
+
 // ---------------------------------------------------------------------------------- TMA
 // 3-D tiled load global -> shared, completion counted on `bar`.  Destination is this CTA's own
 // shared memory only.

@@ -240,6 +240,7 @@ struct PrepArgs {
     __nv_bfloat16* kb;  // [n_context][kv_dim] bf16 key shadow, rows by absolute position (or null)
     __nv_bfloat16* vb;
     int* wm;            // the layer's shadow watermark: shadow rows [0, *wm) equal the cache rows
+    int* err;           // error word (mapped host memory): set when the row copies did not land
     int n, pos0, q_headn, kv_headn, kv_dim, rope_pairs, qk_norm;
     float eps;
 };
@@ -316,63 +317,72 @@ __device__ __forceinline__ void norm_rope_vec(float (&x)[D / 32], const float* _
 }
 
 // Prompt rows before attention: per token, the q heads (norm + RoPE; fp32 and/or bf16 out), the k
-// heads (norm + RoPE) and the v heads into this layer's cache rows (and their bf16 shadow).  Three
-// heads per warp: block (token, group of 3 * kPrepWarps heads: all 48 of a Qwen3-8B token), warp w
-// taking heads w, w + kPrepWarps and w + 2 * kPrepWarps of the group, each lane holding E = D/32
-// consecutive elements of each (one 16- or 8-byte load per head).  All the rows are loaded before
-// the token's cos/sin table is computed into shared memory, so their latency overlaps that
-// computation and the block barrier; three loads per lane in flight instead of one (the kernel is
-// bound by the bytes each SM keeps in flight).
-constexpr int kPrepWarps = 16;
-constexpr int kPrepJobs = 3;  // heads per warp
+// heads (norm + RoPE) and the v heads into this layer's cache rows (and their bf16 shadow).  One
+// block per token: thread 0 brings the token's q, k and v rows (24 KB for Qwen3-8B) into shared
+// memory with three bulk copies, which need no registers, so 8 blocks of an SM keep twice the bytes
+// in flight that register loads did (the kernel is bound by the bytes each SM keeps in flight);
+// the RoPE rotation is computed while they land, then the heads are dealt to the warps (one warp
+// per head, each lane E = D/32 consecutive elements).  q, k, v must be 16-byte aligned.
+constexpr int kPrepWarps = 8;
 template <typename KV, int D>
 __global__ void __launch_bounds__(kPrepWarps * 32) prefill_prep_kernel(const PrepArgs a) {
     // Launched in stream order (its predecessor has completed); the tensor-core kernel that follows
     // is a programmatic dependent and may start its set-up once every block of this grid has begun.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     constexpr int E = D / 32;
-    __shared__ float cs[D / 2], sn[D / 2];  // RoPE rotation of this token, shared by all heads
+    extern __shared__ __align__(16) float rows[];  // [q_headn + 2 * kv_headn][D] of this token
+    __shared__ float cs[D / 2], sn[D / 2];          // RoPE rotation of this token, shared by all heads
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int abort_s;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int i = blockIdx.x;
     const int pos = a.pos0 + i;
     const int n_jobs = a.q_headn + 2 * a.kv_headn;
-    float x[kPrepJobs][E];
-#pragma unroll
-    for (int jj = 0; jj < kPrepJobs; ++jj) {
-        const int job = blockIdx.y * kPrepWarps * kPrepJobs + jj * kPrepWarps + warp;
-        if (job < n_jobs) {
-            const bool is_q = job < a.q_headn, is_k = !is_q && job < a.q_headn + a.kv_headn;
-            const int gi = is_q ? job : (is_k ? job - a.q_headn : job - a.q_headn - a.kv_headn);
-            const float* src = is_q ? a.q + (static_cast<size_t>(i) * a.q_headn + gi) * D
-                                    : (is_k ? a.k : a.v) + (static_cast<size_t>(i) * a.kv_headn + gi) * D;
-            load_vec<E>(src + lane * E, x[jj]);
-        }
+    const uint32_t qbytes = uint32_t(a.q_headn) * D * 4, kbytes = uint32_t(a.kv_headn) * D * 4;
+    if (threadIdx.x == 0) {
+        abort_s = 0;
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+        mbar_arrive_expect_tx(&bar, qbytes + 2 * kbytes);
+        bulk_copy_g2s(rows, a.q + static_cast<size_t>(i) * a.q_headn * D, qbytes, &bar);
+        bulk_copy_g2s(rows + a.q_headn * D, a.k + static_cast<size_t>(i) * a.kv_headn * D, kbytes, &bar);
+        bulk_copy_g2s(rows + (a.q_headn + a.kv_headn) * D, a.v + static_cast<size_t>(i) * a.kv_headn * D, kbytes,
+                      &bar);
     }
     for (int m = threadIdx.x; m < a.rope_pairs; m += blockDim.x)
         sincosf(static_cast<float>(pos) * a.freq[m], &sn[m], &cs[m]);
     // Watermark: with shadows, rows [0, pos0) were brought up to date by shadow_sync_kernel and this
     // grid writes [pos0, pos0 + n) to both; without, the cache rows from pos0 up change under them.
-    if (a.wm && i == 0 && blockIdx.y == 0 && threadIdx.x == 0)
+    if (a.wm && i == 0 && threadIdx.x == 0)
         *a.wm = a.kb ? max(*a.wm, a.pos0 + a.n) : min(*a.wm, a.pos0);
-    __syncthreads();
-#pragma unroll
-    for (int jj = 0; jj < kPrepJobs; ++jj) {
-        const int job = blockIdx.y * kPrepWarps * kPrepJobs + jj * kPrepWarps + warp;
-        if (job >= n_jobs) continue;
+    __syncthreads();  // the barrier's initialisation and the rotation are visible to every thread
+    const uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
+    if (!mbar_wait_bounded(&bar, 0, deadline, &abort_s)) {
+        abort_s = 1;
+        if (a.err) *reinterpret_cast<volatile int*>(a.err) = KERR_TIMEOUT_FULL;
+        // the copies write this block's shared memory: let them land (bounded) before exiting
+        const uint64_t dd = deadline + kWaitLimitNs / 2;
+        while (!mbar_try_wait(&bar, 0) && globaltimer_ns() < dd) {
+        }
+        return;
+    }
+    for (int job = warp; job < n_jobs; job += kPrepWarps) {
         const bool is_q = job < a.q_headn, is_k = !is_q && job < a.q_headn + a.kv_headn;
         const int gi = is_q ? job : (is_k ? job - a.q_headn : job - a.q_headn - a.kv_headn);
+        float x[E];
+        load_vec<E>(rows + job * D + lane * E, x);
         if (is_q) {
-            norm_rope_vec<D>(x[jj], a.qg, a.qk_norm, a.eps, cs, sn, a.rope_pairs, lane);
+            norm_rope_vec<D>(x, a.qg, a.qk_norm, a.eps, cs, sn, a.rope_pairs, lane);
             const size_t o = (static_cast<size_t>(i) * a.q_headn + gi) * D + lane * E;
-            if (a.qf) store_vec_f32<E>(a.qf + o, x[jj]);
-            if (a.qb) store_vec16<__nv_bfloat16, E>(a.qb + o, x[jj]);
+            if (a.qf) store_vec_f32<E>(a.qf + o, x);
+            if (a.qb) store_vec16<__nv_bfloat16, E>(a.qb + o, x);
             continue;
         }
-        if (is_k) norm_rope_vec<D>(x[jj], a.kg, a.qk_norm, a.eps, cs, sn, a.rope_pairs, lane);
+        if (is_k) norm_rope_vec<D>(x, a.kg, a.qk_norm, a.eps, cs, sn, a.rope_pairs, lane);
         const size_t o = static_cast<size_t>(pos) * a.kv_dim + static_cast<size_t>(gi) * D + lane * E;
-        store_vec_kv<KV, E>(reinterpret_cast<KV*>(is_k ? a.kc : a.vc) + o, x[jj]);
+        store_vec_kv<KV, E>(reinterpret_cast<KV*>(is_k ? a.kc : a.vc) + o, x);
         __nv_bfloat16* shadow = is_k ? a.kb : a.vb;
-        if (shadow) store_vec16<__nv_bfloat16, E>(shadow + o, x[jj]);
+        if (shadow) store_vec16<__nv_bfloat16, E>(shadow + o, x);
     }
 }
 
