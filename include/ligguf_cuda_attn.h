@@ -122,6 +122,8 @@ int ligguf_cuda_attn_decode_async(ligguf_attn* h, int layer, int pos, const floa
  * mode: LIGGUF_MODE_SIMT (fp32) or LIGGUF_MODE_TC (bf16 tcgen05, fp32 accumulate). */
 int ligguf_cuda_attn_prefill(ligguf_attn* h, int layer, int pos0, int n, const float* q,
                              const float* k, const float* v, float* out, int mode);
+/* Same with device pointers on `stream`; d_q, d_k and d_v must be 16-byte aligned (their rows are
+ * bulk-copied), else LIGGUF_ATTN_EINVAL. */
 int ligguf_cuda_attn_prefill_async(ligguf_attn* h, int layer, int pos0, int n, const float* d_q,
                                    const float* d_k, const float* d_v, float* d_out, int mode,
                                    void* stream);
