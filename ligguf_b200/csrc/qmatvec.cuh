@@ -250,6 +250,12 @@ __device__ __forceinline__ void load8_a2(const uint8_t* p, uint32_t (&w)[8]) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) w[i] = __funnelshift_r(r[i], r[i + 1], sh);
 }
+// Same from a 16-byte aligned address: two 16-byte loads.
+__device__ __forceinline__ void load8_a16(const uint8_t* p, uint32_t (&w)[8]) {
+    const uint4 lo = lds128(p), hi = lds128(p + 16);
+    w[0] = lo.x; w[1] = lo.y; w[2] = lo.z; w[3] = lo.w;
+    w[4] = hi.x; w[5] = hi.y; w[6] = hi.z; w[7] = hi.w;
+}
 __device__ __forceinline__ void load8_a4(const uint8_t* p, uint32_t (&w)[8]) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) w[i] = reinterpret_cast<const uint32_t*>(p)[i];
@@ -476,7 +482,7 @@ struct WUnit<QT_Q4_K> {
     __device__ __forceinline__ void load(const uint8_t* row, int u) {
         const int s = u & 7;
         const uint8_t* blk = row + 144 * (u >> 3);
-        load8_a4(blk + 16 + 32 * (s >> 1), w);
+        load8_a16(blk + 16 + 32 * (s >> 1), w);  // 144-byte blocks: 16-byte aligned
         const int sh = 4 * (s & 1);
 #pragma unroll
         for (int i = 0; i < 8; ++i) w[i] = (w[i] >> sh) & 0x0F0F0F0Fu;
@@ -503,8 +509,8 @@ struct WUnit<QT_Q5_K> {
         const int s = u & 7;
         const uint8_t* blk = row + 176 * (u >> 3);
         uint32_t h[8];
-        load8_a4(blk + 48 + 32 * (s >> 1), w);
-        load8_a4(blk + 16, h);
+        load8_a16(blk + 48 + 32 * (s >> 1), w);  // 176-byte blocks: 16-byte aligned
+        load8_a16(blk + 16, h);
         const int sh = 4 * (s & 1);
 #pragma unroll
         for (int i = 0; i < 8; ++i) w[i] = ((w[i] >> sh) & 0x0F0F0F0Fu) | (((h[i] >> s) & 0x01010101u) << 4);
