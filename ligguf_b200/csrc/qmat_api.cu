@@ -17,6 +17,7 @@ using lgapi::fail;
 
 struct ligguf_qmat {
     int type = 0, n = 0, d = 0, device = 0, rb = 0;
+    int ktype = 0;             // the kernel's layout of the rows: type, or QT_Q8_0_G32 when repacked
     uint8_t* w = nullptr;      // d rows of rb bytes, allocation padded to a 16-byte multiple
     int* h_err = nullptr;      // mapped pinned error word of the kernels that read this matrix
     int* d_err = nullptr;
@@ -177,7 +178,7 @@ int matmul_enqueue(const ligguf_qmat* const* ws, float* const* outs, const long 
         m.w = w->w;
         m.out = outs[i];
         m.out_stride = out_strides[i];
-        m.type = w->type;
+        m.type = w->ktype;
         m.rows = w->d;
         m.rb = w->rb;
         m.tile_rows = tile_rows(w->rb);
@@ -325,6 +326,26 @@ int ligguf_cuda_qmat_init_cols(int type, int n, int d, const void* rows, int col
         return fail(LIGGUF_ATTN_ENOMEM, "weight matrix of %zu bytes", bytes);
     }
     *w->h_err = 0;
+    w->ktype = type;
+    // Q8_0 rows of a multiple of 1024 elements: repacked into groups of 32 blocks (the values of the
+    // 32 blocks, then their scales; same bytes), so the kernel reads each unit with aligned loads.
+    if (type == lg::QT_Q8_0 && n % 1024 == 0 && bytes > 0) {
+        uint8_t* tmp = nullptr;
+        const size_t n_blocks = bytes / 34;
+        bool ok = cudaMalloc(&tmp, bytes) == cudaSuccess &&
+                  cudaMemcpyAsync(tmp, w->w, bytes, cudaMemcpyDeviceToDevice, w->stream) == cudaSuccess;
+        if (ok) {
+            lg::repack_q80_g32_kernel<<<unsigned((n_blocks + 255) / 256), 256, 0, w->stream>>>(tmp, w->w, n_blocks);
+            ok = cudaGetLastError() == cudaSuccess && cudaStreamSynchronize(w->stream) == cudaSuccess;
+        }
+        if (tmp) cudaFree(tmp);
+        if (!ok) {
+            (void)cudaGetLastError();
+            ligguf_cuda_qmat_free(w);
+            return fail(LIGGUF_ATTN_ENOMEM, "repacking a Q8_0 matrix of %zu bytes", bytes);
+        }
+        w->ktype = lg::QT_Q8_0_G32;
+    }
     *out = w;
     return LIGGUF_ATTN_OK;
 }

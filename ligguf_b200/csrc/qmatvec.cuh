@@ -32,7 +32,8 @@ namespace lg {
 
 // GGUF type numbers (fast/lil_gguf.h:26-44).
 enum : int { QT_F32 = 0, QT_F16 = 1, QT_Q8_0 = 8, QT_Q2_K = 10, QT_Q3_K = 11, QT_Q4_K = 12, QT_Q5_K = 13,
-             QT_Q6_K = 14, QT_Q1_0 = 40, QT_Q1_G = 41 };
+             QT_Q6_K = 14, QT_Q1_0 = 40, QT_Q1_G = 41,
+             QT_Q8_0_G32 = 108 };  // (internal) Q8_0 repacked at upload, see WUnit<QT_Q8_0_G32>
 
 // Bytes and elements of one block of a type (fast/lil_gguf.h:64-119); 0 for an unknown type.
 __host__ __device__ constexpr int qt_block_bytes(int t) {
@@ -47,7 +48,9 @@ __host__ __device__ constexpr int qt_block_elems(int t) {
 // Which activation form a type's dot reads (matmul3 quantizes to Q8_0 for Q8_0/Q1_0/Q1_G,
 // fast/lil_math.cpp:830-834; the engine passes the Q8_K form for the K-quants, :39-40).
 __host__ __device__ constexpr bool qt_uses_q8k(int t) { return t >= QT_Q2_K && t <= QT_Q6_K; }
-__host__ __device__ constexpr bool qt_uses_q80(int t) { return t == QT_Q8_0 || t == QT_Q1_0 || t == QT_Q1_G; }
+__host__ __device__ constexpr bool qt_uses_q80(int t) {
+    return t == QT_Q8_0 || t == QT_Q8_0_G32 || t == QT_Q1_0 || t == QT_Q1_G;
+}
 __host__ __device__ constexpr bool qt_uses_f32(int t) { return t == QT_F32 || t == QT_F16; }
 
 // 7 consumer warps + 1 producer warp, two CTAs per SM (14 consumer warps per SM; the consumers are
@@ -371,6 +374,37 @@ struct WUnit<QT_Q8_0> {
         return d * A.d0[u] * static_cast<float>(dot4(w, a) + dot4(w + 4, a + 4));
     }
 };
+// Q8_0 repacked at upload (rows of a multiple of 1024 elements): per group of 32 units (32
+// blocks, 1088 bytes, as many as in the GGUF layout) the 32 x 32 int8 values first, then the 32
+// fp16 scales, so a unit's values are two aligned 16-byte loads instead of nine 4-byte loads and
+// eight funnel shifts of a 2-byte aligned block.  Same values, same dot.
+template <>
+struct WUnit<QT_Q8_0_G32> {
+    uint32_t w[8];
+    float d;
+    __device__ __forceinline__ void load(const uint8_t* row, int u) {
+        const uint8_t* grp = row + 1088 * (u >> 5);
+        load8_a16(grp + 32 * (u & 31), w);
+        d = h2f(lds16(grp + 1024 + 2 * (u & 31)));
+    }
+    __device__ __forceinline__ float dot(const QmvActView& A, int u) const {
+        int a[8];
+        act_words(A.q0, u, a);
+        return d * A.d0[u] * static_cast<float>(dot4(w, a) + dot4(w + 4, a + 4));
+    }
+};
+// The repack: GGUF Q8_0 rows (src) -> groups of 32 blocks as above (dst), one thread per block.
+__global__ void __launch_bounds__(256) repack_q80_g32_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
+                                                            size_t n_blocks) {
+    const size_t b = blockIdx.x * size_t(256) + threadIdx.x;
+    if (b >= n_blocks) return;
+    const uint8_t* blk = src + 34 * b;
+    uint8_t* grp = dst + 1088 * (b >> 5);
+    const int j = int(b & 31);
+    for (int i = 0; i < 32; ++i) grp[32 * j + i] = blk[2 + i];
+    grp[1024 + 2 * j] = blk[0];
+    grp[1024 + 2 * j + 1] = blk[1];
+}
 // Q1_0 (dot_q8_0_q1_0): block = unit, {fp16 d, 32 sign bits}; weight = bit ? +1 : -1, so the dot is
 // 2 * (sum of x where the bit is set) - (sum of all x).
 __device__ __forceinline__ int sign_dot(const uint32_t* w, const int* a) {
@@ -710,6 +744,7 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const __grid_consta
             LG_QMV_CASE(QT_F32)
             LG_QMV_CASE(QT_F16)
             LG_QMV_CASE(QT_Q8_0)
+            LG_QMV_CASE(QT_Q8_0_G32)
             LG_QMV_CASE(QT_Q1_0)
             LG_QMV_CASE(QT_Q1_G)
             LG_QMV_CASE(QT_Q2_K)
