@@ -640,6 +640,11 @@ def extra_decode_graph(peaks, w):
                        "; inputs larger than L2, replays back to back")}
 
 
+# FP32 FMA peak of one B200 (the SIMT paths' roofline): 148 SMs x 128 FP32 lanes x 2 FLOP per FMA x
+# the 1965 MHz maximum SM clock; nominal (MEASURED_PEAKS.json holds no FP32 figure).
+FP32_FMA_PEAK_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
+
+
 def extra_prefill(peaks, mode):
     import torch
     from ligguf_b200 import AttnConfig, CudaAttention, synth_fill
@@ -673,6 +678,9 @@ def extra_prefill(peaks, mode):
     tf = flops / (ms * 1e-3) / 1e12
     peak = peaks["bf16_tflops"] if mode == 1 else None
     r = {"ms_36_layers": ms, "tflops": tf, "causal_flops": flops}
+    if mode == 0:
+        r["frac_of_fp32_fma_peak"] = tf / FP32_FMA_PEAK_TFLOPS
+        r["fp32_fma_peak_tflops"] = FP32_FMA_PEAK_TFLOPS
     if peak:
         r["frac_of_bf16_peak"] = tf / peak
     return r
@@ -700,6 +708,9 @@ def extra_bert(peaks, mode):
     flops = w.flops_per_layer() * w.n_layers
     tf = flops / (ms * 1e-3) / 1e12
     r = {"ms_12_layers": ms, "tflops": tf, "flops": flops}
+    if mode == 0:
+        r["frac_of_fp32_fma_peak"] = tf / FP32_FMA_PEAK_TFLOPS
+        r["fp32_fma_peak_tflops"] = FP32_FMA_PEAK_TFLOPS
     if mode == 1:
         r["frac_of_bf16_peak"] = tf / peaks["bf16_tflops"]
     return r
