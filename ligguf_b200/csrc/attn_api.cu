@@ -97,37 +97,114 @@ __global__ void kv_synth_kernel(T* layer_base, int kv_dim, int kv_dim_full, int 
 float synth_mul(float scale) { return static_cast<float>(static_cast<double>(scale) / lg::kSynthSd); }
 
 // ---------------------------------------------------------------------------- gather wait
-// Gather wait: one thread per element polls its 64-bit word in this rank's gather slot until the
-// word carries the call's epoch (bounded), then writes the fp32 value to `out`.  The epoch is
-// gstate[0] + 1 (gstate[0] = the last completed call's epoch, advanced here by the last block to
-// finish, gstate[1] counting the finished blocks), the slot is epoch & 1: nothing of a call is
-// decided on the host, so a captured CUDA graph replays correctly.  Launched as a programmatic
-// dependent of the decode kernel, it starts while the decode still runs; it reads nothing the decode
-// writes other than these self-validating words, so it never waits for the decode grid itself (the
-// decode reads gstate[0] only after this kernel's predecessor completed, and the next decode only
-// after this one completed).
+// Gather wait: one thread per element polls its 64-bit words in this rank's gather slot until they
+// carry the call's epoch (bounded), then writes the fp32 value to `out`.  The head's count word says
+// what the shard stored: 1, the normalised output in group 0; G > 1, G first-level merge groups
+// (o unnormalised, m, l), which are merged here as the shard's second merge level would have (weights
+// e^(m_g - M), out = sum w_g o_g / sum w_g l_g).  All of an element's words are loaded before any is
+// checked, so the polls overlap.  The epoch is gstate[0] + 1 (gstate[0] = the last completed call's
+// epoch, advanced here by the last block to finish, gstate[1] counting the finished blocks), the slot
+// is epoch & 1: nothing of a call is decided on the host, so a captured CUDA graph replays correctly.
+// Launched as a programmatic dependent of the decode kernel, it starts while the decode still runs;
+// it reads nothing the decode writes other than these self-validating words, so it never waits for
+// the decode grid itself (the decode reads gstate[0] only after this kernel's predecessor completed,
+// and the next decode only after this one completed).
+__device__ __forceinline__ unsigned long long ld_word(const unsigned long long* p) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+
 __global__ void __launch_bounds__(256) gather_wait_kernel(const unsigned long long* words_base, int* gstate,
-                                                          float* out, int n, int* err) {
+                                                          float* out, int heads, int d, int* err) {
+    constexpr int G = lg::kGatherGroups;
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int epoch = __ldcg(gstate) + 1;
-    const unsigned long long* words = words_base + size_t(epoch & 1) * n;
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) {
+    const size_t vec = size_t(heads) * d;
+    const unsigned long long* slot = words_base + size_t(epoch & 1) * lg::gather_slot_words(heads, d);
+    const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < vec) {
+        const int h = static_cast<int>(i / d);
         const uint64_t deadline = lg::globaltimer_ns() + lg::kWaitLimitNs;
         const uint32_t want = static_cast<uint32_t>(epoch);
-        unsigned long long w;
+        auto cur = [want](unsigned long long w) { return static_cast<uint32_t>(w >> 32) == want; };
+        auto val = [](unsigned long long w) { return __uint_as_float(static_cast<uint32_t>(w)); };
+        const unsigned long long* pc = slot + lg::gather_cnt_off(heads, d) + h;
+        const unsigned long long* pm = slot + lg::gather_m_off(heads, d) + h;
+        const unsigned long long* pl = slot + lg::gather_l_off(heads, d) + h;
+        unsigned long long wc = ld_word(pc), wo[G], wm[G], wl[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) wo[g] = wm[g] = wl[g] = 0ull;
         uint32_t spins = 0;
+        int ng = 0;  // groups of this element, once its count word is current
         bool ok = true;
         while (true) {
-            asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(words + i) : "memory");
-            if (static_cast<uint32_t>(w >> 32) == want) break;
+            bool done = false;
+            if (!ng && cur(wc)) {
+                ng = static_cast<int>(static_cast<uint32_t>(wc));
+                if (ng < 1 || ng > G) {  // not a count this library stores
+                    *reinterpret_cast<volatile int*>(err) = lg::KERR_TIMEOUT_PEER;
+                    ok = false;
+                    break;
+                }
+#pragma unroll
+                for (int g = 0; g < G; ++g)
+                    if (g < ng) {
+                        wo[g] = ld_word(slot + g * vec + i);
+                        if (ng > 1) {
+                            wm[g] = ld_word(pm + g * heads);
+                            wl[g] = ld_word(pl + g * heads);
+                        }
+                    }
+            }
+            if (ng) {
+                done = true;
+#pragma unroll
+                for (int g = 0; g < G; ++g)
+                    if (g < ng) {
+                        if (!cur(wo[g])) {
+                            done = false;
+                            wo[g] = ld_word(slot + g * vec + i);
+                        }
+                        if (ng > 1 && !cur(wm[g])) {
+                            done = false;
+                            wm[g] = ld_word(pm + g * heads);
+                        }
+                        if (ng > 1 && !cur(wl[g])) {
+                            done = false;
+                            wl[g] = ld_word(pl + g * heads);
+                        }
+                    }
+            } else {
+                wc = ld_word(pc);
+            }
+            if (done) break;
             if ((++spins & 63u) == 0u && lg::globaltimer_ns() > deadline) {
                 *reinterpret_cast<volatile int*>(err) = lg::KERR_TIMEOUT_PEER;
                 ok = false;
                 break;
             }
         }
-        if (ok) out[i] = __uint_as_float(static_cast<uint32_t>(w));
+        if (ok) {
+            if (ng == 1) {
+                out[i] = val(wo[0]);
+            } else {
+                float M = -INFINITY;
+#pragma unroll
+                for (int g = 0; g < G; ++g)
+                    if (g < ng) M = fmaxf(M, val(wm[g]));
+                float L = 0.f, O = 0.f;
+#pragma unroll
+                for (int g = 0; g < G; ++g)
+                    if (g < ng) {
+                        const float mv = val(wm[g]);
+                        const float w = mv == -INFINITY ? 0.f : expf(mv - M);
+                        L = fmaf(val(wl[g]), w, L);
+                        O = fmaf(val(wo[g]), w, O);
+                    }
+                out[i] = O / L;
+            }
+        }
     }
     __syncthreads();
     if (threadIdx.x == 0 && atomicAdd(&gstate[1], 1) == static_cast<int>(gridDim.x) - 1) {
@@ -177,7 +254,7 @@ struct ligguf_attn {
     alignas(64) CUtensorMap tm_k;
     alignas(64) CUtensorMap tm_v;
     // SARA gather over CUDA IPC
-    unsigned long long* gbuf = nullptr;  // [2][n_heads*D] gather words: (epoch << 32) | fp32 bits
+    unsigned long long* gbuf = nullptr;  // [2][gather_slot_words] gather words: (epoch << 32) | 32 bits
     size_t gbuf_bytes = 0;
     int g_nranks = 0, g_rank = -1;
     bool g_pending = false;   // a gathered decode was enqueued and its wait not yet
@@ -340,6 +417,9 @@ int decode_enqueue(ligguf_attn* h, int layer, int pos, const float* dq, const fl
         a.dynamic = a.n_split > 1;
     }
     a.n_split = std::max(1, a.n_split);
+    // First-level merge groups: as large as one copy into the ring allows; a gathered decode spreads
+    // its splits over up to kGatherGroups smaller groups instead, whose results the gather wait merges.
+    a.merge_group = gather ? std::min(mg, std::max(1, ceil_div(a.n_split, lg::kGatherGroups))) : mg;
     a.chunk_ctr = h->counters + kvh;
     a.kv_dim = h->kv_dim;
     a.rope_pairs = h->rope_pairs;
@@ -354,6 +434,7 @@ int decode_enqueue(ligguf_attn* h, int layer, int pos, const float* dq, const fl
         a.peer_ll = h->d_peer_ll;
         a.nranks = h->g_nranks;
         a.rank = h->g_rank;
+        a.g_heads = c.n_heads;
         a.q_off = c.kv_head0 * h->nrep * D;
         a.epoch = h->d_gstate;
     }
@@ -1087,7 +1168,7 @@ int ligguf_cuda_attn_gather_ipc_handle(ligguf_attn* h, void* handle_out, size_t 
         return fail(LIGGUF_ATTN_EINVAL, "handle buffer of %zu bytes (need %zu)", handle_size, sizeof(cudaIpcMemHandle_t));
     DeviceGuard dg(h->cfg.device);
     if (!h->gbuf) {
-        h->gbuf_bytes = 2 * size_t(h->cfg.n_heads) * h->cfg.head_dim * sizeof(unsigned long long);
+        h->gbuf_bytes = 2 * lg::gather_slot_words(h->cfg.n_heads, h->cfg.head_dim) * sizeof(unsigned long long);
         if (cudaMalloc(reinterpret_cast<void**>(&h->gbuf), h->gbuf_bytes) != cudaSuccess)
             return fail(LIGGUF_ATTN_ENOMEM, "gather buffer");
         LG_CUDA(cudaMemset(h->gbuf, 0, h->gbuf_bytes));
@@ -1105,7 +1186,7 @@ int ligguf_cuda_attn_gather_open(ligguf_attn* h, int nranks, int rank, const voi
     if (!h->gbuf) return fail(LIGGUF_ATTN_ESTATE, "call ligguf_cuda_attn_gather_ipc_handle first");
     if (h->g_nranks) return fail(LIGGUF_ATTN_ESTATE, "gather already open");
     DeviceGuard dg(h->cfg.device);
-    const size_t vec = size_t(h->cfg.n_heads) * h->cfg.head_dim;
+    const size_t slot_words = lg::gather_slot_words(h->cfg.n_heads, h->cfg.head_dim);
     std::vector<unsigned long long*> slots(2 * nranks);
     h->g_opened.assign(nranks, nullptr);
     for (int r = 0; r < nranks; ++r) {
@@ -1120,7 +1201,7 @@ int ligguf_cuda_attn_gather_open(ligguf_attn* h, int nranks, int rank, const voi
             h->g_opened[r] = p;
             base = static_cast<unsigned long long*>(p);
         }
-        for (int slot = 0; slot < 2; ++slot) slots[slot * nranks + r] = base + slot * vec;
+        for (int slot = 0; slot < 2; ++slot) slots[slot * nranks + r] = base + slot * slot_words;
     }
     LG_CUDA(cudaMalloc(reinterpret_cast<void**>(&h->d_peer_ll), slots.size() * sizeof(unsigned long long*)));
     LG_CUDA(cudaMemcpy(h->d_peer_ll, slots.data(), slots.size() * sizeof(unsigned long long*), cudaMemcpyHostToDevice));
@@ -1159,7 +1240,7 @@ int ligguf_cuda_attn_gather_wait_async(ligguf_attn* h, int layer, float* d_out, 
     lc.attrs = attr;
     lc.numAttrs = 1;
     LG_CUDA(cudaLaunchKernelEx(&lc, gather_wait_kernel, static_cast<const unsigned long long*>(h->gbuf), h->d_gstate,
-                               d_out, vec, h->d_err));
+                               d_out, h->cfg.n_heads, h->cfg.head_dim, h->d_err));
     LG_CUDA(cudaGetLastError());
     h->g_pending = false;
     return LIGGUF_ATTN_OK;

@@ -20,7 +20,9 @@
 // the nrep q vectors, a transposed butterfly reduces nrep*4 dot products with one shuffle per
 // result), an online softmax per tile, P.V accumulation in registers.  The last CTA of a KV head
 // (atomic ticket) merges the splits' (max, sum, o) partials and writes the output, so the whole
-// layer is one launch.  The CTA holding position pos-1 also folds in the current token.
+// layer is one launch.  The CTA holding position pos-1 also folds in the current token.  A gathered
+// (multi-GPU) decode with many splits stops after the first merge level: each group's merger stores
+// the group's (max, sum, o) into every rank's gather slot, and the gather wait merges the groups.
 //
 // Every wait is bounded (kWaitLimitNs): a wait that gives up raises a shared abort flag, writes the
 // error word and lets the kernel finish without writing its output.
@@ -50,6 +52,26 @@ __host__ __device__ constexpr int decode_merge_group(int nrep, int d) {
                : 48;
 }
 
+// Multi-GPU gather words.  With up to kGatherGroups first-level merge groups per KV head, a gathered
+// decode stores each group's (o, m, l) and the gather wait on every rank merges them, instead of a
+// second merge level on the shard's GPU.
+constexpr int kGatherGroups = 8;
+// One gather slot (one per epoch parity), in 64-bit words, for `heads` q heads of `d`:
+//   o[kGatherGroups][heads * d]   group results (unnormalised), or the output in group 0
+//   m[kGatherGroups][heads], l[kGatherGroups][heads]
+//   cnt[heads]                    the number of groups the head's words carry (1: normalised output)
+// padded to 32 words, so that both slots start on 256 bytes (the o words take 16-byte stores).
+__host__ __device__ constexpr size_t gather_slot_words(int heads, int d) {
+    return (size_t(kGatherGroups) * heads * d + 2 * size_t(kGatherGroups) * heads + heads + 31) & ~size_t(31);
+}
+__host__ __device__ constexpr size_t gather_m_off(int heads, int d) { return size_t(kGatherGroups) * heads * d; }
+__host__ __device__ constexpr size_t gather_l_off(int heads, int d) {
+    return gather_m_off(heads, d) + size_t(kGatherGroups) * heads;
+}
+__host__ __device__ constexpr size_t gather_cnt_off(int heads, int d) {
+    return gather_l_off(heads, d) + size_t(kGatherGroups) * heads;
+}
+
 struct DecodeArgs {
     const float* q;     // [q_headn][D] raw q of this layer
     const float* k;     // [kv_headn][D] raw k
@@ -67,9 +89,10 @@ struct DecodeArgs {
     int* err;           // error word (mapped host memory)
     int* shadow_wm;     // the layer's bf16-shadow watermark (tensor-core prefill): lowered to pos
     unsigned long long* const* peer_ll;  // multi-GPU gather (or null): [2][nranks] gather slots of
-                                         // [n_heads*D] words, slot = call epoch & 1
+                                         // gather_slot_words(g_heads, D) words, slot = call epoch & 1
     int nranks;
     int rank;
+    int g_heads;        // q heads of the whole model (the gathered vector holds g_heads * D)
     int q_off;          // element offset of this shard's heads in the gathered vector
     int kv_head0;       // global index of this shard's first KV head (gather flag slot)
     const int* epoch;   // gather: the last completed call's epoch (device); this call's is one more
@@ -82,6 +105,7 @@ struct DecodeArgs {
     int dynamic;        // 0: the static chunks cover all tiles (n_split*chunk >= n_tiles), no grabs
     int* chunk_ctr;     // = counters + kv_headn
     int n_split;
+    int merge_group;    // splits per first-level merge group (at most decode_merge_group)
     int kv_dim;
     int rope_pairs;
     int qk_norm;
@@ -792,11 +816,14 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
     if (*stop_s) return;
 
     const int head0 = g * NREP;
+    int grp_out = 0, n_out = 1;  // gather: the group this CTA's words carry, of how many (1: the output)
     if (a.n_split > 1) {
-        // Two-level merge: the last CTA of each group of Sm::kMergeGroup splits merges the group,
-        // then (with more than one group) the last group merger merges the group results.
+        // Two-level merge: the last CTA of each group of a.merge_group splits merges the group,
+        // then (with more than one group) the last group merger merges the group results.  A
+        // gathered decode with at most kGatherGroups groups skips the second level: each group
+        // merger stores its group's result and the gather wait of every rank merges them.
         constexpr int PS = decode_part_stride(NREP, D);
-        constexpr int GRP = Sm::kMergeGroup;
+        const int GRP = a.merge_group;  // <= Sm::kMergeGroup, so that a group's copy fits the ring
         const int kvh = a.kv_dim / D;
         float* pp = a.part + (static_cast<size_t>(g) * kDecodeMaxSplit + split) * PS;
         for (int idx = tid; idx < NREP * D; idx += kDecodeConsumers) pp[idx] = o_s[idx];
@@ -818,24 +845,40 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
                                      a.err))
             return;
         if (tid == 0) *grp_ctr = 0;
-        if (n_groups > 1) {
-            float* gp = a.gpart + (static_cast<size_t>(g) * kDecodeMaxGroups + grp) * PS;
-            for (int idx = tid; idx < NREP * D; idx += kDecodeConsumers) gp[idx] = o_s[idx];
-            if (tid < NREP) {
-                gp[NREP * D + tid] = m_s[tid];
-                gp[NREP * D + NREP + tid] = l_s[tid];
+        if (a.peer_ll && n_groups > 1 && n_groups <= kGatherGroups) {
+            grp_out = grp;
+            n_out = n_groups;
+            // With grabs, the last group merger of the head (head ticket) frees the grab counter:
+            // every CTA of the head took its group ticket after its last grab.
+            if (a.dynamic) {
+                if (tid == 0) *last_s = (ticket_acq_rel(&a.counters[g]) == n_groups - 1) ? 1 : 0;
+                named_bar_sync(1, kDecodeConsumers);
+                if (tid == 0 && *last_s) {
+                    a.counters[g] = 0;
+                    a.chunk_ctr[g] = 0;
+                }
             }
-            named_bar_sync(1, kDecodeConsumers);
-            if (tid == 0) *last_s = (ticket_acq_rel(&a.counters[g]) == n_groups - 1) ? 1 : 0;
-            named_bar_sync(1, kDecodeConsumers);
-            if (!*last_s) return;
-            if (!merge_partials<NREP, D>(a.gpart + static_cast<size_t>(g) * kDecodeMaxGroups * PS, n_groups, tiles,
-                                         sc, merge_bar, 1, o_s, m_s, l_s, tid, warp, lane, deadline, abort_s, a.err))
-                return;
-            if (tid == 0) a.counters[g] = 0;
+        } else {
+            if (n_groups > 1) {
+                float* gp = a.gpart + (static_cast<size_t>(g) * kDecodeMaxGroups + grp) * PS;
+                for (int idx = tid; idx < NREP * D; idx += kDecodeConsumers) gp[idx] = o_s[idx];
+                if (tid < NREP) {
+                    gp[NREP * D + tid] = m_s[tid];
+                    gp[NREP * D + NREP + tid] = l_s[tid];
+                }
+                named_bar_sync(1, kDecodeConsumers);
+                if (tid == 0) *last_s = (ticket_acq_rel(&a.counters[g]) == n_groups - 1) ? 1 : 0;
+                named_bar_sync(1, kDecodeConsumers);
+                if (!*last_s) return;
+                if (!merge_partials<NREP, D>(a.gpart + static_cast<size_t>(g) * kDecodeMaxGroups * PS, n_groups,
+                                             tiles, sc, merge_bar, 1, o_s, m_s, l_s, tid, warp, lane, deadline,
+                                             abort_s, a.err))
+                    return;
+                if (tid == 0) a.counters[g] = 0;
+            }
+            // Every CTA of this head took its group ticket after its last grab: the counter is free.
+            if (tid == 0) a.chunk_ctr[g] = 0;
         }
-        // Every CTA of this head took its group ticket after its last grab: the counter is free.
-        if (tid == 0) a.chunk_ctr[g] = 0;
     }
     if (a.peer_ll) {
         // The next layer's decode may start once the gathered words have arrived, before this grid
@@ -844,21 +887,43 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
             __threadfence();
             named_bar_sync(1, kDecodeConsumers);
         }
-        // Multi-GPU gather: every output element goes to every rank's gather slot as one 64-bit word,
+        // Multi-GPU gather: every value goes to every rank's gather slot as one 64-bit word,
         // (epoch << 32) | fp32 bits, stored with a single relaxed system-scope store.  A reader that
         // sees the current epoch in a word has that word's value: no fence, no flags.
         // The epoch lives in device memory (the gather wait of the previous call advanced it), so a
-        // captured CUDA graph replays correctly.  Two consecutive elements per 16-byte store.
+        // captured CUDA graph replays correctly.  Two consecutive elements per 16-byte store.  One
+        // group: the normalised output; several: this group's o (unnormalised), m and l.  Each head's
+        // count word tells the readers which.
         const int epoch = __ldcg(a.epoch) + 1;
         unsigned long long* const* peers = a.peer_ll + (epoch & 1) * a.nranks;
         const unsigned long long tag = static_cast<unsigned long long>(static_cast<uint32_t>(epoch)) << 32;
+        const size_t vec = static_cast<size_t>(a.g_heads) * D;
+        const size_t obase = static_cast<size_t>(grp_out) * vec + a.q_off + static_cast<size_t>(head0) * D;
         for (int idx = 2 * tid; idx < NREP * D; idx += 2 * kDecodeConsumers) {
-            const unsigned long long w0 = tag | __float_as_uint(o_s[idx] / l_s[idx / D]);
-            const unsigned long long w1 = tag | __float_as_uint(o_s[idx + 1] / l_s[(idx + 1) / D]);
-            const size_t e = static_cast<size_t>(a.q_off) + static_cast<size_t>(head0) * D + idx;
+            const float v0 = n_out == 1 ? o_s[idx] / l_s[idx / D] : o_s[idx];
+            const float v1 = n_out == 1 ? o_s[idx + 1] / l_s[(idx + 1) / D] : o_s[idx + 1];
+            const unsigned long long w0 = tag | __float_as_uint(v0);
+            const unsigned long long w1 = tag | __float_as_uint(v1);
             for (int rr = 0; rr < a.nranks; ++rr)
-                asm volatile("st.relaxed.sys.global.v2.b64 [%0], {%1, %2};" ::"l"(peers[rr] + e), "l"(w0), "l"(w1)
+                asm volatile("st.relaxed.sys.global.v2.b64 [%0], {%1, %2};" ::"l"(peers[rr] + obase + idx), "l"(w0),
+                             "l"(w1)
                              : "memory");
+        }
+        if (tid < NREP) {
+            const size_t qh = static_cast<size_t>(a.q_off / D + head0 + tid);  // global q head
+            const size_t mo = gather_m_off(a.g_heads, D) + static_cast<size_t>(grp_out) * a.g_heads + qh;
+            const size_t lo = gather_l_off(a.g_heads, D) + static_cast<size_t>(grp_out) * a.g_heads + qh;
+            const size_t co = gather_cnt_off(a.g_heads, D) + qh;
+            const unsigned long long wm = tag | __float_as_uint(m_s[tid]);
+            const unsigned long long wl = tag | __float_as_uint(l_s[tid]);
+            const unsigned long long wc = tag | static_cast<uint32_t>(n_out);
+            for (int rr = 0; rr < a.nranks; ++rr) {
+                if (n_out > 1) {
+                    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(peers[rr] + mo), "l"(wm) : "memory");
+                    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(peers[rr] + lo), "l"(wl) : "memory");
+                }
+                asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(peers[rr] + co), "l"(wc) : "memory");
+            }
         }
         return;
     }

@@ -381,3 +381,50 @@ def test_self_gather_epochs_advance_on_device_and_replay(gpu):
     check()
     del g
     h.close()
+
+
+@pytest.mark.parametrize("H,Hk,kv_type", [
+    (4, 1, 0),   # one KV head at 32K (the 8-GPU shard's shape): 256 static splits in 6 merge groups
+    (4, 1, 1),   # the same in fp16: 256 splits of 2 tiles, 6 groups
+    (16, 4, 0),  # four KV heads: 74 splits per head with grabs, in 2 groups
+])
+def test_self_gather_merges_group_results(gpu, H, Hk, kv_type):
+    """A gathered decode with several first-level merge groups per KV head stores each group's
+    (max, sum, o) and the gather wait merges them, in place of a second merge level on the shard's
+    GPU.  With grabs, the head's last group merger frees the grab counter, so repeated calls (direct,
+    then from a CUDA graph) must each see zeroed counters.  A one-rank gather of the whole model
+    exercises the same words as a multi-GPU one; every output equals the reference's."""
+    import torch
+    port = orc.Checker("port")
+    pos = 32768
+    c = cases.decode_case(H=H, Hk=Hk, D=128, n_ctx=pos + 64, kv_type=kv_type, theta=1e6, qk_norm=1, pos=pos,
+                          seed=70 + H + kv_type, layer=0)
+    h = make_handle(c)
+    h.kv_synth(0, 1, 0, pos, c["seed"], c["scale"])
+    h.gather_open(0, [h.gather_ipc_handle()])
+    dev = torch.device("cuda", 0)
+    q, k, v = (torch.from_numpy(np.ascontiguousarray(c[x])).to(dev) for x in ("q", "k", "v"))
+    out = torch.full((H * 128,), float("nan"), device=dev)
+    ref, _, _ = cases.run_decode(port, c)
+
+    def step():
+        h.decode_gather_async(0, pos, q, k, v)
+        h.gather_wait_async(0, out)
+
+    def check():
+        torch.cuda.synchronize()
+        h.sync()
+        assert cases.rel_err(out.cpu().numpy(), ref) <= TOL
+        out.fill_(float("nan"))
+
+    for _ in range(3):
+        step()
+        check()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    for _ in range(3):
+        g.replay()
+        check()
+    del g
+    h.close()
