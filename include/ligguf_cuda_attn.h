@@ -164,12 +164,14 @@ int ligguf_cuda_attn_sync(ligguf_attn* h);
 /* ---- SARA all-gather over NVLink peer memory -------------------------------------------- */
 /* The reference's SARA run reduces per-rank partials over TCP (cpp/ligguf_distrib.cpp:1025-1047).
  * Here every rank owns a KV-head slice and the per-head outputs are all-gathered.  These calls
- * set up a gather buffer of 2 x [n_heads*head_dim] 64-bit words per rank, shared through CUDA
- * IPC; decode_gather then stores this rank's head outputs straight into every peer's buffer from
- * the decode kernel's epilogue, each element as one word (call epoch << 32 | fp32 bits), so a
- * reader that sees the current epoch in a word has its value; gather_wait polls (bounded) until
- * every word of the call carries its epoch and writes the full fp32 vector to d_out.  The two
- * calls alternate between the two halves of the buffer. */
+ * set up a gather buffer of two slots of 64-bit words per rank (per slot: up to 8 merge groups of
+ * [n_heads*head_dim] values plus their per-head max and sum, and a count word per head), shared
+ * through CUDA IPC; decode_gather then stores this rank's results straight into every peer's
+ * buffer from the decode kernel's epilogue, each value as one word (call epoch << 32 | 32 bits),
+ * so a reader that sees the current epoch in a word has its value.  A head with one merge group
+ * sends its output; a head split over several groups sends each group's (max, sum, o) and the
+ * readers merge them.  gather_wait polls (bounded) until every word of the call carries its epoch
+ * and writes the full fp32 vector to d_out.  The two calls alternate between the two slots. */
 int ligguf_cuda_attn_gather_ipc_handle(ligguf_attn* h, void* handle_out /* 64 bytes */,
                                        size_t handle_size);
 int ligguf_cuda_attn_gather_open(ligguf_attn* h, int nranks, int rank,
