@@ -189,6 +189,35 @@ def test_decode_host_pinned_buffers(gpu):
     h.close()
 
 
+@pytest.mark.parametrize("H,Hk,D,kv_type", [
+    (32, 8, 128, 0),  # Qwen3-8B heads, fp32 cache
+    (64, 8, 128, 1),  # nrep 8, fp16: the prologue's second round of jobs reads q, k, v again
+    (64, 8, 64, 2),   # nrep 8, head_dim 64, bf16
+])
+def test_decode_host_call_and_device_call_alternate(gpu, H, Hk, D, kv_type):
+    """The host-pointer call (one staging copy of q, k, v) alternates with the device-pointer call on
+    the same handle, at positions 0, 1 and 700: every output equals the reference's."""
+    import torch
+    port = orc.Checker("port")
+    for pos in (0, 1, 700):
+        c = cases.decode_case(H=H, Hk=Hk, D=D, n_ctx=768, theta=1e6, qk_norm=1, kv_type=kv_type, pos=pos,
+                              seed=80 + pos, scale=1.0 if D == 128 else 0.125, layer=0)
+        h = make_handle(c)
+        out, krow, vrow, _ = gpu_decode(c, h)
+        ref, kref, vref = cases.run_decode(port, c)
+        assert cases.rel_err(out, ref) <= TOL, pos
+        assert np.array_equal(vrow, vref), pos
+        dev = torch.device("cuda", 0)
+        qd, kd, vd = (torch.from_numpy(np.ascontiguousarray(c[x])).to(dev) for x in ("q", "k", "v"))
+        od = torch.empty(H * D, device=dev)
+        h.decode_async(0, pos, qd, kd, vd, od)
+        torch.cuda.synchronize()
+        h.sync()
+        assert cases.rel_err(od.cpu().numpy(), ref) <= TOL, pos
+        assert cases.rel_err(h.decode(0, pos, c["q"], c["k"], c["v"]), ref) <= TOL, pos
+        h.close()
+
+
 def test_back_to_back_steps_read_the_rows_they_append(gpu):
     """Decode steps launched back to back on one stream with no host synchronisation, alternating two
     layers: every step reads the row its layer's previous step appended.  (A decode may start loading
