@@ -713,6 +713,16 @@ def extra_bert(peaks, mode):
         r["fp32_fma_peak_tflops"] = FP32_FMA_PEAK_TFLOPS
     if mode == 1:
         r["frac_of_bf16_peak"] = tf / peaks["bf16_tflops"]
+    # The layer's roofline is the slower of its arithmetic at peak and its fp32 interface in HBM (the
+    # valid rows of q, k and v read, the output written: the reference's types, so no kernel of
+    # either path can move fewer bytes).
+    io_bytes = 4 * sum(w.lens()) * E * 4
+    t_io = io_bytes / (peaks["hbm_gbs"] * 1e3)  # us
+    t_math = w.flops_per_layer() / ((FP32_FMA_PEAK_TFLOPS if mode == 0 else peaks["bf16_tflops"]) * 1e6)
+    us_layer = ms * 1e3 / w.n_layers
+    r["layer_roofline"] = {"bound": "hbm" if t_io > t_math else ("fma" if mode == 0 else "tensor"),
+                           "io_bytes": io_bytes, "us_hbm": t_io, "us_math": t_math, "us_measured": us_layer,
+                           "frac": max(t_io, t_math) / us_layer}
     return r
 
 
