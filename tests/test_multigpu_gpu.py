@@ -1,6 +1,6 @@
 """SARA KV-head sharding across GPUs (one process per GPU, NCCL), both gather paths:
 NCCL all-gather of head outputs, and the fused path where the decode kernel stores its head outputs
-into every peer's buffer over NVLink and raises flags (bounded wait on the reader).
+into every peer's buffer over NVLink as epoch-tagged words (bounded wait on the reader).
 
 Needs at least 2 GPUs; every rank has its own GPU (kernels that wait on one another never share
 one).  Checked against the CPU restatement of the reference (unsharded) at 1e-4 of the output scale.
@@ -33,7 +33,12 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, gather, q):
+# (H, Hk, D, n_ctx, layers, positions): Qwen3-8B heads split 4 + 4; and 12 heads over 3 KV heads,
+# split 2 + 1, so the ranks decode different numbers of splits and merge groups into the same slots.
+SHAPES = {"even": (32, 8, 128, 2200, 3, (2049, 2050)), "uneven": (12, 3, 128, 6500, 2, (6400, 6401))}
+
+
+def _worker(rank, world, port, gather, q, shape="even"):
     try:
         sys.path.insert(0, ROOT)
         sys.path.insert(0, os.path.join(ROOT, "tests"))
@@ -47,14 +52,14 @@ def _worker(rank, world, port, gather, q):
         torch.cuda.set_device(rank)
         dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                                 device_id=torch.device("cuda", rank))
-        H, Hk, D, n_ctx, L = 32, 8, 128, 2200, 3
+        H, Hk, D, n_ctx, L, positions = SHAPES[shape]
         cfg = AttnConfig(n_layers=L, n_heads=H, n_kv_heads=Hk, head_dim=D, n_context=n_ctx, rope_dim=D,
                          rope_base=1e6, rms_epsilon=1e-6, qk_norm=True, device=rank)
         sara = SaraAttention(cfg, rank, world, dist, gather=gather)
         s = sara.shard
         dev = torch.device("cuda", rank)
         errs = []
-        for step, pos in enumerate((2049, 2050)):
+        for step, pos in enumerate(positions):
             for layer in range(L):
                 c = cases.decode_case(H=H, Hk=Hk, D=D, n_ctx=n_ctx, theta=1e6, qk_norm=1, pos=pos, seed=40 + layer,
                                       layer=layer, kv_head0=s["kv_head0"], kv_headn=s["kv_headn"])
@@ -70,11 +75,12 @@ def _worker(rank, world, port, gather, q):
                 if rank == 0:
                     full = cases.decode_case(H=H, Hk=Hk, D=D, n_ctx=n_ctx, theta=1e6, qk_norm=1, pos=pos,
                                              seed=40 + layer, layer=layer)
-                    if step == 1:  # the cache now also holds position 2049 written by step 0
-                        prev = cases.decode_case(H=H, Hk=Hk, D=D, n_ctx=n_ctx, theta=1e6, qk_norm=1, pos=2049,
+                    if step == 1:  # the cache now also holds the row step 0 wrote
+                        p0 = positions[0]
+                        prev = cases.decode_case(H=H, Hk=Hk, D=D, n_ctx=n_ctx, theta=1e6, qk_norm=1, pos=p0,
                                                  seed=40 + layer, layer=layer)
                         _, krow, vrow = cases.run_decode(orc.Checker("port"), prev)
-                        full["kc"][2049], full["vc"][2049] = krow, vrow
+                        full["kc"][p0], full["vc"][p0] = krow, vrow
                     ref, _, _ = cases.run_decode(orc.Checker("port"), full)
                     errs.append(float(np.abs(out.cpu().numpy() - ref).max() / np.abs(ref).max()))
         sara.attn.sync()
@@ -87,13 +93,13 @@ def _worker(rank, world, port, gather, q):
 
 
 @pytest.mark.skipif(_ngpu() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("gather", ["nccl", "p2p"])
-def test_sara_two_gpus(gather):
+@pytest.mark.parametrize("gather,shape", [("nccl", "even"), ("p2p", "even"), ("nccl", "uneven"), ("p2p", "uneven")])
+def test_sara_two_gpus(gather, shape):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
     world = 2
-    ps = [ctx.Process(target=_worker, args=(r, world, port, gather, q)) for r in range(world)]
+    ps = [ctx.Process(target=_worker, args=(r, world, port, gather, q, shape)) for r in range(world)]
     for p in ps:
         p.start()
     res = {}
