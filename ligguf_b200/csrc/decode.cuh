@@ -142,7 +142,8 @@ struct DecodeSmem {
     static constexpr size_t kBarOff = (kMiscOff + 3 * NREP * 4 + 16 + 4 * kDecodeStages + 7) & ~size_t(7);
     static constexpr size_t kTotal = kBarOff + (3 * kDecodeStages + 1) * 8;  // + the merge barrier
     static constexpr int kMergeGroup = decode_merge_group(NREP, D);
-    static_assert(kDecodeConsumerWarps * NREP * D * 4 <= kTilesBytes, "reduction buffer alias");
+    static_assert((kDecodeConsumerWarps * NREP * D + kDecodeConsumerWarps * 2 * NREP) * 4 <= kTilesBytes,
+                  "reduction buffer alias");
     static_assert(size_t(kMergeGroup) * decode_part_stride(NREP, D) * 4 <= kTilesBytes, "merge copy fits the ring");
     static_assert(kMergeGroup * NREP <= 2 * NREP * Sh::kTileRows, "merge weights fit the score buffer");
 };
@@ -456,7 +457,6 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
     volatile int* abort_s = reinterpret_cast<volatile int*>(l_s + NREP);
     volatile int* last_s = abort_s + 1;
     volatile int* stop_s = abort_s + 2;
-    volatile int* decide_s = abort_s + 3;   // consumers' uniform loop-exit decision
     volatile int* tile_id_s = abort_s + 4;  // [kDecodeStages]: tile held by each stage, -1 = end
     uint64_t* full_k = reinterpret_cast<uint64_t*>(smem + Sm::kBarOff);
     uint64_t* full_v = full_k + kDecodeStages;
@@ -635,28 +635,45 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
     for (int h = 0; h < NREP; ++h)
 #pragma unroll
         for (int e = 0; e < EPL; ++e) acc[h][e] = 0.f;
-    float m_run = -INFINITY, l_run = 0.f;  // used by warps < NREP (warp == head)
     bool ok = true;
     const bool div = a.scale_div != 0;
     const float scale = a.scale;
+    // Each warp consumes its own R rows of every tile (rows [warp*R, warp*R + R)) and keeps its own
+    // online softmax: the running max and sum of each head over the rows it has seen.  The warps
+    // never wait for one another inside the loop; their (max, sum, o) are combined once, below.
+    // Softmax items: (head h, local row lr) = q = h*R + lr; lane takes q = lane + 32k, so the R items
+    // of a head sit on an aligned group of R lanes (segmented shuffles), and each lane keeps the
+    // running max / sum of its items' heads (replicated over the group).
+    constexpr int R = NI * RPI;
+    constexpr int NP = NREP * R;
+    constexpr int IPL = (NP + 31) / 32;
+    static_assert(R <= 32 && (R & (R - 1)) == 0, "a warp's rows form an aligned lane group");
+    float* wsc = sc + warp * NREP * R;  // this warp's scores, then probabilities: [h][lr]
+    float m_lane[IPL], l_lane[IPL];
+#pragma unroll
+    for (int k = 0; k < IPL; ++k) {
+        m_lane[k] = -INFINITY;
+        l_lane[k] = 0.f;
+    }
 
     for (int it = 0;; ++it) {
         const int s = it % kDecodeStages;
         const uint32_t par = (it / kDecodeStages) & 1;
-        float* scb = sc + (it & 1) * NREP * TP;
         const uint8_t* kt = tiles + s * Sm::kStageBytes;
         const uint8_t* vt = kt + kDecodeTileBytes;
 
-        if (ok) {
-            ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full_k[s], par, deadline, abort_s));
-            if (!ok && lane == 0) {
+        ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full_k[s], par, deadline, abort_s));
+        if (!ok) {
+            if (lane == 0) {
                 *abort_s = 1;
                 *reinterpret_cast<volatile int*>(a.err) = KERR_TIMEOUT_FULL;
             }
+            break;
         }
-        const int tile = ok ? tile_id_s[s] : -1;  // -1: the producer's end marker
+        const int tile = tile_id_s[s];  // -1: the producer's end marker
+        if (tile < 0) break;
         const int tbase = tile * TP;
-        if (ok && tile >= 0) {
+        {
             float part[NV];
 #pragma unroll
             for (int i = 0; i < NI; ++i) {
@@ -679,115 +696,132 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
                 for (int u = 0; u < VF; ++u) {
                     const int vi = j * VF + u;
                     const int i = vi / NREP, h = vi % NREP;
-                    const int row = (warp * NI + i) * RPI + r;
+                    const int lr = i * RPI + r;
                     const float sv = div ? part[u] / scale : part[u] * scale;
-                    scb[h * TP + row] = (tbase + row < t_end) ? sv : -INFINITY;
+                    wsc[h * R + lr] = (tbase + (warp * NI + i) * RPI + r < t_end) ? sv : -INFINITY;
                 }
             } else {
                 constexpr int DUP = (1 << S) / NV;
                 if (j % DUP == 0) {
                     const int vi = j / DUP;
                     const int i = vi / NREP, h = vi % NREP;
-                    const int row = (warp * NI + i) * RPI + r;
+                    const int lr = i * RPI + r;
                     const float sv = div ? part[0] / scale : part[0] * scale;
-                    scb[h * TP + row] = (tbase + row < t_end) ? sv : -INFINITY;
-                }
-            }
-        }
-        named_bar_sync(1, kDecodeConsumers);
-        // Loop exit is decided once for all consumer warps (so every warp runs the same number of
-        // named barriers): written here by thread 0, read by everyone after the next barrier.
-        if (tid == 0) *decide_s = (*abort_s != 0 || tile_id_s[s] < 0) ? 1 : 0;
-        if (ok && tile >= 0 && warp < NREP) {  // online softmax of this tile for head `warp`
-            constexpr int PU = TP / 32;
-            float sv[PU];
-            float mx = -INFINITY;
-#pragma unroll
-            for (int u = 0; u < PU; ++u) {
-                sv[u] = scb[warp * TP + lane + 32 * u];
-                mx = fmaxf(mx, sv[u]);
-            }
-            mx = warp_max(mx);
-            const float m_new = fmaxf(m_run, mx);
-            float corr = 1.f, psum = 0.f;
-            if (m_new == -INFINITY) {
-#pragma unroll
-                for (int u = 0; u < PU; ++u) scb[warp * TP + lane + 32 * u] = 0.f;
-            } else {
-                corr = expf(m_run - m_new);
-#pragma unroll
-                for (int u = 0; u < PU; ++u) {
-                    const float p = expf(sv[u] - m_new);
-                    scb[warp * TP + lane + 32 * u] = p;
-                    psum += p;
-                }
-            }
-            psum = warp_sum(psum);
-            l_run = l_run * corr + psum;
-            m_run = m_new;
-            if (lane == 0) corr_s[warp] = corr;
-        }
-        named_bar_sync(1, kDecodeConsumers);
-        if (*decide_s) break;
-        if (ok) {
-            ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full_v[s], par, deadline, abort_s));
-            if (!ok && lane == 0) {
-                *abort_s = 1;
-                *reinterpret_cast<volatile int*>(a.err) = KERR_TIMEOUT_FULL;
-            }
-        }
-        if (ok) {
-#pragma unroll
-            for (int h = 0; h < NREP; ++h) {
-                const float c = corr_s[h];
-#pragma unroll
-                for (int e = 0; e < EPL; ++e) acc[h][e] *= c;
-            }
-#pragma unroll
-            for (int i = 0; i < NI; ++i) {
-                const int row = (warp * NI + i) * RPI + r;
-                const uint4 raw = lds128(vt + row * RB + j * 16);
-                if (tbase + row < t_end) {
-                    float vx[EPL];
-                    KvTraits<KV>::unpack(raw, vx);
-#pragma unroll
-                    for (int h = 0; h < NREP; ++h) {
-                        const float p = scb[h * TP + row];
-#pragma unroll
-                        for (int e = 0; e < EPL; ++e) acc[h][e] = fmaf(p, vx[e], acc[h][e]);
-                    }
+                    wsc[h * R + lr] = (tbase + (warp * NI + i) * RPI + r < t_end) ? sv : -INFINITY;
                 }
             }
         }
         __syncwarp();
+        // Online softmax of this warp's rows, per head.
+        float ck[IPL];
+#pragma unroll
+        for (int k = 0; k < IPL; ++k) {
+            const int q = lane + 32 * k;
+            const float sv = q < NP ? wsc[q] : -INFINITY;
+            float mx = sv;
+#pragma unroll
+            for (int o = R / 2; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            const float mn = fmaxf(m_lane[k], mx);
+            ck[k] = mn == -INFINITY ? 1.f : expf(m_lane[k] - mn);
+            const float p = mn == -INFINITY ? 0.f : expf(sv - mn);
+            float ps = p;
+#pragma unroll
+            for (int o = R / 2; o >= 1; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+            l_lane[k] = l_lane[k] * ck[k] + ps;
+            m_lane[k] = mn;
+            if (q < NP) wsc[q] = p;
+        }
+        __syncwarp();
+        ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full_v[s], par, deadline, abort_s));
+        if (!ok) {
+            if (lane == 0) {
+                *abort_s = 1;
+                *reinterpret_cast<volatile int*>(a.err) = KERR_TIMEOUT_FULL;
+            }
+            break;
+        }
+#pragma unroll
+        for (int h = 0; h < NREP; ++h) {
+            const float c = __shfl_sync(0xffffffffu, ck[(h * R) / 32], (h * R) % 32);
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) acc[h][e] *= c;
+        }
+#pragma unroll
+        for (int i = 0; i < NI; ++i) {
+            const int row = (warp * NI + i) * RPI + r;
+            const uint4 raw = lds128(vt + row * RB + j * 16);
+            if (tbase + row < t_end) {
+                float vx[EPL];
+                KvTraits<KV>::unpack(raw, vx);
+#pragma unroll
+                for (int h = 0; h < NREP; ++h) {
+                    const float p = wsc[h * R + i * RPI + r];
+#pragma unroll
+                    for (int e = 0; e < EPL; ++e) acc[h][e] = fmaf(p, vx[e], acc[h][e]);
+                }
+            }
+        }
+        __syncwarp();  // every lane is done with this stage and with wsc
         if (lane == 0) mbar_arrive(&empty[s]);
     }
 
     // ------------------------------------------------------------------ CTA reduction
+    // Warp w holds (m_w, l_w, o_w) per head over its rows; with M = max_w m_w the CTA's result is
+    // o = sum_w o_w e^(m_w - M), l = sum_w l_w e^(m_w - M), m = M.
 #pragma unroll
     for (int o = LPR; o < 32; o <<= 1)
 #pragma unroll
         for (int h = 0; h < NREP; ++h)
 #pragma unroll
             for (int e = 0; e < EPL; ++e) acc[h][e] += __shfl_xor_sync(0xffffffffu, acc[h][e], o);
+    float mh[NREP], lh[NREP];
+#pragma unroll
+    for (int h = 0; h < NREP; ++h) {
+        mh[h] = __shfl_sync(0xffffffffu, m_lane[(h * R) / 32], (h * R) % 32);
+        lh[h] = __shfl_sync(0xffffffffu, l_lane[(h * R) / 32], (h * R) % 32);
+    }
     named_bar_sync(1, kDecodeConsumers);  // every warp is done with the tiles before `red` aliases them
-    float* red = reinterpret_cast<float*>(tiles);
+    float* red = reinterpret_cast<float*>(tiles);                       // [warp][NREP][D]
+    float* wml = red + kDecodeConsumerWarps * NREP * D;                 // [warp][2][NREP]
     if (lane < LPR) {
 #pragma unroll
         for (int h = 0; h < NREP; ++h)
 #pragma unroll
             for (int e = 0; e < EPL; ++e) red[(warp * NREP + h) * D + j * EPL + e] = acc[h][e];
     }
-    if (warp < NREP && lane == 0) {
-        m_s[warp] = m_run;
-        l_s[warp] = l_run;
+    if (lane == 0) {
+#pragma unroll
+        for (int h = 0; h < NREP; ++h) {
+            wml[(warp * 2) * NREP + h] = mh[h];
+            wml[(warp * 2 + 1) * NREP + h] = lh[h];
+        }
     }
     named_bar_sync(1, kDecodeConsumers);
     for (int idx = tid; idx < NREP * D; idx += kDecodeConsumers) {
+        const int h = idx / D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kDecodeConsumerWarps; ++w) M = fmaxf(M, wml[(w * 2) * NREP + h]);
         float sum = 0.f;
 #pragma unroll
-        for (int w = 0; w < kDecodeConsumerWarps; ++w) sum += red[w * NREP * D + idx];
+        for (int w = 0; w < kDecodeConsumerWarps; ++w) {
+            const float mw = wml[(w * 2) * NREP + h];
+            if (mw != -INFINITY) sum = fmaf(red[w * NREP * D + idx], expf(mw - M), sum);
+        }
         o_s[idx] = sum;
+    }
+    if (tid < NREP) {
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kDecodeConsumerWarps; ++w) M = fmaxf(M, wml[(w * 2) * NREP + tid]);
+        float L = 0.f;
+#pragma unroll
+        for (int w = 0; w < kDecodeConsumerWarps; ++w) {
+            const float mw = wml[(w * 2) * NREP + tid];
+            if (mw != -INFINITY) L = fmaf(wml[(w * 2 + 1) * NREP + tid], expf(mw - M), L);
+        }
+        m_s[tid] = M;
+        l_s[tid] = L;
     }
     named_bar_sync(1, kDecodeConsumers);
 
