@@ -484,6 +484,10 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
         *stop_s = 0;
         fence_mbar_init();
     }
+    // The barriers and flags are initialised before any thread waits on the previous grid, so that
+    // the producer can start its early copies at once (a CTA barrier after the consumers' wait
+    // would hold the producer until the previous grid completes).
+    __syncthreads();
     // Launched as a programmatic dependent of the previous kernel in the stream: everything above
     // touches only this CTA's shared memory; every global read (inputs, the partials and counters
     // this kernel shares with other launches, cache rows) comes after the previous grid has
@@ -509,7 +513,6 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
     if (first_job)
         head_load<D>(pin, warp < NREP ? a.q + static_cast<size_t>(g * NREP + warp) * D
                                       : (warp == NREP ? a.k : a.v) + static_cast<size_t>(g) * D, lane);
-    __syncthreads();
 
     // ------------------------------------------------------------------ producer warp
     if (warp == kDecodeConsumerWarps) {
