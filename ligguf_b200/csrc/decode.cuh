@@ -114,6 +114,14 @@ struct DecodeArgs {
     float eps;
 };
 
+// 2^x on the MUFU (ex2.approx.ftz: relative error about 2^-22; -inf gives +0).
+__device__ __forceinline__ float decode_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+constexpr float kLog2e = 1.4426950408889634f;  // log2(e): e^x = 2^(x log2 e)
+
 template <typename KV, int D>
 struct DecodeShape {
     static constexpr int kRowBytes = D * static_cast<int>(sizeof(KV));
@@ -651,7 +659,7 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
     constexpr int NP = NREP * R;
     constexpr int IPL = (NP + 31) / 32;
     static_assert(R <= 32 && (R & (R - 1)) == 0, "a warp's rows form an aligned lane group");
-    float* wsc = sc + warp * NREP * R;  // this warp's scores, then probabilities: [h][lr]
+    float* wsc = sc + warp * NREP * R;  // this warp's scores, then probabilities: [lr][h]
     float m_lane[IPL], l_lane[IPL];
 #pragma unroll
     for (int k = 0; k < IPL; ++k) {
@@ -701,7 +709,7 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
                     const int i = vi / NREP, h = vi % NREP;
                     const int lr = i * RPI + r;
                     const float sv = div ? part[u] / scale : part[u] * scale;
-                    wsc[h * R + lr] = (tbase + (warp * NI + i) * RPI + r < t_end) ? sv : -INFINITY;
+                    wsc[lr * NREP + h] = (tbase + (warp * NI + i) * RPI + r < t_end) ? sv : -INFINITY;
                 }
             } else {
                 constexpr int DUP = (1 << S) / NV;
@@ -710,29 +718,34 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
                     const int i = vi / NREP, h = vi % NREP;
                     const int lr = i * RPI + r;
                     const float sv = div ? part[0] / scale : part[0] * scale;
-                    wsc[h * R + lr] = (tbase + (warp * NI + i) * RPI + r < t_end) ? sv : -INFINITY;
+                    wsc[lr * NREP + h] = (tbase + (warp * NI + i) * RPI + r < t_end) ? sv : -INFINITY;
                 }
             }
         }
         __syncwarp();
-        // Online softmax of this warp's rows, per head.
+        // Online softmax of this warp's rows, per head: e^x as 2^(x log2 e) on the MUFU
+        // (ex2.approx, relative error about 2^-22).  The accumulators are rescaled only when some
+        // head's running maximum moved (a factor of exactly 1 otherwise).
         float ck[IPL];
+        bool moved = false;
 #pragma unroll
         for (int k = 0; k < IPL; ++k) {
             const int q = lane + 32 * k;
-            const float sv = q < NP ? wsc[q] : -INFINITY;
+            const int ws = (q % R) * NREP + q / R;  // item (head q / R, row q % R)
+            const float sv = q < NP ? wsc[ws] : -INFINITY;
             float mx = sv;
 #pragma unroll
             for (int o = R / 2; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
             const float mn = fmaxf(m_lane[k], mx);
-            ck[k] = mn == -INFINITY ? 1.f : expf(m_lane[k] - mn);
-            const float p = mn == -INFINITY ? 0.f : expf(sv - mn);
+            ck[k] = mn == -INFINITY ? 1.f : decode_exp2((m_lane[k] - mn) * kLog2e);
+            moved |= ck[k] != 1.f;
+            const float p = mn == -INFINITY ? 0.f : decode_exp2((sv - mn) * kLog2e);
             float ps = p;
 #pragma unroll
             for (int o = R / 2; o >= 1; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
             l_lane[k] = l_lane[k] * ck[k] + ps;
             m_lane[k] = mn;
-            if (q < NP) wsc[q] = p;
+            if (q < NP) wsc[ws] = p;
         }
         __syncwarp();
         ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full_v[s], par, deadline, abort_s));
@@ -743,11 +756,13 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
             }
             break;
         }
+        if (__any_sync(0xffffffffu, moved)) {
 #pragma unroll
-        for (int h = 0; h < NREP; ++h) {
-            const float c = __shfl_sync(0xffffffffu, ck[(h * R) / 32], (h * R) % 32);
+            for (int h = 0; h < NREP; ++h) {
+                const float c = __shfl_sync(0xffffffffu, ck[(h * R) / 32], (h * R) % 32);
 #pragma unroll
-            for (int e = 0; e < EPL; ++e) acc[h][e] *= c;
+                for (int e = 0; e < EPL; ++e) acc[h][e] *= c;
+            }
         }
 #pragma unroll
         for (int i = 0; i < NI; ++i) {
@@ -756,12 +771,28 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
             if (tbase + row < t_end) {
                 float vx[EPL];
                 KvTraits<KV>::unpack(raw, vx);
+                float pv[NREP];  // the row's probabilities for every head, one vector load
+                const float* pr = wsc + (i * RPI + r) * NREP;
+                if constexpr (NREP % 4 == 0) {
 #pragma unroll
-                for (int h = 0; h < NREP; ++h) {
-                    const float p = wsc[h * R + i * RPI + r];
-#pragma unroll
-                    for (int e = 0; e < EPL; ++e) acc[h][e] = fmaf(p, vx[e], acc[h][e]);
+                    for (int c = 0; c < NREP / 4; ++c) {
+                        const float4 t4 = reinterpret_cast<const float4*>(pr)[c];
+                        pv[4 * c] = t4.x;
+                        pv[4 * c + 1] = t4.y;
+                        pv[4 * c + 2] = t4.z;
+                        pv[4 * c + 3] = t4.w;
+                    }
+                } else if constexpr (NREP == 2) {
+                    const float2 t2 = *reinterpret_cast<const float2*>(pr);
+                    pv[0] = t2.x;
+                    pv[1] = t2.y;
+                } else {
+                    pv[0] = pr[0];
                 }
+#pragma unroll
+                for (int h = 0; h < NREP; ++h)
+#pragma unroll
+                    for (int e = 0; e < EPL; ++e) acc[h][e] = fmaf(pv[h], vx[e], acc[h][e]);
             }
         }
         __syncwarp();  // every lane is done with this stage and with wsc
