@@ -13,8 +13,9 @@
 // static chunk of 16 KB tiles of cached positions [0, pos) and then takes further chunks of the
 // head from an atomic counter (so CTAs that stream faster take more tiles; one static wave left SMs
 // idle for a fifth of the kernel at 32K).  When each CTA has only a few tiles (short contexts, or
-// one KV head per GPU), the static chunks cover everything instead: no grabs, and the whole chunk
-// (up to the ring's depth) is requested before the previous kernel in the stream has finished.  It computes all nrep q heads of the group, so each K/V byte is
+// one KV head per GPU), the static chunks cover everything instead: no grabs, and the first
+// kDecodeEarlyTiles tiles of a chunk are requested before the previous kernel in the stream has
+// finished.  A CTA computes all nrep q heads of the group, so each K/V byte is
 // read from HBM once.  Warp 8 is the producer: one lane grabs chunks and streams their K and V tiles
 // with TMA into a 3-stage shared-memory ring, publishing each stage's tile index in shared memory.  Warps 0..7 consume: scores (each lane dots 16 B of a row with
 // the nrep q vectors, a transposed butterfly reduces nrep*4 dot products with one shuffle per
@@ -40,6 +41,10 @@ constexpr int kDecodeTileBytes = 16384;
 constexpr int kDecodeMaxSplit = 1024;
 constexpr int kDecodeMaxGroups = 32;   // first-level merge groups per KV head (the host bounds n_split)
 constexpr int kDecodeStaticMaxTiles = 8;  // up to this many tiles per CTA: static chunks, no grabs
+// Tiles a CTA requests before the previous grid completes.  Enough to cover that grid's tail; more
+// compete with the tail (its partials, tickets and merge) for memory (4K: 3 tiles 13.5 us per
+// layer, 2 tiles 13.0, 1 tile 13.2; one-KV-head 32K shard 16.3 / 15.7 / 15.5; 32K unchanged).
+constexpr int kDecodeEarlyTiles = 2;
 
 // One partial (o[NREP][D], m[NREP], l[NREP]) in floats, padded to 16 bytes so that a run of
 // partials can be fetched with one bulk copy.
@@ -133,6 +138,7 @@ struct DecodeShape {
     static constexpr int kLog2Lpr = kLanesPerRow == 32 ? 5 : kLanesPerRow == 16 ? 4 : 3;
     static_assert(kRowBytes >= 128 && kRowBytes <= 512, "one head row must be 128..512 bytes");
     static_assert(kInstr == 4, "tile mapping expects 4 row loads per warp per tile");
+    static_assert(kDecodeEarlyTiles <= kDecodeStages, "early copies fill at most the ring");
 };
 
 template <typename KV, int D, int NREP>
@@ -547,7 +553,7 @@ __global__ void __launch_bounds__(kDecodeThreads, (NREP * DecodeShape<KV, D>::kE
             // predecessor before it lets its dependent launch).
             int t0 = base;
             const int lim0 = min(base + a.chunk, a.n_tiles);
-            for (; t0 < lim0 && it < kDecodeStages && (t0 + 1) * TP <= a.pre_rows; ++t0, ++it) issue(t0, it);
+            for (; t0 < lim0 && it < kDecodeEarlyTiles && (t0 + 1) * TP <= a.pre_rows; ++t0, ++it) issue(t0, it);
             asm volatile("griddepcontrol.wait;" ::: "memory");
             bool first = true;
             while (!fail && base < a.n_tiles) {
